@@ -1,0 +1,533 @@
+"""Benchmark of the progressive int2 GEMV path on B200 (one JSON line on rank 0).
+
+Workloads (seeded synthetic weights, FP16 activations):
+  llama7b_block_p2   q,k,v,o 4096x4096; gate,up 11008x4096; down 4096x11008; prefix 2; 1 GPU
+  llama70b_mlp_p3    gate,up 28672x8192; down 8192x28672; prefix 3; output rows sharded
+                     over the ranks with an FP16 all-gather of each layer's output (NCCL)
+Default: llama7b_block_p2 at one GPU, llama70b_mlp_p3 when --gpus > 1.
+
+A step is one pass over every layer of the workload at batch 1.  `value` is the
+aggregate algorithmic HBM bytes (selected planes + scales + FP16 x + FP16 y, the
+same bytes the reference's layout would need) per second over all ranks; weight
+buffers rotate over copies totalling > 3x L2 so every step streams from HBM.
+
+--impl reference times the reference's own C++ ProgressiveLinearReference
+(native/src/stage_codec.cpp, compiled in place into oracle/_ref) on the host cores
+for the same workload and metric.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+sys.path.insert(0, str(ROOT / "harp-q_b200"))
+
+METRIC = "µs per layer & achieved HBM GB/s vs B200 peak, batch-1 GEMV at prefix depth 1–4"
+L2_BYTES = 126 * 1024 * 1024
+
+WORKLOADS = {
+    # name: (prefix, [(layer, rows, cols, input)], std, per-rank sharding)
+    "llama7b_block_p2": (2, [("q", 4096, 4096, "a"), ("k", 4096, 4096, "a"), ("v", 4096, 4096, "a"),
+                             ("o", 4096, 4096, "b"), ("gate", 11008, 4096, "c"), ("up", 11008, 4096, "c"),
+                             ("down", 4096, 11008, "d")], 0.02),
+    "llama70b_mlp_p3": (3, [("gate", 28672, 8192, "a"), ("up", 28672, 8192, "a"), ("down", 8192, 28672, "b")],
+                        0.015),
+    "single_4096_p1": (1, [("w", 4096, 4096, "a")], 0.02),
+    "single_4096_p4": (4, [("w", 4096, 4096, "a")], 0.02),
+    "single_11008_p1": (1, [("w", 11008, 4096, "a")], 0.02),
+    "single_11008_p4": (4, [("w", 11008, 4096, "a")], 0.02),
+}
+
+
+def algorithmic_bytes(rows: int, cols: int, prefix: int, batch: int = 1) -> int:
+    """d*17*N*K/64 (codes + one FP16 scale per row per 128 columns) + FP16 x and y."""
+    return prefix * (rows * cols // 4 + rows * (-(-cols // 128)) * 2) + 2 * cols * batch + 2 * rows * batch
+
+
+# ---------------------------------------------------------------------------------------
+# synthetic weights: the reference's LS int2 fit (quantization.py:466-521) restated with
+# torch on the GPU, for input generation only (never timed).  Same steps as
+# oracle/quantize.py; FP64 reduction order may differ in the last bit.
+
+def quantize_gpu(w: torch.Tensor, stages: int = 4):
+    n, k = w.shape
+    npad, kpad = -(-n // 128) * 128, -(-k // 128) * 128
+    res = torch.zeros(npad, kpad, dtype=torch.float32, device=w.device)
+    res[:n, :k] = w
+    codes_out, bits_out = [], []
+    for _ in range(stages):
+        g = res.view(npad, kpad // 128, 128)
+        peak = g.abs().amax(-1)
+        s = torch.where(peak > 0, peak / 1.5, torch.zeros_like(peak))
+        for _ in range(4):
+            nz = (s != 0)[..., None]
+            q = torch.where(nz, g / torch.where(nz, s[..., None], torch.ones_like(s[..., None])), torch.zeros_like(g))
+            c = torch.clamp(torch.round(q), -2, 1)
+            num = (g.double() * c.double()).sum(-1)
+            den = (c.double() ** 2).sum(-1)
+            fit = torch.where(den != 0, num / torch.where(den != 0, den, torch.ones_like(den)), torch.zeros_like(num))
+            s = torch.where(den != 0, fit, s.double()).float().clamp_min(0.0)
+        s16 = s.half()
+        ex = s16.float()
+        nz = (ex != 0)[..., None]
+        q = torch.where(nz, g / torch.where(nz, ex[..., None], torch.ones_like(ex[..., None])), torch.zeros_like(g))
+        c = torch.clamp(torch.round(q), -2, 1)
+        res -= (c * ex[..., None]).view(npad, kpad)
+        two = (c.to(torch.int8) & 3).to(torch.uint8).view(-1, 4)
+        packed = two[:, 0] | (two[:, 1] << 2) | (two[:, 2] << 4) | (two[:, 3] << 6)
+        codes_out.append(packed.contiguous())
+        # scale layout [tile_row][tile_col][row_in_tile]
+        bits = s16.view(npad // 128, 128, kpad // 128).permute(0, 2, 1).contiguous().view(-1).view(torch.int16)
+        bits_out.append(bits)
+        del g, q, c, two
+    return codes_out, bits_out
+
+
+def make_layer(rows, cols, std, seed, device):
+    gen = torch.Generator(device=device)
+    gen.manual_seed(seed)
+    w = torch.randn(rows, cols, generator=gen, device=device, dtype=torch.float32) * std
+    codes, bits = quantize_gpu(w)
+    del w
+    return codes, bits
+
+
+def shard_rows(rows: int, world: int, rank: int) -> tuple[int, int]:
+    """Tile-row aligned contiguous slice of the output rows for one rank."""
+    tiles = -(-rows // 128)
+    t0, t1 = tiles * rank // world, tiles * (rank + 1) // world
+    r0, r1 = t0 * 128, min(t1 * 128, rows)
+    return r0, r1 - r0
+
+
+def slice_stage_rows(codes, bits, rows, cols, r0, nrows):
+    kpad = -(-cols // 128) * 128
+    cpr = kpad // 4
+    c = [x[r0 * cpr:(r0 + -(-nrows // 128) * 128) * cpr].contiguous() for x in codes]
+    per_tile_row = (kpad // 128) * 128
+    t0 = r0 // 128
+    nt = -(-nrows // 128)
+    b = [x[t0 * per_tile_row:(t0 + nt) * per_tile_row].contiguous() for x in bits]
+    return c, b
+
+
+# ---------------------------------------------------------------------------------------
+# clocks
+
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        visible = os.environ.get("CUDA_VISIBLE_DEVICES")
+        ids = [v.strip() for v in visible.split(",")] if visible else []
+        self.idx = ids[device_index] if device_index < len(ids) else str(device_index)
+        self.proc = None
+        self.lines: list[str] = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx.append(float(parts[2]))
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[5:9]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------------------
+# our arm
+
+def build_workload(name, rank, world, device, rotation_target):
+    import harpq_b200 as hqb
+
+    prefix, layers, std = WORKLOADS[name]
+    built = []
+    step_bytes = 0
+    for li, (lname, rows, cols, src) in enumerate(layers):
+        codes, bits = make_layer(rows, cols, std, 1000 + li, device)
+        r0, nrows = (0, rows) if world == 1 else shard_rows(rows, world, rank)
+        if world > 1:
+            codes, bits = slice_stage_rows(codes, bits, rows, cols, r0, nrows)
+        pm = hqb.PlaneMatrix.from_stages(nrows, cols, codes, bits)
+        del codes, bits
+        built.append({"name": lname, "rows": rows, "cols": cols, "src": src, "r0": r0, "nrows": nrows,
+                      "copies": [pm]})
+        step_bytes += algorithmic_bytes(nrows, cols, prefix)
+    torch.cuda.synchronize()
+    plane_bytes_step = sum(sum(p.numel() for p in L["copies"][0].planes[:prefix]) for L in built)
+    ncopies = max(2, -(-rotation_target // max(1, plane_bytes_step)))
+    import harpq_b200 as hqb  # noqa: F811
+
+    for L in built:
+        base = L["copies"][0]
+        for _ in range(ncopies - 1):
+            cp = hqb.PlaneMatrix(base.rows, base.cols)
+            cp.planes = [p.clone() for p in base.planes]
+            L["copies"].append(cp)
+    torch.cuda.synchronize()
+    return prefix, built, step_bytes, ncopies
+
+
+def run_ours(args, rank, world, device):
+    import harpq_b200 as hqb
+
+    name = args.workload
+    prefix, layers, step_bytes, ncopies = build_workload(name, rank, world, device, 3 * L2_BYTES)
+    srcs = {}
+    for L in layers:
+        srcs.setdefault(L["src"], L["cols"])
+    gen = torch.Generator(device=device)
+    gen.manual_seed(7)
+    x_dev = {s: torch.randn(1, k, generator=gen, device=device).half() for s, k in srcs.items()}
+    xfrag = {s: hqb.prepare_x(x_dev[s]) for s in srcs}
+    y_loc = {L["name"]: torch.empty(1, L["nrows"], dtype=torch.float16, device=device) for L in layers}
+    y_full = {L["name"]: torch.empty(world, -(-(-(-L["rows"] // 128)) // world) * 128 if world > 1 else L["rows"],
+                                     dtype=torch.float16, device=device) for L in layers}
+    ws_bytes = max(L["copies"][0].workspace_bytes(1, hqb.F16) for L in layers)
+    ws = hqb.Workspace(ws_bytes, device)
+    launches_per_step = len(srcs) + len(layers)
+
+    def gather(L):
+        if world == 1:
+            return
+        n = L["nrows"]
+        pad = y_full[L["name"]].shape[1]
+        send = y_loc[L["name"]] if n == pad else torch.nn.functional.pad(y_loc[L["name"]], (0, pad - n))
+        torch.distributed.all_gather_into_tensor(y_full[L["name"]].view(-1), send.view(-1))
+
+    def step(copy, x_src=None):
+        for s in srcs:
+            hqb.prepare_x(x_dev[s] if x_src is None else x_src[s], out=xfrag[s])
+        for L in layers:
+            pm = L["copies"][copy]
+            pm.gemv(x_dev[L["src"]], prefix=prefix, out=y_loc[L["name"]], workspace=ws,
+                    x_prepared=xfrag[L["src"]], flags=hqb.FLAG_PDL)
+            gather(L)
+
+    # warm-up (also JIT/driver setup)
+    for i in range(max(3, args.warmup)):
+        step(i % ncopies)
+    torch.cuda.synchronize()
+
+    use_graph = world == 1 and not args.no_graph
+    graphs = []
+    if use_graph:
+        for c in range(ncopies):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                step(c)
+            graphs.append(g)
+        for i in range(3):
+            graphs[i % ncopies].replay()
+        torch.cuda.synchronize()
+
+    def barrier():
+        if world > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize()
+
+    # ---- timed region: K steps
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(torch.cuda.current_device()) as clk:
+        barrier()
+        start.record()
+        for i in range(args.steps):
+            if use_graph:
+                graphs[i % ncopies].replay()
+            else:
+                step(i % ncopies)
+        end.record()
+        barrier()
+    ms = start.elapsed_time(end)
+    ms_max = ms
+    if world > 1:
+        t = torch.tensor([ms], device=device)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms_max = float(t.item())
+    ms_per_step = ms_max / args.steps
+    total_bytes = step_bytes * world  # every rank streams its own shard
+    if world > 1:
+        total_bytes = sum(algorithmic_bytes(L["rows"], L["cols"], prefix) for L in layers)
+    value = total_bytes / (ms_per_step * 1e-3) / 1e9
+
+    # ---- per-kernel roofline: GEMV launches timed alone with events on this stream
+    per_layer_ms = {L["name"]: [] for L in layers}
+    for i in range(max(6, ncopies)):
+        for L in layers:
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            L["copies"][i % ncopies].gemv(x_dev[L["src"]], prefix=prefix, out=y_loc[L["name"]], workspace=ws,
+                                          x_prepared=xfrag[L["src"]])
+            e1.record()
+            per_layer_ms[L["name"]].append((e0, e1))
+    torch.cuda.synchronize()
+    kern = {}
+    tot_b, tot_ms = 0, 0.0
+    for L in layers:
+        times = sorted(a.elapsed_time(b) for a, b in per_layer_ms[L["name"]][2:])
+        med = statistics.median(times)
+        b = algorithmic_bytes(L["nrows"], L["cols"], prefix)
+        kern[L["name"]] = {"us": round(med * 1e3, 3), "gbs": round(b / (med * 1e-3) / 1e9, 1)}
+        tot_b += b
+        tot_ms += med
+    achieved = tot_b / (tot_ms * 1e-3) / 1e9
+
+    # ---- e2e through the public API: pinned host x -> device, GEMVs, device -> host y
+    host_x = {s: x_dev[s].cpu().pin_memory() for s in srcs}
+    host_y = {L["name"]: torch.empty_like(y_full[L["name"]] if world > 1 else y_loc[L["name"]], device="cpu").pin_memory()
+              for L in layers}
+    x_stage = {s: torch.empty_like(x_dev[s]) for s in srcs}
+
+    def e2e_step(copy):
+        for s in srcs:
+            x_stage[s].copy_(host_x[s], non_blocking=True)
+        step(copy, x_src=x_stage)
+        for L in layers:
+            host_y[L["name"]].copy_(y_full[L["name"]] if world > 1 else y_loc[L["name"]], non_blocking=True)
+
+    for i in range(3):
+        e2e_step(i % ncopies)
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(args.steps):
+        e2e_step(i % ncopies)
+    e1.record()
+    barrier()
+    e2e_ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=device)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    e2e_ms /= args.steps
+    h2d = sum(x.numel() * 2 for x in host_x.values())
+    d2h = sum(y.numel() * 2 for y in host_y.values())
+
+    flags = ws.error_flags()
+    result = {
+        "metric": METRIC,
+        "value": round(value, 1),
+        "unit": "GB/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms_per_step, 5),
+        "us_per_layer": round(ms_per_step * 1e3 / len(layers), 3),
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "int2 codes x FP16 scales, FP16 x/y, FP32 accumulate",
+        "data": "synthetic: seeded N(0,std) weights quantized by the reference LS int2 fit (GPU restatement), "
+                "seeded N(0,1) FP16 activations",
+        "config": {"workload": name, "prefix": prefix, "batch": 1,
+                   "layers": [[L["name"], L["nrows"], L["cols"]] for L in layers],
+                   "parallelism": f"row-shard{world}+allgather" if world > 1 else "single",
+                   "l2": f"{ncopies} rotating weight copies, {ncopies * step_bytes / 2**20:.0f} MiB > 3x L2",
+                   "graph": use_graph},
+        "roofline": None,
+        "kernels": kern,
+        "e2e": {"value": round(total_bytes / (e2e_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
+                "us_per_step": round(e2e_ms * 1e3, 2), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+        "gpu_launches": launches_per_step * args.steps,
+        "clocks": clk.summary(),
+        "device_error_flags": flags,
+    }
+    peaks = {}
+    try:
+        peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
+    except (OSError, ValueError):
+        pass
+    peak = peaks.get("hbm_gbs", 6650.0)
+    traffic = _recorded_traffic_ratio()
+    result["roofline"] = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                          "frac": round(achieved / peak, 4),
+                          "peak_source": "measured" if "hbm_gbs" in peaks else "fallback",
+                          "traffic": None if traffic is None else round(traffic * tot_b / len(layers)),
+                          "kernel": "hqb::gemv_kernel<1,1,false>",
+                          "achieved_note": "algorithmic bytes of all GEMV launches / sum of their median "
+                                           "CUDA-event durations"}
+    return result
+
+
+def _recorded_traffic_ratio():
+    """DRAM bytes per algorithmic byte of the GEMV kernel from the committed ncu summary."""
+    p = ROOT / "profiles" / "gemv_kernel_traffic.txt"
+    try:
+        for line in p.read_text().splitlines():
+            if line.startswith("dram_bytes_per_algorithmic_byte:"):
+                return float(line.split(":", 1)[1])
+    except OSError:
+        pass
+    return None
+
+
+# ---------------------------------------------------------------------------------------
+# reference arm / CPU baseline
+
+def reference_inputs(name, device):
+    """Host progressive matrices (oracle.Matrix) for the workload plus FP16-exact x."""
+    from oracle import oracle as orc
+
+    prefix, layers, std = WORKLOADS[name]
+    mats, xs = [], {}
+    for li, (lname, rows, cols, src) in enumerate(layers):
+        if device is not None:
+            codes, bits = make_layer(rows, cols, std, 1000 + li, device)
+            codes = [c.cpu().numpy() for c in codes]
+            scales = [b.cpu().numpy().view(np.float16).astype(np.float32) for b in bits]
+        else:
+            from oracle import quantize as qz
+            rng = np.random.default_rng(1000 + li)
+            q = qz.quantize(rng.normal(0, std, size=(rows, cols)).astype(np.float32))
+            codes = q.codes
+            scales = [s.astype(np.float32).reshape(-1) for s in q.scales]
+        rp, cp = -(-rows // 128) * 128, -(-cols // 128) * 128
+        mats.append((lname, src, orc.Matrix((rows, cols, rp, cp, 128, 128, 128), codes, scales)))
+        xs.setdefault(src, np.random.default_rng(7).standard_normal(cols).astype(np.float16).astype(np.float32))
+    return prefix, mats, xs
+
+
+def time_reference(name, steps, warmup, device, threads=None, budget_s=None):
+    from oracle import refcpu
+
+    if not refcpu.available():
+        raise RuntimeError("oracle/_ref/libharpq_ref.so is not built")
+    threads = threads or os.cpu_count() or 1
+    prefix, mats, xs = reference_inputs(name, device)
+    runners = [(lname, src, m, refcpu.ShardedReference(m, threads)) for lname, src, m in mats]
+    step_bytes = sum(algorithmic_bytes(m.rows, m.cols, prefix) for _, _, m, _ in runners)
+
+    def one():
+        for _, src, _, r in runners:
+            r.linear(xs[src], prefix)
+
+    for _ in range(warmup):
+        one()
+    times = []
+    t_all = time.perf_counter()
+    for _ in range(steps):
+        t0 = time.perf_counter()
+        one()
+        times.append(time.perf_counter() - t0)
+        if budget_s is not None and time.perf_counter() - t_all > budget_s:
+            break
+    for *_, r in runners:
+        r.close()
+    mean = sum(times) / len(times)
+    return {"value": round(step_bytes / mean / 1e9, 4), "unit": "GB/s", "cores": threads, "kind": "reference",
+            "sample": f"{len(times)} full {name} step(s), tile-row shards over {threads} threads, "
+                      f"{mean * 1e3:.1f} ms/step", "ms_per_step": mean * 1e3, "steps_timed": len(times)}
+
+
+def run_reference_arm(args, device):
+    name = args.workload
+    r = time_reference(name, args.steps, max(1, min(args.warmup, 2)), device)
+    prefix, layers, _ = WORKLOADS[name]
+    return {"metric": METRIC, "impl": "reference", "value": r["value"], "unit": "GB/s", "n_gpus": args.gpus,
+            "steps": r["steps_timed"], "warmup": args.warmup, "ms_per_step": round(r["ms_per_step"], 3),
+            "us_per_layer": round(r["ms_per_step"] * 1e3 / len(layers), 1), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "int2 codes x FP32 scales, FP32 x/y (reference C++)",
+            "data": "synthetic, the product arm's weights (same seeds and quantizer)",
+            "config": {"workload": name, "prefix": prefix, "batch": 1},
+            "cpu_baseline": {k: r[k] for k in ("value", "unit", "cores", "kind", "sample")},
+            "e2e": {"value": r["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+# ---------------------------------------------------------------------------------------
+
+def main(argv=None) -> int:
+    ap = argparse.ArgumentParser(description=__doc__)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", default="auto", choices=["auto", *WORKLOADS])
+    ap.add_argument("--no-graph", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args(argv)
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.workload == "auto":
+        args.workload = "llama7b_block_p2" if world == 1 else "llama70b_mlp_p3"
+    have_gpu = torch.cuda.is_available()
+    device = torch.device("cuda", local) if have_gpu else None
+    if have_gpu:
+        torch.cuda.set_device(device)
+
+    if args.impl == "reference":
+        if rank != 0:
+            return 0
+        print(json.dumps(run_reference_arm(args, device)), flush=True)
+        return 0
+
+    if world > 1:
+        import datetime
+
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                             device_id=device)
+    import harpq_b200  # noqa: F401  (fails loudly when the library is missing)
+
+    result = run_ours(args, rank, world, device)
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cb = time_reference(args.workload, 3, 1, device, budget_s=20.0)
+        result["cpu_baseline"] = {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")}
+    if world > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

@@ -1,0 +1,1012 @@
+// Plane-layout kernels of the progressive int2 GEMV for sm_100a.
+//
+//   repack_kernel     reference row-major stage -> plane records (one per tile)
+//   prep_x_kernel     activations -> per-tile tensor-core B fragments + correction sums
+//   gemv_kernel       warp-specialised, bulk-copy pipelined GEMV (tensor-core or CUDA-core
+//                     consumer), stream-K partition with deterministic split-row fix-up
+//   decode_kernel     planes -> dense FP32 weights, bit-identical to DequantizePrefix
+//   depth_plan_kernel per-tile depth map -> row-cost prefix sums (the mixed-depth schedule)
+//   fill_kernel       prefix 0: bias or exact zeros
+//
+// Plane record of one (tile, stage), HQB_TILE_RECORD_BYTES = 8 x 544:
+//   row block rb (tile rows 16rb..16rb+15) at rb*544:
+//     [0, 512)   32 slots of 16 B, slot t = 4g+q holds four 32-bit code words
+//                  w0 = row 16rb+g,   columns 32q..32q+15     (2 bits/code, LSB first)
+//                  w1 = row 16rb+g+8, columns 32q..32q+15
+//                  w2 = row 16rb+g,   columns 32q+16..32q+31
+//                  w3 = row 16rb+g+8, columns 32q+16..32q+31
+//                so lane t of a warp gets exactly its m16n8k16 A-fragment codes with
+//                one 16-byte shared-memory load;
+//     [512, 544) 8 pairs {scale(row 16rb+g), scale(row 16rb+g+8)} as raw FP16 bits.
+//
+// Tensor-core decode: code pair j of each 16-bit half (positions 0..3 of w, 4..7 of
+// w >> 8) becomes the FP16 subnormal (code+2)·4^(j%4)·2^-24 with one LOP3 (mask, then
+// flip bit 1).  The B operand holds x·2^-e·4^-(j%4) (per-tile exponent e), so every
+// product is (code+2)·x·2^(-24-e) and the FP32 accumulator of one tile-stage is
+// 2^(-24-e)·Σ(code+2)·x.  The epilogue applies f = 2^(24+e), subtracts the
+// row-independent 2·Σx term and multiplies by the row's FP16 scale.
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdint>
+#include <cstring>
+#include <mutex>
+#include <type_traits>
+
+#include "harpq_b200.h"
+#include "hqb_device.cuh"
+#include "hqb_internal.h"
+#include "hqb_schedule.h"
+
+namespace hqb {
+
+constexpr uint32_t kRowBlockBytes = 544;
+constexpr uint32_t kRecordBytes = HQB_TILE_RECORD_BYTES;
+constexpr uint32_t kConsumerWarps = 8;
+constexpr uint32_t kGemvThreads = (kConsumerWarps + 1) * 32;
+constexpr uint32_t kRingLog2 = 3;  // 8 tile-stage slots per CTA (34 KB in flight)
+constexpr uint32_t kXRing = 4;
+constexpr uint32_t kMaxCtasPerSm = 2;
+
+static_assert(kRecordBytes == 8 * kRowBlockBytes, "record = 8 row blocks");
+
+struct GemvParams {
+  const uint8_t* planes[HQB_MAX_STAGES];
+  const uint8_t* depth;  // [R][C] or null (uniform)
+  const uint32_t* plan;  // [R+1] or null
+  const uint8_t* xfrag;
+  const void* bias;
+  void* y;
+  float* partials;     // [G][2][batch][128]
+  uint32_t* counters;  // [R][8]
+  int* error;
+  uint64_t total;      // units (uniform); mixed reads plan[R]
+  uint32_t rows;
+  uint32_t R, C;
+  uint32_t prefix;
+  uint32_t stage_count;
+  uint32_t batch;
+  uint32_t xslot_bytes;
+  int bias_dtype;
+  int y_dtype;
+};
+
+__host__ __device__ inline uint32_t xslot_bytes_for(uint32_t batch, uint32_t xl) {
+  return static_cast<uint32_t>((batch * (256u * xl + 8u) + 15u) / 16u * 16u);
+}
+
+// --------------------------------------------------------------------------------------
+// repack
+
+__global__ void __launch_bounds__(256) repack_kernel(const uint8_t* __restrict__ codes,
+                                                     const uint16_t* __restrict__ scales,
+                                                     uint8_t* __restrict__ plane,
+                                                     uint64_t row_bytes, uint32_t rows,
+                                                     uint32_t cols, uint32_t C, int* flags,
+                                                     int aligned4) {
+  const uint32_t tile = blockIdx.x;
+  const uint32_t r = tile / C, c = tile % C;
+  const uint32_t rb = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, q = lane & 3;
+  uint32_t words[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint32_t row = r * 128 + rb * 16 + g + 8 * (i & 1);
+    const uint32_t col0 = c * 128 + 32 * q + 16 * (i >> 1);
+    uint32_t w = 0;
+    if (row < rows && col0 < cols) {
+      const uint8_t* src = codes + static_cast<uint64_t>(row) * row_bytes + c * 32 + 8 * q + 4 * (i >> 1);
+      w = aligned4 ? *reinterpret_cast<const uint32_t*>(src)
+                   : (uint32_t)src[0] | ((uint32_t)src[1] << 8) | ((uint32_t)src[2] << 16) |
+                         ((uint32_t)src[3] << 24);
+      const uint32_t valid = cols - col0;
+      if (valid < 16) w &= (1u << (2 * valid)) - 1u;  // clear codes of padded columns
+    }
+    words[i] = w;
+  }
+  uint8_t* rec = plane + static_cast<uint64_t>(tile) * kRecordBytes + rb * kRowBlockBytes;
+  *reinterpret_cast<uint4*>(rec + lane * 16) = make_uint4(words[0], words[1], words[2], words[3]);
+  if (lane < 8) {
+    const uint64_t base = static_cast<uint64_t>(tile) * 128 + rb * 16 + lane;
+    const uint32_t s0 = scales[base], s1 = scales[base + 8];
+    int bad = 0;
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const uint32_t s = k ? s1 : s0;
+      if (((s >> 10) & 0x1F) == 0x1F || ((s & 0x8000u) && (s & 0x7FFFu))) bad = 1;
+    }
+    if (bad && flags != nullptr) atomicOr(flags, HQB_DEVERR_SCALE);
+    *reinterpret_cast<uint32_t*>(rec + 512 + lane * 4) = s0 | (s1 << 16);
+  }
+}
+
+// --------------------------------------------------------------------------------------
+// activation preparation
+
+template <int XL, typename XT>
+__global__ void __launch_bounds__(128) prep_x_kernel(const XT* __restrict__ x, uint32_t cols,
+                                                     uint32_t batch, uint8_t* __restrict__ xfrag,
+                                                     uint32_t xslot) {
+  __shared__ float red[4];
+  const uint32_t c = blockIdx.x, b = blockIdx.y, k = threadIdx.x;
+  const uint32_t col = c * 128 + k;
+  float v = 0.0f;
+  if (col < cols) {
+    if constexpr (sizeof(XT) == 2) v = __half2float(x[static_cast<uint64_t>(b) * cols + col]);
+    else v = x[static_cast<uint64_t>(b) * cols + col];
+  }
+  // tile exponent e: the largest |x| of the tile lands in [2^14, 2^15) after 2^-e
+  float a = fabsf(v);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
+  if ((k & 31) == 0) red[k >> 5] = a;
+  __syncthreads();
+  const float amax = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+  __syncthreads();
+  int e = 0;
+  if (amax > 0.0f) e = max(-100, min(100, ilogbf(amax) - 14));
+  const uint32_t m = k & 7, which = (k >> 3) & 3, q = k >> 5, jj = m & 3;
+  const float xs = ldexpf(v, -e - 2 * static_cast<int>(jj));
+  const __half hi = __float2half_rn(xs);
+  float eff = __half2float(hi);
+  uint8_t* slot = xfrag + static_cast<uint64_t>(c) * xslot;
+  const uint32_t idx = (b * 4 + q) * 32 + m * 4 + which;
+  reinterpret_cast<__half*>(slot)[idx] = hi;
+  if constexpr (XL == 2) {
+    const __half lo = __float2half_rn(xs - eff);
+    eff += __half2float(lo);
+    reinterpret_cast<__half*>(slot + batch * 256)[idx] = lo;
+  }
+  float xt = ldexpf(eff, 2 * static_cast<int>(jj));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) xt += __shfl_xor_sync(0xffffffffu, xt, o);
+  if ((k & 31) == 0) red[k >> 5] = xt;
+  __syncthreads();
+  if (k == 0) {
+    const float sum = (red[0] + red[1]) + (red[2] + red[3]);
+    *reinterpret_cast<float2*>(slot + batch * 256 * XL + b * 8) =
+        make_float2(ldexpf(1.0f, 24 + e), ldexpf(sum, e + 1));
+  }
+}
+
+// --------------------------------------------------------------------------------------
+// GEMV
+
+struct Cursor {
+  uint32_t r, c, s, d;
+
+  __device__ bool init(uint64_t u, const GemvParams& p) {
+    if (p.plan == nullptr) {
+      const uint64_t per_row = static_cast<uint64_t>(p.C) * p.prefix;
+      r = static_cast<uint32_t>(u / per_row);
+      const uint64_t rem = u - static_cast<uint64_t>(r) * per_row;
+      c = static_cast<uint32_t>(rem / p.prefix);
+      s = static_cast<uint32_t>(rem - static_cast<uint64_t>(c) * p.prefix);
+      d = p.prefix;
+      return true;
+    }
+    r = row_of_unit(u, p.plan, p.R, 0);
+    uint64_t off = u - p.plan[r];
+    for (c = 0; c < p.C; ++c) {
+      d = clamp_depth(p.depth[static_cast<uint64_t>(r) * p.C + c], p.stage_count);
+      if (off < d) {
+        s = static_cast<uint32_t>(off);
+        return true;
+      }
+      off -= d;
+    }
+    return false;  // plan and depth map disagree
+  }
+
+  __device__ void advance(const GemvParams& p) {
+    if (++s < d) return;
+    s = 0;
+    if (++c == p.C) {
+      c = 0;
+      ++r;
+    }
+    if (p.plan != nullptr && r < p.R) d = clamp_depth(p.depth[static_cast<uint64_t>(r) * p.C + c], p.stage_count);
+  }
+
+  __device__ const uint8_t* record(const GemvParams& p) const {
+    return p.planes[s] + (static_cast<uint64_t>(r) * p.C + c) * kRecordBytes;
+  }
+};
+
+struct Pipe {
+  uint8_t* ring;
+  uint8_t* xring;
+  uint64_t* full;
+  uint64_t* empty;
+  uint64_t* xfull;
+  uint64_t* xempty;
+};
+
+__device__ void gemv_producer(const GemvParams& p, const Pipe& pp, uint64_t u0, uint32_t n) {
+  const uint64_t stream_policy = policy_evict_first();
+  const uint64_t keep_policy = policy_evict_last();
+  constexpr uint32_t NS = 1u << kRingLog2;
+  Cursor cur;
+  if (!cur.init(u0, p)) {
+    atomicOr(p.error, HQB_DEVERR_DEPTH);
+    return;  // nothing issued
+  }
+  // Prologue: weight records do not depend on the preceding kernel (see
+  // HQB_FLAG_PDL), so fill the ring before waiting for it.
+  const uint32_t pre = min(n, NS);
+  uint32_t issued = 0, tiles = 0;
+  bool ok = true;
+  Cursor pc = cur;
+  for (; issued < pre; ++issued) {
+    if (pc.r >= p.R) {  // only reachable when a depth plan disagrees with its map
+      atomicOr(p.error, HQB_DEVERR_DEPTH);
+      ok = false;
+      break;
+    }
+    mbar_expect_tx(&pp.full[issued], kRecordBytes);
+    bulk_load(pp.ring + issued * kRecordBytes, pc.record(p), kRecordBytes, &pp.full[issued], stream_policy);
+    pc.advance(p);
+  }
+  griddep_wait();
+  for (uint32_t i = 0; ok && i < n; ++i) {
+    if (cur.r >= p.R) {
+      atomicOr(p.error, HQB_DEVERR_DEPTH);
+      break;
+    }
+    if (i == 0 || cur.s == 0) {
+      const uint32_t xs = tiles % kXRing;
+      if (tiles >= kXRing && !mbar_wait(&pp.xempty[xs], ((tiles / kXRing) - 1) & 1, p.error)) break;
+      mbar_expect_tx(&pp.xfull[xs], p.xslot_bytes);
+      bulk_load(pp.xring + xs * p.xslot_bytes, p.xfrag + static_cast<uint64_t>(cur.c) * p.xslot_bytes,
+                p.xslot_bytes, &pp.xfull[xs], keep_policy);
+      ++tiles;
+    }
+    if (i >= NS) {
+      const uint32_t slot = i & (NS - 1);
+      if (!mbar_wait(&pp.empty[slot], ((i >> kRingLog2) - 1) & 1, p.error)) break;
+      mbar_expect_tx(&pp.full[slot], kRecordBytes);
+      bulk_load(pp.ring + slot * kRecordBytes, cur.record(p), kRecordBytes, &pp.full[slot], stream_policy);
+      issued = i + 1;
+    }
+    cur.advance(p);
+  }
+  griddep_launch_dependents();
+  // Every bulk copy this CTA issued must land before the CTA may exit, whatever
+  // path led here (consumers may have left early on an error).
+  for (uint32_t j = issued > NS ? issued - NS : 0; j < issued; ++j)
+    mbar_wait(&pp.full[j & (NS - 1)], (j >> kRingLog2) & 1, p.error);
+  for (uint32_t t = tiles > kXRing ? tiles - kXRing : 0; t < tiles; ++t)
+    mbar_wait(&pp.xfull[t % kXRing], (t / kXRing) & 1, p.error);
+}
+
+template <int NB>
+__device__ __forceinline__ void store_out(const GemvParams& p, const float (&v)[NB][4], uint32_t row0,
+                                          uint32_t q) {
+  const uint32_t row1 = row0 + 8;
+#pragma unroll
+  for (int nb = 0; nb < NB; ++nb) {
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const uint32_t b = 2 * q + j + 8 * nb;
+      if (b >= p.batch) continue;
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const uint32_t row = h ? row1 : row0;
+        if (row >= p.rows) continue;
+        float out = v[nb][2 * h + j];
+        if (p.bias != nullptr) {
+          out += p.bias_dtype == HQB_F16 ? __half2float(static_cast<const __half*>(p.bias)[row])
+                                         : static_cast<const float*>(p.bias)[row];
+        }
+        const uint64_t o = static_cast<uint64_t>(b) * p.rows + row;
+        if (p.y_dtype == HQB_F16) static_cast<__half*>(p.y)[o] = __float2half_rn(out);
+        else static_cast<float*>(p.y)[o] = out;
+      }
+    }
+  }
+}
+
+// Finishes the contribution of this warp's 16 rows of tile row r.
+template <int NB>
+__device__ void flush_rows(const GemvParams& p, uint32_t r, const float (&y)[NB][4], uint32_t cta,
+                           uint64_t total, uint32_t ctas, uint32_t warp, uint32_t lane) {
+  const uint64_t per_row = static_cast<uint64_t>(p.C) * p.prefix;
+  const uint64_t rb = row_begin(r, p.plan, per_row), re = row_begin(r + 1, p.plan, per_row);
+  const uint32_t first = unit_owner(rb, total, ctas), last = unit_owner(re - 1, total, ctas);
+  const uint32_t g = lane >> 2, q = lane & 3;
+  const uint32_t rit0 = warp * 16 + g;
+  const uint32_t row0 = r * 128 + rit0;
+  if (first == last) {
+    store_out<NB>(p, y, row0, q);
+    return;
+  }
+  const uint32_t k = row_of_unit(unit_start(cta, total, ctas), p.plan, p.R, per_row) == r ? 0 : 1;
+  float* part = p.partials + static_cast<uint64_t>(cta * 2 + k) * p.batch * 128;
+#pragma unroll
+  for (int nb = 0; nb < NB; ++nb)
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const uint32_t b = 2 * q + j + 8 * nb;
+      if (b < p.batch) {
+        part[b * 128 + rit0] = y[nb][j];
+        part[b * 128 + rit0 + 8] = y[nb][2 + j];
+      }
+    }
+  __threadfence();
+  __syncwarp();
+  uint32_t ticket = 0;
+  if (lane == 0) ticket = atomicAdd(&p.counters[r * 8 + warp], 1u);
+  ticket = __shfl_sync(0xffffffffu, ticket, 0);
+  if (ticket != last - first) return;
+  __threadfence();
+  float sum[NB][4];
+#pragma unroll
+  for (int nb = 0; nb < NB; ++nb)
+#pragma unroll
+    for (int k2 = 0; k2 < 4; ++k2) sum[nb][k2] = 0.0f;
+  for (uint32_t i = first; i <= last; ++i) {
+    const uint32_t ki = row_of_unit(unit_start(i, total, ctas), p.plan, p.R, per_row) == r ? 0 : 1;
+    const float* src = p.partials + static_cast<uint64_t>(i * 2 + ki) * p.batch * 128;
+#pragma unroll
+    for (int nb = 0; nb < NB; ++nb)
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const uint32_t b = 2 * q + j + 8 * nb;
+        if (b < p.batch) {
+          sum[nb][j] += __ldcg(src + b * 128 + rit0);
+          sum[nb][2 + j] += __ldcg(src + b * 128 + rit0 + 8);
+        }
+      }
+  }
+  store_out<NB>(p, sum, row0, q);
+  if (lane == 0) p.counters[r * 8 + warp] = 0;  // cleared for the next launch
+}
+
+__device__ __forceinline__ uint32_t int2_pair(uint32_t w, uint32_t w_hi, int m) {
+  const int sh = 2 * (m & 3);
+  return (((m < 4) ? w : w_hi) & (0x00030003u << sh)) ^ (0x00020002u << sh);
+}
+
+// Tensor-core consumer state for one warp.
+template <int NB, int XL>
+struct MmaConsumer {
+  uint32_t bf[NB][XL][8][2];
+  float f[NB][2], gsum[NB][2];
+
+  __device__ void load_x(const GemvParams& p, const uint8_t* slot, uint32_t lane) {
+    const uint32_t g = lane >> 2, q = lane & 3;
+#pragma unroll
+    for (int nb = 0; nb < NB; ++nb) {
+      const uint32_t b = g + 8 * nb;
+#pragma unroll
+      for (int l = 0; l < XL; ++l) {
+        if (b < p.batch) {
+          const uint8_t* src = slot + l * p.batch * 256 + (b * 4 + q) * 64;
+#pragma unroll
+          for (int v = 0; v < 4; ++v) {
+            const uint4 t = lds128(src + 16 * v);
+            bf[nb][l][2 * v][0] = t.x;
+            bf[nb][l][2 * v][1] = t.y;
+            bf[nb][l][2 * v + 1][0] = t.z;
+            bf[nb][l][2 * v + 1][1] = t.w;
+          }
+        } else {
+#pragma unroll
+          for (int m = 0; m < 8; ++m) bf[nb][l][m][0] = bf[nb][l][m][1] = 0u;
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const uint32_t bb = 2 * q + j + 8 * nb;
+        float2 fg = make_float2(0.0f, 0.0f);
+        if (bb < p.batch) fg = lds_f2(slot + p.batch * 256 * XL + bb * 8);
+        f[nb][j] = fg.x;
+        gsum[nb][j] = fg.y;
+      }
+    }
+  }
+
+  __device__ __forceinline__ void tile_stage(const uint4 w, uint32_t sc, float (&y)[NB][4]) const {
+    const uint32_t h0 = w.x >> 8, h1 = w.y >> 8, h2 = w.z >> 8, h3 = w.w >> 8;
+    float acc[NB][2][4];
+#pragma unroll
+    for (int nb = 0; nb < NB; ++nb)
+#pragma unroll
+      for (int k = 0; k < 2; ++k)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc[nb][k][e] = 0.0f;
+#pragma unroll
+    for (int m = 0; m < 8; ++m) {
+      const uint32_t a0 = int2_pair(w.x, h0, m), a1 = int2_pair(w.y, h1, m);
+      const uint32_t a2 = int2_pair(w.z, h2, m), a3 = int2_pair(w.w, h3, m);
+#pragma unroll
+      for (int nb = 0; nb < NB; ++nb)
+#pragma unroll
+        for (int l = 0; l < XL; ++l) mma_f16(acc[nb][m & 1], a0, a1, a2, a3, bf[nb][l][m][0], bf[nb][l][m][1]);
+    }
+    const float s_lo = half_bits_to_float(sc & 0xFFFFu), s_hi = half_bits_to_float(sc >> 16);
+#pragma unroll
+    for (int nb = 0; nb < NB; ++nb) {
+      const float t0 = acc[nb][0][0] + acc[nb][1][0], t1 = acc[nb][0][1] + acc[nb][1][1];
+      const float t2 = acc[nb][0][2] + acc[nb][1][2], t3 = acc[nb][0][3] + acc[nb][1][3];
+      y[nb][0] = fmaf(s_lo, fmaf(t0, f[nb][0], -gsum[nb][0]), y[nb][0]);
+      y[nb][1] = fmaf(s_lo, fmaf(t1, f[nb][1], -gsum[nb][1]), y[nb][1]);
+      y[nb][2] = fmaf(s_hi, fmaf(t2, f[nb][0], -gsum[nb][0]), y[nb][2]);
+      y[nb][3] = fmaf(s_hi, fmaf(t3, f[nb][1], -gsum[nb][1]), y[nb][3]);
+    }
+  }
+
+  __device__ __forceinline__ void finish(float (&)[NB][4], uint32_t) const {}
+};
+
+// CUDA-core consumer (comparison kernel): codes decoded to FP32 with an exponent
+// trick, FFMA per code and batch row.  Batch <= 8, FP16 activations.
+struct SimtConsumer {
+  const uint8_t* slot;
+  float xscale[8];  // 2^e of the current tile per batch row
+  float part[2][8];
+
+  __device__ void reset() {
+#pragma unroll
+    for (int h = 0; h < 2; ++h)
+#pragma unroll
+      for (int b = 0; b < 8; ++b) part[h][b] = 0.0f;
+  }
+
+  __device__ void load_x(const GemvParams& p, const uint8_t* s, uint32_t) {
+    slot = s;
+#pragma unroll
+    for (int b = 0; b < 8; ++b)
+      xscale[b] = b < static_cast<int>(p.batch) ? lds_f2(s + p.batch * 256 + b * 8).x * 0x1p-24f : 0.0f;
+  }
+
+  __device__ __forceinline__ void tile_stage(const GemvParams& p, uint32_t lane, const uint4 w, uint32_t sc) {
+    const uint32_t q = lane & 3;
+    const float s_lo = half_bits_to_float(sc & 0xFFFFu), s_hi = half_bits_to_float(sc >> 16);
+#pragma unroll
+    for (uint32_t b = 0; b < 8; ++b) {
+      if (b >= p.batch) break;
+      const uint8_t* src = slot + (b * 4 + q) * 64;
+      uint32_t hx[16];
+#pragma unroll
+      for (int v = 0; v < 4; ++v) {
+        const uint4 t = lds128(src + 16 * v);
+        hx[4 * v] = t.x;
+        hx[4 * v + 1] = t.y;
+        hx[4 * v + 2] = t.z;
+        hx[4 * v + 3] = t.w;
+      }
+      float d0 = 0.0f, d1 = 0.0f;
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const int m = i & 7, which = i >> 3;
+        const int idx = m * 4 + which;  // half index inside (b, q)
+        const uint32_t hb = (idx & 1) ? (hx[idx >> 1] >> 16) : (hx[idx >> 1] & 0xFFFFu);
+        const float xv = half_bits_to_float(hb) * static_cast<float>(1 << (2 * (m & 3)));
+        const uint32_t wg = i < 16 ? w.x : w.z, wh = i < 16 ? w.y : w.w;
+        const int sh = 2 * (i & 15);
+        const float cg = __uint_as_float(0x4B000000u | (((wg >> sh) & 3u) ^ 2u)) - 8388610.0f;
+        const float ch = __uint_as_float(0x4B000000u | (((wh >> sh) & 3u) ^ 2u)) - 8388610.0f;
+        d0 = fmaf(cg, xv, d0);
+        d1 = fmaf(ch, xv, d1);
+      }
+      part[0][b] = fmaf(s_lo * xscale[b], d0, part[0][b]);
+      part[1][b] = fmaf(s_hi * xscale[b], d1, part[1][b]);
+    }
+  }
+
+  // Reduce the quad's column partials and move to the tensor-core output layout.
+  __device__ void finish(float (&y)[1][4], uint32_t lane) {
+    const uint32_t q = lane & 3;
+#pragma unroll
+    for (int h = 0; h < 2; ++h)
+#pragma unroll
+      for (int b = 0; b < 8; ++b) {
+        float v = part[h][b];
+        v += __shfl_xor_sync(0xffffffffu, v, 1);
+        v += __shfl_xor_sync(0xffffffffu, v, 2);
+        part[h][b] = v;
+      }
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      float v0 = 0.0f, v1 = 0.0f;
+#pragma unroll
+      for (int b = 0; b < 8; ++b)
+        if (static_cast<uint32_t>(b) == 2 * q + j) {
+          v0 = part[0][b];
+          v1 = part[1][b];
+        }
+      y[0][j] = v0;
+      y[0][2 + j] = v1;
+    }
+    reset();
+  }
+};
+
+template <int NB, int XL, bool SIMT>
+__global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_constant__ GemvParams p) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  constexpr uint32_t NS = 1u << kRingLog2;
+  const uint32_t ctas = gridDim.x, cta = blockIdx.x;
+  const uint64_t total = p.plan != nullptr ? static_cast<uint64_t>(p.plan[p.R]) : p.total;
+  const uint64_t u0 = unit_start(cta, total, ctas), u1 = unit_start(cta + 1, total, ctas);
+  if (u0 >= u1) return;
+  const uint32_t n = static_cast<uint32_t>(u1 - u0);
+
+  Pipe pp;
+  pp.ring = smem;
+  pp.xring = smem + NS * kRecordBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(pp.xring + kXRing * p.xslot_bytes);
+  pp.full = bars;
+  pp.empty = bars + NS;
+  pp.xfull = bars + 2 * NS;
+  pp.xempty = bars + 2 * NS + kXRing;
+  const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (uint32_t i = 0; i < NS; ++i) {
+      mbar_init(&pp.full[i], 1);
+      mbar_init(&pp.empty[i], kConsumerWarps);
+    }
+    for (uint32_t i = 0; i < kXRing; ++i) {
+      mbar_init(&pp.xfull[i], 1);
+      mbar_init(&pp.xempty[i], kConsumerWarps);
+    }
+    fence_barrier_init();
+  }
+  __syncthreads();
+
+  if (warp == kConsumerWarps) {
+    if (lane == 0) gemv_producer(p, pp, u0, n);
+    return;
+  }
+
+  Cursor cur;
+  if (!cur.init(u0, p)) return;  // producer records the error
+  griddep_wait();
+  using Consumer = typename std::conditional<SIMT, SimtConsumer, MmaConsumer<NB, XL>>::type;
+  Consumer cons;
+  if constexpr (SIMT) cons.reset();
+  float y[NB][4];
+#pragma unroll
+  for (int nb = 0; nb < NB; ++nb)
+#pragma unroll
+    for (int k = 0; k < 4; ++k) y[nb][k] = 0.0f;
+  const uint32_t g = lane >> 2;
+  uint32_t tiles = 0;
+  for (uint32_t i = 0; i < n; ++i) {
+    if (cur.r >= p.R) return;  // inconsistent depth plan: the producer records it
+    if (i == 0 || cur.s == 0) {
+      const uint32_t xs = tiles % kXRing;
+      if (!mbar_wait(&pp.xfull[xs], (tiles / kXRing) & 1, p.error)) return;
+      cons.load_x(p, pp.xring + xs * p.xslot_bytes, lane);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&pp.xempty[xs]);
+      ++tiles;
+    }
+    const uint32_t slot = i & (NS - 1);
+    if (!mbar_wait(&pp.full[slot], (i >> kRingLog2) & 1, p.error)) return;
+    const uint8_t* rec = pp.ring + slot * kRecordBytes + warp * kRowBlockBytes;
+    const uint4 w = lds128(rec + lane * 16);
+    const uint32_t sc = lds32(rec + 512 + g * 4);
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&pp.empty[slot]);
+    if constexpr (SIMT) cons.tile_stage(p, lane, w, sc);
+    else cons.tile_stage(w, sc, y);
+    const uint32_t r_now = cur.r;
+    cur.advance(p);
+    if (i + 1 == n || cur.r != r_now) {
+      if constexpr (SIMT) cons.finish(y, lane);
+      flush_rows<NB>(p, r_now, y, cta, total, ctas, warp, lane);
+#pragma unroll
+      for (int nb = 0; nb < NB; ++nb)
+#pragma unroll
+        for (int k = 0; k < 4; ++k) y[nb][k] = 0.0f;
+    }
+  }
+}
+
+// --------------------------------------------------------------------------------------
+// decode (bit-exact dense weights), depth plan, prefix-0 fill
+
+__global__ void __launch_bounds__(256) decode_kernel(hqb_plane_matrix m, uint32_t prefix,
+                                                     const uint8_t* __restrict__ depth, float* __restrict__ out) {
+  const uint32_t tile = blockIdx.x;
+  const uint32_t r = tile / m.grid_cols, c = tile % m.grid_cols;
+  const uint32_t rb = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, q = lane & 3;
+  uint32_t d = prefix;
+  if (depth != nullptr) d = clamp_depth(depth[tile], m.stage_count);
+  uint32_t words[HQB_MAX_STAGES][4];
+  float sc[HQB_MAX_STAGES][2];
+#pragma unroll
+  for (uint32_t s = 0; s < HQB_MAX_STAGES; ++s) {
+    if (s < d) {
+      const uint8_t* rec = static_cast<const uint8_t*>(m.planes[s]) + static_cast<uint64_t>(tile) * kRecordBytes +
+                           rb * kRowBlockBytes;
+      const uint4 w = *reinterpret_cast<const uint4*>(rec + lane * 16);
+      words[s][0] = w.x;
+      words[s][1] = w.y;
+      words[s][2] = w.z;
+      words[s][3] = w.w;
+      const uint32_t pair = *reinterpret_cast<const uint32_t*>(rec + 512 + g * 4);
+      sc[s][0] = half_bits_to_float(pair & 0xFFFFu);
+      sc[s][1] = half_bits_to_float(pair >> 16);
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint64_t row = static_cast<uint64_t>(r) * 128 + rb * 16 + g + 8 * (i & 1);
+    const uint64_t col0 = static_cast<uint64_t>(c) * 128 + 32 * q + 16 * (i >> 1);
+    if (row >= m.rows) continue;
+#pragma unroll 4
+    for (int k = 0; k < 16; ++k) {
+      if (col0 + k >= m.cols) break;
+      float wsum = 0.0f;
+#pragma unroll
+      for (uint32_t s = 0; s < HQB_MAX_STAGES; ++s) {
+        if (s >= d) break;
+        const uint32_t raw = (words[s][i] >> (2 * k)) & 3u;
+        const float code = static_cast<float>(raw >= 2 ? static_cast<int>(raw) - 4 : static_cast<int>(raw));
+        wsum = __fadd_rn(wsum, __fmul_rn(code, sc[s][i & 1]));
+      }
+      out[row * m.cols + col0 + k] = wsum;
+    }
+  }
+}
+
+__global__ void __launch_bounds__(1024) depth_plan_kernel(const uint8_t* __restrict__ depth, uint32_t R,
+                                                          uint32_t C, uint32_t stage_count,
+                                                          uint32_t* __restrict__ plan, int* flags) {
+  const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  for (uint32_t r = warp; r < R; r += nw) {
+    uint32_t cost = 0;
+    int bad = 0;
+    for (uint32_t c = lane; c < C; c += 32) {
+      const uint32_t d = depth[static_cast<uint64_t>(r) * C + c];
+      if (d < 1 || d > stage_count) bad = 1;
+      cost += clamp_depth(d, stage_count);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      cost += __shfl_xor_sync(0xffffffffu, cost, o);
+      bad |= __shfl_xor_sync(0xffffffffu, bad, o);
+    }
+    if (lane == 0) {
+      plan[r + 1] = cost;
+      if (bad && flags != nullptr) atomicOr(flags, HQB_DEVERR_DEPTH);
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    uint32_t run = 0;
+    plan[0] = 0;
+    for (uint32_t r = 0; r < R; ++r) {
+      run += plan[r + 1];
+      plan[r + 1] = run;
+    }
+  }
+}
+
+__global__ void fill_kernel(const void* bias, int bias_dtype, void* y, int y_dtype, uint32_t rows, uint32_t batch) {
+  const uint64_t n = static_cast<uint64_t>(rows) * batch;
+  for (uint64_t i = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
+    const uint32_t row = static_cast<uint32_t>(i % rows);
+    float v = 0.0f;
+    if (bias != nullptr)
+      v = bias_dtype == HQB_F16 ? __half2float(static_cast<const __half*>(bias)[row]) : static_cast<const float*>(bias)[row];
+    if (y_dtype == HQB_F16) static_cast<__half*>(y)[i] = __float2half_rn(v);
+    else static_cast<float*>(y)[i] = v;
+  }
+}
+
+// --------------------------------------------------------------------------------------
+// host side
+
+int device_sm_count(int device) {
+  static std::mutex mu;
+  static int cache[64] = {0};
+  if (device < 0 || device >= 64) return 0;
+  std::lock_guard<std::mutex> lock(mu);
+  if (cache[device] == 0) {
+    int v = 0;
+    if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, device) != cudaSuccess) {
+      cudaGetLastError();
+      return 0;
+    }
+    cache[device] = v;
+  }
+  return cache[device];
+}
+
+namespace {
+
+struct WsLayout {
+  uint64_t counters, partials, xfrag, total;
+};
+
+WsLayout ws_layout(uint32_t R, uint32_t C, uint32_t batch, uint32_t xl, int sms) {
+  WsLayout L{};
+  L.counters = 256;
+  L.partials = L.counters + round_up(static_cast<uint64_t>(R) * 8 * 4, 256);
+  const uint64_t gmax = static_cast<uint64_t>(sms) * kMaxCtasPerSm;
+  L.xfrag = L.partials + round_up(gmax * 2 * batch * 128 * 4, 256);
+  L.total = L.xfrag + round_up(static_cast<uint64_t>(C) * xslot_bytes_for(batch, xl), 256);
+  return L;
+}
+
+bool plane_matrix_ok(const hqb_plane_matrix* m) {
+  if (m == nullptr || m->rows == 0 || m->cols == 0 || m->stage_count == 0 || m->stage_count > HQB_MAX_STAGES)
+    return false;
+  if (m->grid_rows != (m->rows + 127) / 128 || m->grid_cols != (m->cols + 127) / 128) return false;
+  if (m->rows > 0xFFFFFFFFull || m->cols > 0xFFFFFFFFull) return false;
+  return true;
+}
+
+bool stage_planes_ok(const hqb_plane_matrix* m, uint32_t needed) {
+  for (uint32_t s = 0; s < needed; ++s) {
+    if (m->planes[s] == nullptr || (reinterpret_cast<uintptr_t>(m->planes[s]) & 15u) != 0) return false;
+  }
+  return true;
+}
+
+using GemvKernel = void (*)(GemvParams);
+
+GemvKernel pick_kernel(uint32_t nb, uint32_t xl, bool simt) {
+  if (simt) return gemv_kernel<1, 1, true>;
+  if (nb == 1) return xl == 1 ? gemv_kernel<1, 1, false> : gemv_kernel<1, 2, false>;
+  return xl == 1 ? gemv_kernel<2, 1, false> : gemv_kernel<2, 2, false>;
+}
+
+uint32_t gemv_smem_bytes(uint32_t xslot) {
+  return (1u << kRingLog2) * kRecordBytes + kXRing * xslot + (2 * (1u << kRingLog2) + 2 * kXRing) * 8;
+}
+
+// Resident CTAs per SM for a kernel variant at a given shared-memory size (cached).
+int ctas_per_sm(GemvKernel k, uint32_t smem, int device) {
+  struct Entry {
+    GemvKernel k;
+    uint32_t smem;
+    int device;
+    int ctas;
+  };
+  static std::mutex mu;
+  static Entry cache[64];
+  static int used = 0;
+  std::lock_guard<std::mutex> lock(mu);
+  for (int i = 0; i < used; ++i)
+    if (cache[i].k == k && cache[i].smem == smem && cache[i].device == device) return cache[i].ctas;
+  if (cudaFuncSetAttribute(reinterpret_cast<const void*>(k), cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           static_cast<int>(smem)) != cudaSuccess)
+    return 0;
+  int n = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k, kGemvThreads, smem) != cudaSuccess) return 0;
+  n = std::min<int>(n, kMaxCtasPerSm);
+  if (used < 64) cache[used++] = Entry{k, smem, device, n};
+  return n;
+}
+
+cudaError_t launch_prep(const void* x, int x_dtype, uint64_t cols, uint32_t batch, void* xfrag, cudaStream_t st) {
+  const uint32_t C = static_cast<uint32_t>((cols + 127) / 128);
+  const uint32_t xl = x_dtype == HQB_F32 ? 2 : 1;
+  const dim3 grid(C, batch);
+  const uint32_t xs = xslot_bytes_for(batch, xl);
+  if (x_dtype == HQB_F32)
+    prep_x_kernel<2, float><<<grid, 128, 0, st>>>(static_cast<const float*>(x), static_cast<uint32_t>(cols), batch,
+                                                  static_cast<uint8_t*>(xfrag), xs);
+  else
+    prep_x_kernel<1, __half><<<grid, 128, 0, st>>>(static_cast<const __half*>(x), static_cast<uint32_t>(cols), batch,
+                                                   static_cast<uint8_t*>(xfrag), xs);
+  return cudaGetLastError();
+}
+
+}  // namespace
+}  // namespace hqb
+
+using namespace hqb;
+
+extern "C" {
+
+HQB_API int hqb_version(void) { return 1; }
+
+HQB_API const char* hqb_status_string(int status) {
+  switch (status) {
+    case HQB_OK: return "success";
+    case HQB_ERR_INVALID: return "invalid argument (nothing enqueued)";
+    case HQB_ERR_UNSUPPORTED: return "geometry not supported by the plane layout";
+    default: return cudaGetErrorString(static_cast<cudaError_t>(status));
+  }
+}
+
+HQB_API uint64_t hqb_plane_bytes(const hqb_geometry* g) {
+  if (g == nullptr || g->tile_rows != HQB_TILE || g->tile_columns != HQB_TILE || g->group_size != HQB_TILE) return 0;
+  if (g->original_rows == 0 || g->original_columns == 0) return 0;
+  const uint64_t R = (g->original_rows + 127) / 128, C = (g->original_columns + 127) / 128;
+  if (g->padded_rows != R * 128 || g->padded_columns != C * 128) return 0;
+  uint64_t tiles = 0, bytes = 0;
+  if (!mul_ok(R, C, &tiles) || !mul_ok(tiles, kRecordBytes, &bytes)) return 0;
+  return bytes;
+}
+
+HQB_API int hqb_repack_stage(const hqb_geometry* g, const hqb_raw_stage* stage, void* plane, int* device_flags,
+                             void* stream) {
+  const uint64_t bytes = hqb_plane_bytes(g);
+  if (g != nullptr && bytes == 0 &&
+      (g->tile_rows != HQB_TILE || g->tile_columns != HQB_TILE || g->group_size != HQB_TILE))
+    return HQB_ERR_UNSUPPORTED;
+  if (bytes == 0 || stage == nullptr || plane == nullptr || stage->packed_codes == nullptr ||
+      stage->scale_fp16_bits == nullptr || (reinterpret_cast<uintptr_t>(plane) & 15u) != 0)
+    return HQB_ERR_INVALID;
+  const uint64_t R = g->padded_rows / 128, C = g->padded_columns / 128;
+  if (g->original_rows > 0xFFFFFFFFull || g->original_columns > 0xFFFFFFFFull || R * C > 0x7FFFFFFFull)
+    return HQB_ERR_INVALID;
+  if (stage->packed_code_bytes != g->padded_rows * g->padded_columns / 4 || stage->scale_count != R * C * 128)
+    return HQB_ERR_INVALID;
+  const cudaError_t prior = take_prior_error();
+  if (prior != cudaSuccess) return prior;
+  const int aligned4 = (reinterpret_cast<uintptr_t>(stage->packed_codes) & 3u) == 0;
+  repack_kernel<<<static_cast<unsigned>(R * C), 256, 0, as_stream(stream)>>>(
+      stage->packed_codes, stage->scale_fp16_bits, static_cast<uint8_t*>(plane), g->padded_columns / 4,
+      static_cast<uint32_t>(g->original_rows), static_cast<uint32_t>(g->original_columns), static_cast<uint32_t>(C),
+      device_flags, aligned4);
+  return cudaGetLastError();
+}
+
+HQB_API uint64_t hqb_xfrag_bytes(uint64_t cols, uint32_t batch, int x_dtype) {
+  if (cols == 0 || batch == 0 || batch > HQB_MAX_BATCH || (x_dtype != HQB_F16 && x_dtype != HQB_F32)) return 0;
+  return ((cols + 127) / 128) * xslot_bytes_for(batch, x_dtype == HQB_F32 ? 2 : 1);
+}
+
+HQB_API int hqb_prepare_x(const void* x, int x_dtype, uint64_t cols, uint32_t batch, void* xfrag, void* stream) {
+  if (x == nullptr || xfrag == nullptr || hqb_xfrag_bytes(cols, batch, x_dtype) == 0 || cols > 0xFFFFFFFFull ||
+      (reinterpret_cast<uintptr_t>(xfrag) & 15u) != 0)
+    return HQB_ERR_INVALID;
+  const cudaError_t prior = take_prior_error();
+  if (prior != cudaSuccess) return prior;
+  return launch_prep(x, x_dtype, cols, batch, xfrag, as_stream(stream));
+}
+
+HQB_API uint64_t hqb_workspace_bytes(const hqb_plane_matrix* m, uint32_t batch, int x_dtype, int device) {
+  if (!plane_matrix_ok(m) || batch == 0 || batch > HQB_MAX_BATCH || (x_dtype != HQB_F16 && x_dtype != HQB_F32))
+    return 0;
+  const int sms = device_sm_count(device);
+  if (sms <= 0) return 0;
+  return ws_layout(m->grid_rows, m->grid_cols, batch, x_dtype == HQB_F32 ? 2 : 1, sms).total;
+}
+
+HQB_API int hqb_workspace_init(void* workspace, uint64_t bytes, void* stream) {
+  if (workspace == nullptr || bytes < 256) return HQB_ERR_INVALID;
+  return cudaMemsetAsync(workspace, 0, bytes, as_stream(stream));
+}
+
+HQB_API int hqb_workspace_error(const void* workspace, int* host_flags, void* stream) {
+  if (workspace == nullptr || host_flags == nullptr) return HQB_ERR_INVALID;
+  cudaError_t e = cudaMemcpyAsync(host_flags, workspace, sizeof(int), cudaMemcpyDeviceToHost, as_stream(stream));
+  if (e != cudaSuccess) return e;
+  return cudaStreamSynchronize(as_stream(stream));
+}
+
+HQB_API uint64_t hqb_depth_plan_bytes(uint32_t grid_rows) { return (static_cast<uint64_t>(grid_rows) + 1) * 4; }
+
+HQB_API int hqb_depth_plan(const uint8_t* depth, uint32_t grid_rows, uint32_t grid_cols, uint32_t stage_count,
+                           uint32_t* plan, int* device_flags, void* stream) {
+  if (depth == nullptr || plan == nullptr || grid_rows == 0 || grid_cols == 0 || stage_count == 0 ||
+      stage_count > HQB_MAX_STAGES || static_cast<uint64_t>(grid_rows) * grid_cols * HQB_MAX_STAGES > 0xFFFFFFFFull)
+    return HQB_ERR_INVALID;
+  const cudaError_t prior = take_prior_error();
+  if (prior != cudaSuccess) return prior;
+  depth_plan_kernel<<<1, 1024, 0, as_stream(stream)>>>(depth, grid_rows, grid_cols, stage_count, plan, device_flags);
+  return cudaGetLastError();
+}
+
+HQB_API int hqb_gemv_ex(const hqb_plane_matrix* m, uint32_t prefix, const uint8_t* depth, const uint32_t* depth_plan,
+                        const void* x, int x_dtype, uint32_t batch, int x_prepared, const void* bias, int bias_dtype,
+                        void* y, int y_dtype, void* workspace, uint64_t workspace_bytes, uint32_t flags,
+                        void* stream) {
+  if (!plane_matrix_ok(m) || x == nullptr || y == nullptr || workspace == nullptr) return HQB_ERR_INVALID;
+  if (batch == 0 || batch > HQB_MAX_BATCH) return HQB_ERR_INVALID;
+  if ((x_dtype != HQB_F16 && x_dtype != HQB_F32) || (y_dtype != HQB_F16 && y_dtype != HQB_F32)) return HQB_ERR_INVALID;
+  if (bias != nullptr && bias_dtype != HQB_F16 && bias_dtype != HQB_F32) return HQB_ERR_INVALID;
+  if ((depth == nullptr) != (depth_plan == nullptr)) return HQB_ERR_INVALID;
+  const bool mixed = depth != nullptr;
+  if (!mixed && prefix > m->stage_count) return HQB_ERR_INVALID;
+  const bool simt = (flags & HQB_FLAG_SIMT) != 0;
+  if (simt && (batch > 8 || x_dtype != HQB_F16)) return HQB_ERR_INVALID;
+  if (!stage_planes_ok(m, mixed ? m->stage_count : prefix)) return HQB_ERR_INVALID;
+  if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0) return HQB_ERR_INVALID;
+  if (x_prepared && (reinterpret_cast<uintptr_t>(x) & 15u) != 0) return HQB_ERR_INVALID;
+  int device = 0;
+  cudaError_t e = cudaGetDevice(&device);
+  if (e != cudaSuccess) return e;
+  const int sms = device_sm_count(device);
+  if (sms <= 0) return cudaErrorNoDevice;
+  const uint32_t xl = x_dtype == HQB_F32 ? 2 : 1;
+  const WsLayout L = ws_layout(m->grid_rows, m->grid_cols, batch, xl, sms);
+  if (workspace_bytes < L.total) return HQB_ERR_INVALID;
+  const cudaError_t prior = take_prior_error();
+  if (prior != cudaSuccess) return prior;
+  const cudaStream_t st = as_stream(stream);
+  if (!mixed && prefix == 0) {
+    const uint64_t n = m->rows * batch;
+    const unsigned blocks = static_cast<unsigned>(std::min<uint64_t>((n + 255) / 256, 4096));
+    fill_kernel<<<blocks, 256, 0, st>>>(bias, bias_dtype, y, y_dtype, static_cast<uint32_t>(m->rows), batch);
+    return cudaGetLastError();
+  }
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  const uint8_t* xfrag = static_cast<const uint8_t*>(x);
+  if (!x_prepared) {
+    e = launch_prep(x, x_dtype, m->cols, batch, ws + L.xfrag, st);
+    if (e != cudaSuccess) return e;
+    xfrag = ws + L.xfrag;
+  }
+  GemvParams p{};
+  for (uint32_t s = 0; s < HQB_MAX_STAGES; ++s) p.planes[s] = static_cast<const uint8_t*>(m->planes[s]);
+  p.depth = depth;
+  p.plan = depth_plan;
+  p.xfrag = xfrag;
+  p.bias = bias;
+  p.y = y;
+  p.error = reinterpret_cast<int*>(ws);
+  p.counters = reinterpret_cast<uint32_t*>(ws + L.counters);
+  p.partials = reinterpret_cast<float*>(ws + L.partials);
+  p.rows = static_cast<uint32_t>(m->rows);
+  p.R = m->grid_rows;
+  p.C = m->grid_cols;
+  p.prefix = mixed ? 0 : prefix;
+  p.stage_count = m->stage_count;
+  p.batch = batch;
+  p.xslot_bytes = xslot_bytes_for(batch, xl);
+  p.bias_dtype = bias_dtype;
+  p.y_dtype = y_dtype;
+  const uint64_t tiles = static_cast<uint64_t>(m->grid_rows) * m->grid_cols;
+  p.total = mixed ? 0 : tiles * prefix;
+  const GemvKernel k = pick_kernel(batch > 8 ? 2 : 1, xl, simt);
+  const uint32_t smem = gemv_smem_bytes(p.xslot_bytes);
+  const int per_sm = ctas_per_sm(k, smem, device);
+  if (per_sm <= 0) return cudaErrorLaunchOutOfResources;
+  uint64_t grid = static_cast<uint64_t>(sms) * per_sm;
+  const uint64_t units = mixed ? tiles : p.total;  // mixed: at least one unit per tile
+  grid = std::max<uint64_t>(1, std::min<uint64_t>(grid, units));
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(static_cast<unsigned>(grid));
+  cfg.blockDim = dim3(kGemvThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  if (flags & HQB_FLAG_PDL) {
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+  }
+  e = cudaLaunchKernelEx(&cfg, k, p);
+  if (e != cudaSuccess) return e;
+  return cudaGetLastError();
+}
+
+HQB_API int hqb_gemv(const hqb_plane_matrix* m, uint32_t prefix, const void* x, int x_dtype, uint32_t batch,
+                     const void* bias, int bias_dtype, void* y, int y_dtype, void* workspace, uint64_t workspace_bytes,
+                     void* stream) {
+  return hqb_gemv_ex(m, prefix, nullptr, nullptr, x, x_dtype, batch, 0, bias, bias_dtype, y, y_dtype, workspace,
+                     workspace_bytes, 0, stream);
+}
+
+HQB_API int hqb_gemv_mixed(const hqb_plane_matrix* m, const uint8_t* depth, const uint32_t* depth_plan, const void* x,
+                           int x_dtype, uint32_t batch, const void* bias, int bias_dtype, void* y, int y_dtype,
+                           void* workspace, uint64_t workspace_bytes, void* stream) {
+  if (depth == nullptr || depth_plan == nullptr) return HQB_ERR_INVALID;
+  return hqb_gemv_ex(m, 0, depth, depth_plan, x, x_dtype, batch, 0, bias, bias_dtype, y, y_dtype, workspace,
+                     workspace_bytes, 0, stream);
+}
+
+HQB_API int hqb_decode_planes(const hqb_plane_matrix* m, uint32_t prefix, const uint8_t* depth, float* out,
+                              uint64_t out_count, void* stream) {
+  if (!plane_matrix_ok(m) || out == nullptr || out_count != m->rows * m->cols) return HQB_ERR_INVALID;
+  if (depth == nullptr && prefix > m->stage_count) return HQB_ERR_INVALID;
+  if (!stage_planes_ok(m, depth != nullptr ? m->stage_count : prefix)) return HQB_ERR_INVALID;
+  const cudaError_t prior = take_prior_error();
+  if (prior != cudaSuccess) return prior;
+  decode_kernel<<<m->grid_rows * m->grid_cols, 256, 0, as_stream(stream)>>>(*m, prefix, depth, out);
+  return cudaGetLastError();
+}
+
+}  // extern "C"

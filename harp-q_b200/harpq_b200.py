@@ -1,0 +1,317 @@
+"""Python binding of the C ABI in include/harpq_b200.h (ctypes over libharpq_b200.so).
+
+Device memory is held in torch tensors (allocation, streams and events only); every
+computation runs in the library's sm_100a kernels.  There is no fallback: importing
+this module without the built library, or calling it without a CUDA device, raises.
+
+    import harpq_b200 as hqb
+    m = hqb.PlaneMatrix.from_stages(rows, cols, codes, fp16_scale_bits)  # repack on device
+    y = m.gemv(x, prefix=2)                        # x: [batch, cols] FP16/FP32 CUDA tensor
+    w = m.decode(prefix=2)                         # dense FP32, bit-exact decode
+"""
+
+from __future__ import annotations
+
+import ctypes
+from pathlib import Path
+from typing import Sequence
+
+import torch
+
+PKG = Path(__file__).resolve().parent
+LIB_PATH = PKG / "lib" / "libharpq_b200.so"
+
+F32, F16 = 0, 1
+FLAG_PDL, FLAG_SIMT = 1, 2
+TILE = 128
+RECORD_BYTES = 4352
+MAX_STAGES = 4
+MAX_BATCH = 16
+DEVERR_SCALE, DEVERR_DEPTH, DEVERR_TIMEOUT = 1, 2, 4
+
+u64, u32, i32, vp = ctypes.c_uint64, ctypes.c_uint32, ctypes.c_int, ctypes.c_void_p
+
+
+class Geometry(ctypes.Structure):
+    _fields_ = [(n, u64) for n in ("original_rows", "original_columns", "padded_rows", "padded_columns",
+                                   "tile_rows", "tile_columns", "group_size")]
+
+
+class RawStage(ctypes.Structure):
+    _fields_ = [("packed_codes", vp), ("packed_code_bytes", u64), ("scale_fp16_bits", vp), ("scale_count", u64)]
+
+
+class RawStageF32(ctypes.Structure):
+    _fields_ = [("packed_codes", vp), ("packed_code_bytes", u64), ("scales", vp), ("scale_count", u64)]
+
+
+class PlaneMatrixC(ctypes.Structure):
+    _fields_ = [("rows", u64), ("cols", u64), ("grid_rows", u32), ("grid_cols", u32), ("stage_count", u32),
+                ("reserved", u32), ("planes", vp * MAX_STAGES)]
+
+
+EXPORTS = {
+    "hqb_version": (i32, []),
+    "hqb_status_string": (ctypes.c_char_p, [i32]),
+    "hqb_plane_bytes": (u64, [ctypes.POINTER(Geometry)]),
+    "hqb_repack_stage": (i32, [ctypes.POINTER(Geometry), ctypes.POINTER(RawStage), vp, vp, vp]),
+    "hqb_xfrag_bytes": (u64, [u64, u32, i32]),
+    "hqb_prepare_x": (i32, [vp, i32, u64, u32, vp, vp]),
+    "hqb_workspace_bytes": (u64, [ctypes.POINTER(PlaneMatrixC), u32, i32, i32]),
+    "hqb_workspace_init": (i32, [vp, u64, vp]),
+    "hqb_workspace_error": (i32, [vp, ctypes.POINTER(i32), vp]),
+    "hqb_depth_plan_bytes": (u64, [u32]),
+    "hqb_depth_plan": (i32, [vp, u32, u32, u32, vp, vp, vp]),
+    "hqb_gemv": (i32, [ctypes.POINTER(PlaneMatrixC), u32, vp, i32, u32, vp, i32, vp, i32, vp, u64, vp]),
+    "hqb_gemv_mixed": (i32, [ctypes.POINTER(PlaneMatrixC), vp, vp, vp, i32, u32, vp, i32, vp, i32, vp, u64, vp]),
+    "hqb_gemv_ex": (i32, [ctypes.POINTER(PlaneMatrixC), u32, vp, vp, vp, i32, u32, i32, vp, i32, vp, i32, vp, u64,
+                          u32, vp]),
+    "hqb_decode_planes": (i32, [ctypes.POINTER(PlaneMatrixC), u32, vp, vp, u64, vp]),
+    "hqb_raw_gemv": (i32, [ctypes.POINTER(Geometry), ctypes.POINTER(RawStage), u32, u32, vp, u64, vp, u64, vp, u64,
+                           vp]),
+    "hqb_raw_dequantize_stage": (i32, [ctypes.POINTER(Geometry), ctypes.POINTER(RawStageF32), u32, u32, vp, vp]),
+    "hqb_raw_dequantize_prefix": (i32, [ctypes.POINTER(Geometry), ctypes.POINTER(RawStageF32), u32, u32, vp, vp]),
+    "hqb_raw_linear_ordered": (i32, [ctypes.POINTER(Geometry), ctypes.POINTER(RawStageF32), u32, u32, vp, u64, vp,
+                                     vp, vp]),
+}
+
+_lib = None
+
+
+class HQBError(RuntimeError):
+    def __init__(self, status: int, what: str):
+        msg = lib().hqb_status_string(status).decode() if _lib is not None else str(status)
+        super().__init__(f"{what}: status {status} ({msg})")
+        self.status = status
+
+
+def lib() -> ctypes.CDLL:
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            raise ImportError(f"{LIB_PATH} is missing: build it with __graft_entry__.build()")
+        L = ctypes.CDLL(str(LIB_PATH))
+        for name, (res, args) in EXPORTS.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = L
+    return _lib
+
+
+def check(status: int, what: str) -> None:
+    if status != 0:
+        raise HQBError(status, what)
+
+
+def _stream(stream) -> int | None:
+    if stream is None:
+        return torch.cuda.current_stream().cuda_stream
+    return stream.cuda_stream if hasattr(stream, "cuda_stream") else stream
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _dtype_code(t: torch.Tensor) -> int:
+    if t.dtype == torch.float16:
+        return F16
+    if t.dtype == torch.float32:
+        return F32
+    raise TypeError(f"unsupported dtype {t.dtype}; use float16 or float32")
+
+
+def geometry(rows: int, cols: int, tile: Sequence[int] = (TILE, TILE), group: int = TILE) -> Geometry:
+    pr = -(-rows // tile[0]) * tile[0]
+    pc = -(-cols // tile[1]) * tile[1]
+    return Geometry(rows, cols, pr, pc, tile[0], tile[1], group)
+
+
+def plane_bytes(g: Geometry) -> int:
+    return lib().hqb_plane_bytes(ctypes.byref(g))
+
+
+def xfrag_bytes(cols: int, batch: int, x_dtype: int) -> int:
+    return lib().hqb_xfrag_bytes(cols, batch, x_dtype)
+
+
+def prepare_x(x: torch.Tensor, out: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+    """Prepared activations for hqb_gemv_ex(x_prepared=1); shareable across matrices."""
+    x = x.contiguous()
+    batch, cols = x.shape
+    n = xfrag_bytes(cols, batch, _dtype_code(x))
+    if n == 0:
+        raise ValueError("invalid activation shape/dtype")
+    if out is None:
+        out = torch.empty(n, dtype=torch.uint8, device=x.device)
+    check(lib().hqb_prepare_x(_ptr(x), _dtype_code(x), cols, batch, _ptr(out), _stream(stream)), "hqb_prepare_x")
+    return out
+
+
+class Workspace:
+    """Caller-owned scratch for GEMV launches (cleared once at allocation)."""
+
+    def __init__(self, nbytes: int, device=None, stream=None):
+        self.buf = torch.zeros(max(256, nbytes), dtype=torch.uint8, device=device or "cuda")
+        self.nbytes = self.buf.numel()
+
+    def ptr(self) -> int:
+        return self.buf.data_ptr()
+
+    def error_flags(self, stream=None) -> int:
+        out = ctypes.c_int(0)
+        check(lib().hqb_workspace_error(self.ptr(), ctypes.byref(out), _stream(stream)), "hqb_workspace_error")
+        return out.value
+
+    def reset(self, stream=None) -> None:
+        check(lib().hqb_workspace_init(self.ptr(), self.nbytes, _stream(stream)), "hqb_workspace_init")
+
+
+class DepthPlan:
+    """Per-tile depth map (uint8 [grid_rows, grid_cols]) and its device schedule."""
+
+    def __init__(self, depth: torch.Tensor, stage_count: int, stream=None):
+        if depth.dtype != torch.uint8 or depth.dim() != 2:
+            raise TypeError("depth must be a uint8 [grid_rows, grid_cols] tensor")
+        self.depth = depth.contiguous()
+        self.grid_rows, self.grid_cols = self.depth.shape
+        self.plan = torch.empty(self.grid_rows + 1, dtype=torch.int32, device=depth.device)
+        self.flags = torch.zeros(1, dtype=torch.int32, device=depth.device)
+        check(lib().hqb_depth_plan(_ptr(self.depth), self.grid_rows, self.grid_cols, stage_count, _ptr(self.plan),
+                                   _ptr(self.flags), _stream(stream)), "hqb_depth_plan")
+
+
+class PlaneMatrix:
+    """A device-resident progressive matrix in the plane layout (one buffer per stage)."""
+
+    def __init__(self, rows: int, cols: int, device=None):
+        self.rows, self.cols = rows, cols
+        self.geom = geometry(rows, cols)
+        self.grid_rows, self.grid_cols = -(-rows // TILE), -(-cols // TILE)
+        self.device = torch.device(device or "cuda")
+        self.planes: list[torch.Tensor] = []
+        self.repack_flags = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self._ws: dict = {}
+
+    @property
+    def stage_count(self) -> int:
+        return len(self.planes)
+
+    def add_stage(self, codes: torch.Tensor, fp16_scale_bits: torch.Tensor, stream=None) -> None:
+        """Repack one newly resident stage (reference layout, on device) into a new plane."""
+        if self.stage_count >= MAX_STAGES:
+            raise ValueError("a progressive matrix holds at most four stages")
+        codes = codes.contiguous()
+        bits = fp16_scale_bits.contiguous()
+        plane = torch.empty(plane_bytes(self.geom), dtype=torch.uint8, device=self.device)
+        st = RawStage(codes.data_ptr(), codes.numel(), bits.data_ptr(), bits.numel())
+        check(lib().hqb_repack_stage(ctypes.byref(self.geom), ctypes.byref(st), _ptr(plane), _ptr(self.repack_flags),
+                                     _stream(stream)), "hqb_repack_stage")
+        self.planes.append(plane)
+
+    @classmethod
+    def from_stages(cls, rows: int, cols: int, codes: Sequence[torch.Tensor], fp16_scale_bits: Sequence[torch.Tensor],
+                    stream=None) -> "PlaneMatrix":
+        m = cls(rows, cols, device=codes[0].device)
+        for c, s in zip(codes, fp16_scale_bits):
+            m.add_stage(c, s, stream)
+        return m
+
+    def c_struct(self) -> PlaneMatrixC:
+        arr = (vp * MAX_STAGES)(*[p.data_ptr() for p in self.planes], *([None] * (MAX_STAGES - len(self.planes))))
+        return PlaneMatrixC(self.rows, self.cols, self.grid_rows, self.grid_cols, self.stage_count, 0, arr)
+
+    def workspace_bytes(self, batch: int, x_dtype: int = F16) -> int:
+        dev = self.device.index if self.device.index is not None else torch.cuda.current_device()
+        return lib().hqb_workspace_bytes(ctypes.byref(self.c_struct()), batch, x_dtype, dev)
+
+    def workspace(self, batch: int, x_dtype: int = F16) -> Workspace:
+        key = (batch, x_dtype)
+        if key not in self._ws:
+            self._ws[key] = Workspace(self.workspace_bytes(batch, x_dtype), self.device)
+        return self._ws[key]
+
+    def gemv(self, x: torch.Tensor, prefix: int | None = None, bias: torch.Tensor | None = None,
+             out: torch.Tensor | None = None, y_dtype=torch.float16, depth: DepthPlan | None = None,
+             workspace: Workspace | None = None, x_prepared: torch.Tensor | None = None, flags: int = 0,
+             stream=None) -> torch.Tensor:
+        """y[b, r] = Σ_c x[b, c]·W[r, c] (+ bias) at a uniform prefix or a depth map."""
+        if x.dim() == 1:
+            x = x.unsqueeze(0)
+        x = x.contiguous()
+        batch = x.shape[0]
+        if x.shape[1] != self.cols:
+            raise ValueError("x has the wrong number of columns")
+        xd = _dtype_code(x)
+        if out is None:
+            out = torch.empty(batch, self.rows, dtype=y_dtype, device=self.device)
+        ws = workspace or self.workspace(batch, xd)
+        prefix = self.stage_count if prefix is None else prefix
+        src = x if x_prepared is None else x_prepared
+        status = lib().hqb_gemv_ex(ctypes.byref(self.c_struct()), prefix, None if depth is None else _ptr(depth.depth),
+                                   None if depth is None else _ptr(depth.plan), _ptr(src), xd, batch,
+                                   0 if x_prepared is None else 1, _ptr(bias),
+                                   F32 if bias is None else _dtype_code(bias), _ptr(out), _dtype_code(out), ws.ptr(),
+                                   ws.nbytes, flags, _stream(stream))
+        check(status, "hqb_gemv_ex")
+        return out
+
+    def decode(self, prefix: int | None = None, depth: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+        out = torch.empty(self.rows, self.cols, dtype=torch.float32, device=self.device)
+        prefix = self.stage_count if prefix is None else prefix
+        check(lib().hqb_decode_planes(ctypes.byref(self.c_struct()), prefix, _ptr(depth), _ptr(out), out.numel(),
+                                      _stream(stream)), "hqb_decode_planes")
+        return out
+
+
+class RawMatrix:
+    """Stages in the reference's own device layout (any tile geometry)."""
+
+    def __init__(self, geom: Geometry, codes: Sequence[torch.Tensor], fp16_scale_bits: Sequence[torch.Tensor] = (),
+                 scales_f32: Sequence[torch.Tensor] = ()):
+        self.geom = geom
+        self.codes = [c.contiguous() for c in codes]
+        self.bits = [b.contiguous() for b in fp16_scale_bits]
+        self.f32 = [s.contiguous() for s in scales_f32]
+
+    def _stages(self):
+        arr = (RawStage * MAX_STAGES)()
+        for i, (c, b) in enumerate(zip(self.codes, self.bits)):
+            arr[i] = RawStage(c.data_ptr(), c.numel(), b.data_ptr(), b.numel())
+        return arr
+
+    def _stages_f32(self):
+        arr = (RawStageF32 * MAX_STAGES)()
+        for i, (c, s) in enumerate(zip(self.codes, self.f32)):
+            arr[i] = RawStageF32(c.data_ptr(), c.numel(), s.data_ptr(), s.numel())
+        return arr
+
+    def gemv(self, x: torch.Tensor, prefix: int, bias: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+        y = torch.empty(self.geom.original_rows, dtype=torch.float32, device=x.device)
+        check(lib().hqb_raw_gemv(ctypes.byref(self.geom), self._stages(), len(self.codes), prefix, _ptr(x), x.numel(),
+                                 _ptr(bias), 0 if bias is None else bias.numel(), _ptr(y), y.numel(), _stream(stream)),
+              "hqb_raw_gemv")
+        return y
+
+    def dequantize_prefix(self, prefix: int, stream=None) -> torch.Tensor:
+        out = torch.empty(self.geom.original_rows, self.geom.original_columns, dtype=torch.float32,
+                          device=self.codes[0].device)
+        check(lib().hqb_raw_dequantize_prefix(ctypes.byref(self.geom), self._stages_f32(), len(self.codes), prefix,
+                                              _ptr(out), _stream(stream)), "hqb_raw_dequantize_prefix")
+        return out
+
+    def dequantize_stage(self, stage: int, stream=None) -> torch.Tensor:
+        out = torch.empty(self.geom.original_rows, self.geom.original_columns, dtype=torch.float32,
+                          device=self.codes[0].device)
+        check(lib().hqb_raw_dequantize_stage(ctypes.byref(self.geom), self._stages_f32(), len(self.codes), stage,
+                                             _ptr(out), _stream(stream)), "hqb_raw_dequantize_stage")
+        return out
+
+    def linear_ordered(self, x: torch.Tensor, prefix: int, bias: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+        x = x.contiguous().reshape(-1, self.geom.original_columns)
+        y = torch.empty(x.shape[0], self.geom.original_rows, dtype=torch.float32, device=x.device)
+        check(lib().hqb_raw_linear_ordered(ctypes.byref(self.geom), self._stages_f32(), len(self.codes), prefix,
+                                           _ptr(x), x.shape[0], _ptr(bias), _ptr(y), _stream(stream)),
+              "hqb_raw_linear_ordered")
+        return y

@@ -1,0 +1,232 @@
+/*
+ * harpq_b200.h — C ABI of the B200-native progressive int2 GEMV library.
+ *
+ * The path: y = x · Wᵀ (+ bias) where W (rows x cols, "out_features x in_features")
+ * is stored as up to four signed-int2 residual stages over 128x128 tiles with one
+ * FP16 scale per (row, tile, stage), evaluated at a caller-selected prefix depth or
+ * a per-tile depth map, without materialising FP16/FP32 weights.
+ *
+ * Every entry point takes plain pointers and sizes.  Device pointers are CUDA device
+ * addresses; `stream` is a cudaStream_t (NULL = legacy default stream).  Status values
+ * are cudaError_t codes: 0 success, 1 (cudaErrorInvalidValue) for any rejected argument
+ * (nothing is enqueued), 801 (cudaErrorNotSupported) for a geometry the fast path does
+ * not cover, otherwise the CUDA error of the failing call.  A sticky CUDA error that is
+ * pending before a launch is returned without launching (reference behaviour,
+ * native/src/progressive_gemv.cu:427-433).  The caller owns every buffer, the stream
+ * ordering and completion, as in the reference (native/include/harpq/progressive_gemv.hpp:49-57).
+ *
+ * Reference interfaces each group replaces are cited per declaration.
+ */
+#ifndef HARPQ_B200_H_
+#define HARPQ_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define HQB_API __attribute__((visibility("default")))
+#else
+#define HQB_API
+#endif
+
+#define HQB_OK 0
+#define HQB_ERR_INVALID 1
+#define HQB_ERR_UNSUPPORTED 801
+
+/* element types of activations, bias and outputs */
+#define HQB_F32 0
+#define HQB_F16 1
+
+/* hqb_gemv_ex flags */
+#define HQB_FLAG_PDL 1u  /* launch with programmatic dependent launch (see hqb_gemv_ex) */
+#define HQB_FLAG_SIMT 2u /* CUDA-core decode+FFMA consumer instead of tensor-core mma */
+
+/* Fast-path tiling: 128x128 tiles, one scale group per tile row (group 128). */
+#define HQB_TILE 128
+/* One stage of one tile in the plane layout: 8 row-blocks x (512 B codes + 32 B scales). */
+#define HQB_TILE_RECORD_BYTES 4352
+#define HQB_MAX_STAGES 4
+#define HQB_MAX_BATCH 16
+
+/* Device-error bits reported through the int flag words below. */
+#define HQB_DEVERR_SCALE 1        /* a non-finite or negative FP16 scale was repacked   */
+#define HQB_DEVERR_DEPTH 2        /* a depth-map entry outside [1, stage_count]          */
+#define HQB_DEVERR_TIMEOUT 4      /* a pipeline wait exceeded its bound (kernel returned) */
+
+/* Matrix geometry, same fields and order as ProgressiveGemvGeometry
+ * (reference native/include/harpq/progressive_gemv.hpp:15-23). */
+typedef struct hqb_geometry {
+  uint64_t original_rows;
+  uint64_t original_columns;
+  uint64_t padded_rows;
+  uint64_t padded_columns;
+  uint64_t tile_rows;
+  uint64_t tile_columns;
+  uint64_t group_size;
+} hqb_geometry;
+
+/* One stage in the reference's device layout: row-major packed codes over the padded
+ * matrix (4 codes/byte, LSB first) and raw FP16 scale bits in
+ * [tile_row][tile_col][row_in_tile][group] order.  Same fields as
+ * ProgressiveGemvStageDeviceView (progressive_gemv.hpp:27-32). */
+typedef struct hqb_raw_stage {
+  const uint8_t* packed_codes;
+  uint64_t packed_code_bytes;
+  const uint16_t* scale_fp16_bits;
+  uint64_t scale_count;
+} hqb_raw_stage;
+
+/* Same stage with host-decoded FP32 scales, as DecodedStage carries them
+ * (native/include/harpq/native/stage_codec.hpp:26-31); used by the decode and
+ * reference-order entry points that must accept any finite non-negative scale. */
+typedef struct hqb_raw_stage_f32 {
+  const uint8_t* packed_codes;
+  uint64_t packed_code_bytes;
+  const float* scales;
+  uint64_t scale_count;
+} hqb_raw_stage_f32;
+
+/* A device-resident matrix in the plane layout: planes[s] holds stage s as
+ * grid_rows*grid_cols tile records (row-major over tiles) of HQB_TILE_RECORD_BYTES.
+ * Stages are independent buffers, so a newly resident residual stage is one more
+ * plane (hqb_repack_stage) without touching the others. */
+typedef struct hqb_plane_matrix {
+  uint64_t rows;        /* original rows (output features)  */
+  uint64_t cols;        /* original columns (input features) */
+  uint32_t grid_rows;   /* ceil(rows / 128) */
+  uint32_t grid_cols;   /* ceil(cols / 128) */
+  uint32_t stage_count; /* planes[0..stage_count) are valid */
+  uint32_t reserved;
+  const void* planes[HQB_MAX_STAGES];
+} hqb_plane_matrix;
+
+HQB_API int hqb_version(void);
+HQB_API const char* hqb_status_string(int status);
+
+/* ---- plane layout ---------------------------------------------------------------- */
+
+/* Bytes of one stage plane for geometry g; 0 when g is not 128x128 tiles with group
+ * 128 (such matrices run only through hqb_raw_gemv). */
+HQB_API uint64_t hqb_plane_bytes(const hqb_geometry* g);
+
+/* Device repack of one reference-layout stage into one plane (16-byte slots in
+ * mma-fragment order, codes of padded columns cleared, FP16 scale pairs per row
+ * block).  device_flags (optional, device int) gets HQB_DEVERR_SCALE OR-ed in when a
+ * scale is NaN/Inf/negative — the checks of DecodeStagePayload
+ * (native/src/stage_codec.cpp:205-213), done on the device.  Replaces the reference's
+ * per-call use of the row-major layout (native/src/progressive_gemv.cu:359-392). */
+HQB_API int hqb_repack_stage(const hqb_geometry* g, const hqb_raw_stage* stage, void* plane,
+                             int* device_flags, void* stream);
+
+/* ---- activations ----------------------------------------------------------------- */
+
+/* Bytes of the prepared-activation buffer for `batch` rows of `cols` inputs. */
+HQB_API uint64_t hqb_xfrag_bytes(uint64_t cols, uint32_t batch, int x_dtype);
+
+/* Converts x [batch][cols] (FP16 or FP32, row-major) into per-tile tensor-core
+ * B fragments plus per-tile correction sums.  One prepared buffer serves every
+ * matrix with the same `cols` (e.g. q/k/v).  No reference counterpart (the reference
+ * reads FP32 x directly, progressive_gemv.cu:392). */
+HQB_API int hqb_prepare_x(const void* x, int x_dtype, uint64_t cols, uint32_t batch,
+                          void* xfrag, void* stream);
+
+/* ---- workspace ------------------------------------------------------------------- */
+
+/* Scratch bytes a GEMV on m with this batch needs on `device`: an error word, per
+ * row-block arrival counters, split-row partial sums and a prepared-activation area. */
+HQB_API uint64_t hqb_workspace_bytes(const hqb_plane_matrix* m, uint32_t batch, int x_dtype,
+                                     int device);
+/* Clears a workspace (required once after allocation and after any reported device
+ * error).  GEMVs leave it cleared for the next call. */
+HQB_API int hqb_workspace_init(void* workspace, uint64_t bytes, void* stream);
+/* Copies the workspace error word (HQB_DEVERR_* bits) to *host_flags, synchronously. */
+HQB_API int hqb_workspace_error(const void* workspace, int* host_flags, void* stream);
+
+/* ---- mixed depth ------------------------------------------------------------------ */
+
+/* Bytes of the schedule a depth map needs: (grid_rows + 1) uint32 row-cost prefix sums. */
+HQB_API uint64_t hqb_depth_plan_bytes(uint32_t grid_rows);
+/* Builds the schedule for a device depth map [grid_rows][grid_cols] (uint8, values in
+ * [1, stage_count]); bad entries set HQB_DEVERR_DEPTH in device_flags and are clamped.
+ * No reference symbol: the reference selects one prefix per matrix
+ * (progressive_gemv.hpp:58-62); its allocator emits per-group prefixes
+ * (src/harpq/allocator.py:1-9). */
+HQB_API int hqb_depth_plan(const uint8_t* depth, uint32_t grid_rows, uint32_t grid_cols,
+                           uint32_t stage_count, uint32_t* plan, int* device_flags,
+                           void* stream);
+
+/* ---- GEMV ----------------------------------------------------------------------- */
+
+/* y[b][r] = Σ_c x[b][c]·W_prefix[r][c] (+ bias[r]) for b < batch (1..16), FP32
+ * accumulation, y FP16 or FP32 [batch][rows].  Replaces LaunchProgressiveGemv
+ * (progressive_gemv.hpp:58-62, progressive_gemv.cu:420-439) for plane matrices and
+ * extends it to batch 2-16.  prefix 0 writes bias or exact zeros.  x is raw
+ * [batch][cols]; it is prepared into the workspace first. */
+HQB_API int hqb_gemv(const hqb_plane_matrix* m, uint32_t prefix, const void* x, int x_dtype,
+                     uint32_t batch, const void* bias, int bias_dtype, void* y, int y_dtype,
+                     void* workspace, uint64_t workspace_bytes, void* stream);
+
+/* Same with a per-tile depth map and its plan (hqb_depth_plan). */
+HQB_API int hqb_gemv_mixed(const hqb_plane_matrix* m, const uint8_t* depth,
+                           const uint32_t* depth_plan, const void* x, int x_dtype,
+                           uint32_t batch, const void* bias, int bias_dtype, void* y,
+                           int y_dtype, void* workspace, uint64_t workspace_bytes,
+                           void* stream);
+
+/* General form.  depth/depth_plan NULL selects the uniform prefix.  x_prepared != 0
+ * means x is a buffer filled by hqb_prepare_x (x_dtype as given to it).
+ * HQB_FLAG_PDL launches the GEMV as a programmatic dependent of the previous kernel
+ * in the stream: it prefetches weight planes before waiting for that kernel, so that
+ * kernel must not write the planes (a preceding hqb_prepare_x or GEMV is fine).
+ * HQB_FLAG_SIMT selects the CUDA-core comparison kernel (batch <= 8, FP16 x). */
+HQB_API int hqb_gemv_ex(const hqb_plane_matrix* m, uint32_t prefix, const uint8_t* depth,
+                        const uint32_t* depth_plan, const void* x, int x_dtype,
+                        uint32_t batch, int x_prepared, const void* bias, int bias_dtype,
+                        void* y, int y_dtype, void* workspace, uint64_t workspace_bytes,
+                        uint32_t flags, void* stream);
+
+/* Dense FP32 weights [rows][cols] decoded from planes, Σ_{s<d} code·scale summed in
+ * stage order from 0.0f — bit-identical to DequantizePrefix
+ * (native/src/stage_codec.cpp:254-272).  depth NULL: uniform prefix. */
+HQB_API int hqb_decode_planes(const hqb_plane_matrix* m, uint32_t prefix, const uint8_t* depth,
+                              float* out, uint64_t out_count, void* stream);
+
+/* ---- reference-layout (drop-in) entry points --------------------------------------- */
+
+/* LaunchProgressiveGemv semantics on the reference's own device layout, any tile
+ * geometry, FP32 x/bias/y, batch 1 (native/include/harpq/progressive_gemv.hpp:49-62,
+ * native/src/progressive_gemv.cu:266-321 validation, :420-439 launch).  stages[] has
+ * stage_count entries; entries < prefix must be valid. */
+HQB_API int hqb_raw_gemv(const hqb_geometry* g, const hqb_raw_stage* stages, uint32_t stage_count,
+                         uint32_t prefix, const float* x, uint64_t x_count, const float* bias,
+                         uint64_t bias_count, float* y, uint64_t y_count, void* stream);
+
+/* out[rows][cols] = code·scale of one stage, the exact FP32 product
+ * (DequantizeStage, native/src/stage_codec.cpp:218-252).  Scales are FP32. */
+HQB_API int hqb_raw_dequantize_stage(const hqb_geometry* g, const hqb_raw_stage_f32* stages,
+                                     uint32_t stage_count, uint32_t stage, float* out,
+                                     void* stream);
+
+/* out[rows][cols] = Σ_{s<prefix} code·scale added in stage order into 0.0f
+ * (DequantizePrefix, native/src/stage_codec.cpp:254-272).  Scales are FP32. */
+HQB_API int hqb_raw_dequantize_prefix(const hqb_geometry* g, const hqb_raw_stage_f32* stages,
+                                      uint32_t stage_count, uint32_t prefix, float* out,
+                                      void* stream);
+
+/* ProgressiveLinearReference's exact scalar order on the device: per stage a fresh
+ * FP32 dot per (batch,row) over columns, stage-major, bias last, every multiply and
+ * add rounded separately (native/src/stage_codec.cpp:274-326).  Bit-identical to the
+ * reference's CPU result. */
+HQB_API int hqb_raw_linear_ordered(const hqb_geometry* g, const hqb_raw_stage_f32* stages,
+                                   uint32_t stage_count, uint32_t prefix, const float* x,
+                                   uint64_t batch, const float* bias, float* y, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* HARPQ_B200_H_ */

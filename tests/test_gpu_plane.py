@@ -1,0 +1,251 @@
+"""GPU parity of the plane-layout path (repack, bit-exact decode, tensor-core GEMV).
+
+Every case is checked against the CPU oracle on the same seeded inputs:
+* decode: bit-identical to the oracle's DequantizePrefix restatement;
+* GEMV, FP32 outputs: |a - e| <= 2e-4 + 2e-4*|e| against the oracle's scalar-order
+  ProgressiveLinearReference (the reference's fused-GEMV contract,
+  native/tests/progressive_gemv_test.cu:36-37, docs/DECISIONS.md D-019), and
+  rel-L2 <= 1e-3 against an FP64 materialize-then-matvec of the exact decoded weights;
+* GEMV, FP16 outputs: |a - e| <= 2e-4 + 2^-10*|e| against that FP64 result (one FP16
+  rounding of the output on top of the FP32 contract), rel-L2 <= 1e-3.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+from conftest import (SEEDED_NAMES, assert_close, load_seeded, plane_matrix, random_matrix,  # noqa: E402
+                      rel_l2)
+from oracle import oracle as orc  # noqa: E402
+
+FP16_RTOL = 2.0 ** -10
+
+
+def _fp64_reference(m, x, prefix, bias=None, depth=None):
+    w = orc.dequantize_prefix_np(m, prefix, depth=depth).astype(np.float64)
+    y = np.asarray(x, np.float64).reshape(-1, m.cols) @ w.T
+    if bias is not None:
+        y = y + np.asarray(bias, np.float64)[None, :]
+    return y
+
+
+@pytest.mark.parametrize("name", SEEDED_NAMES)
+def test_plane_decode_bit_exact(name):
+    m, _, _ = load_seeded(name)
+    pm = plane_matrix(m)
+    for p in range(5):
+        got = pm.decode(p).cpu().numpy()
+        assert got.tobytes() == orc.dequantize_prefix(m, p).tobytes(), f"prefix {p}"
+    assert int(pm.repack_flags.item()) == 0
+
+
+@pytest.mark.parametrize("name", SEEDED_NAMES)
+@pytest.mark.parametrize("y_dtype", ["f32", "f16"])
+def test_gemv_seeded_against_oracle(name, y_dtype):
+    m, _, z = load_seeded(name)
+    pm = plane_matrix(m)
+    x = z["x"]  # FP16-exact activations, [batch, cols]
+    bias = z["bias"]
+    xt = torch.from_numpy(x).cuda().half()
+    bt = torch.from_numpy(bias).cuda()
+    ydt = torch.float32 if y_dtype == "f32" else torch.float16
+    for p in range(5):
+        y = pm.gemv(xt, prefix=p, bias=bt, y_dtype=ydt).float().cpu().numpy()
+        e64 = _fp64_reference(m, x, p, bias)
+        if y_dtype == "f32":
+            scalar = orc.linear_reference(m, x, p, bias)
+            assert_close(y, scalar, 2e-4, 2e-4, f"{name} p{p} vs scalar oracle")
+        else:
+            assert_close(y, e64, 2e-4, FP16_RTOL, f"{name} p{p} f16")
+        assert rel_l2(y, e64) <= 1e-3
+
+
+@pytest.mark.parametrize("batch", [1, 2, 5, 8, 9, 16])
+@pytest.mark.parametrize("x_dtype", ["f16", "f32"])
+def test_gemv_batches_and_dtypes(batch, x_dtype):
+    rng = np.random.default_rng(100 + batch)
+    m = random_matrix(rng, 300, 520)
+    pm = plane_matrix(m)
+    x = rng.standard_normal((batch, m.cols)).astype(np.float32) * 3
+    if x_dtype == "f16":
+        x = x.astype(np.float16).astype(np.float32)
+    xt = torch.from_numpy(x).cuda()
+    xt = xt.half() if x_dtype == "f16" else xt
+    bias = rng.standard_normal(m.rows).astype(np.float32)
+    bt = torch.from_numpy(bias).cuda().half()
+    for p in (1, 2, 3, 4):
+        y = pm.gemv(xt, prefix=p, bias=bt, y_dtype=torch.float32).cpu().numpy()
+        e64 = _fp64_reference(m, x, p, bias.astype(np.float16).astype(np.float32))
+        assert_close(y, e64, 2e-4, 2e-4, f"b{batch} {x_dtype} p{p}")
+        assert rel_l2(y, e64) <= 1e-3
+
+
+def test_fp32_activations_wide_dynamic_range():
+    """FP32 x spanning 1e-6..1e6 goes through the hi/lo split with a per-tile exponent."""
+    rng = np.random.default_rng(7)
+    m = random_matrix(rng, 256, 384)
+    pm = plane_matrix(m)
+    mag = 10.0 ** rng.uniform(-6, 6, size=(2, m.cols))
+    x = (np.sign(rng.standard_normal((2, m.cols))) * mag).astype(np.float32)
+    y = pm.gemv(torch.from_numpy(x).cuda(), prefix=4, y_dtype=torch.float32).cpu().numpy()
+    e64 = _fp64_reference(m, x, 4)
+    assert rel_l2(y, e64) <= 1e-5
+
+
+def test_prefix_zero_writes_bias_or_zeros():
+    rng = np.random.default_rng(1)
+    m = random_matrix(rng, 200, 130)
+    pm = plane_matrix(m)
+    x = torch.randn(3, m.cols, device="cuda").half()
+    y = pm.gemv(x, prefix=0, y_dtype=torch.float32)
+    assert torch.count_nonzero(y).item() == 0
+    bias = torch.randn(m.rows, device="cuda")
+    y = pm.gemv(x, prefix=0, bias=bias, y_dtype=torch.float32)
+    assert torch.equal(y, bias.expand(3, -1))
+
+
+def test_split_rows_deterministic_and_workspace_left_clean():
+    """Many split tile rows (stream-K fix-up) give identical bytes run to run."""
+    rng = np.random.default_rng(11)
+    m = random_matrix(rng, 1000, 3000)
+    pm = plane_matrix(m)
+    x = torch.from_numpy(rng.standard_normal((4, m.cols)).astype(np.float16)).cuda()
+    ws = pm.workspace(4)
+    outs = [pm.gemv(x, prefix=p, y_dtype=torch.float32, workspace=ws).cpu().numpy() for p in (1, 3, 4, 3)]
+    assert outs[1].tobytes() == outs[3].tobytes()
+    e64 = _fp64_reference(m, x.float().cpu().numpy(), 4)
+    assert_close(outs[2], e64, 2e-4, 2e-4, "split rows p4")
+    assert ws.error_flags() == 0
+    grid_rows = pm.grid_rows
+    counters = ws.buf[256:256 + grid_rows * 8 * 4].view(torch.int32)
+    assert torch.count_nonzero(counters).item() == 0
+
+
+def test_mixed_depth_against_oracle():
+    rng = np.random.default_rng(7)
+    m = random_matrix(rng, 520, 700)
+    pm = plane_matrix(m)
+    gr, gc = m.grid
+    depth = rng.integers(1, 5, size=(gr, gc), dtype=np.uint8)
+    import harpq_b200 as hqb
+
+    plan = hqb.DepthPlan(torch.from_numpy(depth).cuda(), pm.stage_count)
+    assert int(plan.flags.item()) == 0
+    assert plan.plan.cpu().numpy()[-1] == int(depth.sum())
+    w = pm.decode(depth=plan.depth).cpu().numpy()
+    assert w.tobytes() == orc.dequantize_mixed(m, depth).tobytes()
+    for batch in (1, 3, 12):
+        x = rng.standard_normal((batch, m.cols)).astype(np.float16).astype(np.float32)
+        bias = rng.standard_normal(m.rows).astype(np.float32)
+        y = pm.gemv(torch.from_numpy(x).cuda().half(), depth=plan, bias=torch.from_numpy(bias).cuda(),
+                    y_dtype=torch.float32).cpu().numpy()
+        scalar = orc.linear_mixed(m, x, depth, bias)
+        assert_close(y, scalar, 2e-4, 2e-4, f"mixed b{batch}")
+    # uniform depth map == uniform prefix
+    for p in (1, 4):
+        u = hqb.DepthPlan(torch.full((gr, gc), p, dtype=torch.uint8, device="cuda"), 4)
+        x = torch.randn(2, m.cols, device="cuda").half()
+        a = pm.gemv(x, depth=u, y_dtype=torch.float32)
+        b = pm.gemv(x, prefix=p, y_dtype=torch.float32)
+        assert torch.equal(a, b)
+
+
+def test_depth_plan_flags_bad_entries():
+    import harpq_b200 as hqb
+
+    depth = torch.tensor([[0, 2], [5, 1]], dtype=torch.uint8, device="cuda")
+    plan = hqb.DepthPlan(depth, 4)
+    assert int(plan.flags.item()) & hqb.DEVERR_DEPTH
+    assert plan.plan.cpu().tolist() == [0, 3, 5]  # clamped to [1, 4]
+
+
+def test_repack_flags_bad_scales():
+    import harpq_b200 as hqb
+
+    rng = np.random.default_rng(3)
+    m = random_matrix(rng, 128, 128, stages=1)
+    codes = torch.from_numpy(m.codes[0]).cuda()
+    bits = torch.from_numpy(m.scales[0].astype(np.float16).view(np.int16)).cuda()
+    bits[5] = 0x7E00  # NaN
+    pm = hqb.PlaneMatrix(128, 128)
+    pm.add_stage(codes, bits)
+    assert int(pm.repack_flags.item()) & hqb.DEVERR_SCALE
+
+
+def test_progressive_stage_append_matches_full_build():
+    """Stages repacked one at a time (residency grows) give the same results."""
+    rng = np.random.default_rng(21)
+    m = random_matrix(rng, 256, 256)
+    full = plane_matrix(m)
+    import harpq_b200 as hqb
+    from conftest import device_stages
+
+    codes, bits, _ = device_stages(m)
+    grow = hqb.PlaneMatrix(m.rows, m.cols)
+    x = torch.randn(1, m.cols, device="cuda").half()
+    for s in range(4):
+        grow.add_stage(codes[s], bits[s])
+        assert torch.equal(grow.gemv(x, prefix=s + 1, y_dtype=torch.float32),
+                           full.gemv(x, prefix=s + 1, y_dtype=torch.float32))
+
+
+@pytest.mark.parametrize("rows,cols", [(1, 1), (129, 127), (4096, 128), (128, 4224)])
+def test_edge_shapes(rows, cols):
+    rng = np.random.default_rng(rows * 7 + cols)
+    m = random_matrix(rng, rows, cols)
+    pm = plane_matrix(m)
+    assert pm.decode(4).cpu().numpy().tobytes() == orc.dequantize_prefix_np(m, 4).tobytes()
+    x = rng.standard_normal((2, cols)).astype(np.float16).astype(np.float32)
+    y = pm.gemv(torch.from_numpy(x).cuda().half(), prefix=4, y_dtype=torch.float32).cpu().numpy()
+    assert_close(y, _fp64_reference(m, x, 4), 2e-4, 2e-4, f"{rows}x{cols}")
+
+
+def test_simt_comparison_kernel_matches():
+    import harpq_b200 as hqb
+
+    rng = np.random.default_rng(5)
+    m = random_matrix(rng, 384, 640)
+    pm = plane_matrix(m)
+    for batch in (1, 4, 8):
+        x = rng.standard_normal((batch, m.cols)).astype(np.float16).astype(np.float32)
+        y = pm.gemv(torch.from_numpy(x).cuda().half(), prefix=3, y_dtype=torch.float32,
+                    flags=hqb.FLAG_SIMT).cpu().numpy()
+        assert_close(y, _fp64_reference(m, x, 3), 2e-4, 2e-4, f"simt b{batch}")
+
+
+def test_prepared_activations_shared_across_matrices():
+    import harpq_b200 as hqb
+
+    rng = np.random.default_rng(9)
+    a = plane_matrix(random_matrix(rng, 256, 512))
+    b = plane_matrix(random_matrix(rng, 640, 512))
+    x = torch.randn(3, 512, device="cuda").half()
+    xf = hqb.prepare_x(x)
+    for pm in (a, b):
+        ya = pm.gemv(x, prefix=2, y_dtype=torch.float32, x_prepared=xf)
+        yb = pm.gemv(x, prefix=2, y_dtype=torch.float32)
+        assert torch.equal(ya, yb)
+    # PDL launch flag gives the same result
+    y1 = a.gemv(x, prefix=3, y_dtype=torch.float32, x_prepared=xf, flags=hqb.FLAG_PDL)
+    y2 = a.gemv(x, prefix=3, y_dtype=torch.float32)
+    torch.cuda.synchronize()
+    assert torch.equal(y1, y2)
+
+
+def test_invalid_arguments_rejected_without_launch():
+    import harpq_b200 as hqb
+
+    rng = np.random.default_rng(2)
+    pm = plane_matrix(random_matrix(rng, 128, 128))
+    x = torch.randn(1, 128, device="cuda").half()
+    with pytest.raises(hqb.HQBError) as e:
+        pm.gemv(x, prefix=5)
+    assert e.value.status == 1
+    with pytest.raises(hqb.HQBError):
+        pm.gemv(torch.randn(17, 128, device="cuda").half(), prefix=1)
+    with pytest.raises(hqb.HQBError):
+        pm.gemv(x, prefix=1, flags=hqb.FLAG_SIMT, y_dtype=torch.float32, workspace=hqb.Workspace(256))
