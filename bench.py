@@ -105,25 +105,6 @@ def make_layer(rows, cols, std, seed, device):
     return codes, bits
 
 
-def shard_rows(rows: int, world: int, rank: int) -> tuple[int, int]:
-    """Tile-row aligned contiguous slice of the output rows for one rank."""
-    tiles = -(-rows // 128)
-    t0, t1 = tiles * rank // world, tiles * (rank + 1) // world
-    r0, r1 = t0 * 128, min(t1 * 128, rows)
-    return r0, r1 - r0
-
-
-def slice_stage_rows(codes, bits, rows, cols, r0, nrows):
-    kpad = -(-cols // 128) * 128
-    cpr = kpad // 4
-    c = [x[r0 * cpr:(r0 + -(-nrows // 128) * 128) * cpr].contiguous() for x in codes]
-    per_tile_row = (kpad // 128) * 128
-    t0 = r0 // 128
-    nt = -(-nrows // 128)
-    b = [x[t0 * per_tile_row:(t0 + nt) * per_tile_row].contiguous() for x in bits]
-    return c, b
-
-
 # ---------------------------------------------------------------------------------------
 # clocks
 
@@ -194,9 +175,11 @@ def build_workload(name, rank, world, device, rotation_target):
     step_bytes = 0
     for li, (lname, rows, cols, src) in enumerate(layers):
         codes, bits = make_layer(rows, cols, std, 1000 + li, device)
-        r0, nrows = (0, rows) if world == 1 else shard_rows(rows, world, rank)
+        r0, nrows = (0, rows) if world == 1 else hqb.shard_rows(rows, world, rank)
         if world > 1:
-            codes, bits = slice_stage_rows(codes, bits, rows, cols, r0, nrows)
+            codes, bits = hqb.slice_stage_rows(codes, bits, cols, r0, nrows)
+            codes = [c.contiguous() for c in codes]
+            bits = [b.contiguous() for b in bits]
         pm = hqb.PlaneMatrix.from_stages(nrows, cols, codes, bits)
         del codes, bits
         built.append({"name": lname, "rows": rows, "cols": cols, "src": src, "r0": r0, "nrows": nrows,
@@ -230,7 +213,7 @@ def run_ours(args, rank, world, device):
     x_dev = {s: torch.randn(1, k, generator=gen, device=device).half() for s, k in srcs.items()}
     xfrag = {s: hqb.prepare_x(x_dev[s]) for s in srcs}
     y_loc = {L["name"]: torch.empty(1, L["nrows"], dtype=torch.float16, device=device) for L in layers}
-    y_full = {L["name"]: torch.empty(world, -(-(-(-L["rows"] // 128)) // world) * 128 if world > 1 else L["rows"],
+    y_full = {L["name"]: torch.empty(world, hqb.shard_pad_rows(L["rows"], world) if world > 1 else L["rows"],
                                      dtype=torch.float16, device=device) for L in layers}
     ws_bytes = max(L["copies"][0].workspace_bytes(1, hqb.F16) for L in layers)
     ws = hqb.Workspace(ws_bytes, device)

@@ -45,8 +45,8 @@ constexpr uint32_t kRowBlockBytes = 544;
 constexpr uint32_t kRecordBytes = HQB_TILE_RECORD_BYTES;
 constexpr uint32_t kConsumerWarps = 8;
 constexpr uint32_t kGemvThreads = (kConsumerWarps + 1) * 32;
-constexpr uint32_t kRingLog2 = 3;  // 8 tile-stage slots per CTA (34 KB in flight)
-constexpr uint32_t kXRing = 4;
+constexpr uint32_t kUnitsInFlight = 12;     // tile-stages buffered per CTA (52 KB)
+constexpr uint32_t kSmemBudget = 100 * 1024;  // ring bytes per CTA, two CTAs per SM
 constexpr uint32_t kMaxCtasPerSm = 2;
 
 static_assert(kRecordBytes == 8 * kRowBlockBytes, "record = 8 row blocks");
@@ -68,6 +68,9 @@ struct GemvParams {
   uint32_t stage_count;
   uint32_t batch;
   uint32_t xslot_bytes;
+  uint32_t ring_slots;   // ring slots (runs) per CTA
+  uint32_t slot_stride;  // header + activation fragments + max-run records
+  uint32_t shift_mul;    // 2^24: w >> 8 computed as a high multiply
   int bias_dtype;
   int y_dtype;
 };
@@ -171,24 +174,36 @@ __global__ void __launch_bounds__(128) prep_x_kernel(const XT* __restrict__ x, u
 
 // --------------------------------------------------------------------------------------
 // GEMV
+//
+// Warp roles per CTA: warp 8 lane 0 is the producer; warps 0..7 are consumers, warp w
+// owning rows 16w..16w+15 of every tile.  The CTA's unit range is walked as "runs":
+// stages [s0, s1) of one tile.  One ring slot carries one run:
+//     [16-byte header][activation fragments of the tile][record s0]...[record s1-1]
+// The producer alone walks the schedule (uniform prefix or depth map), writes the
+// header and issues the bulk copies; consumers only follow headers.
 
-struct Cursor {
-  uint32_t r, c, s, d;
+constexpr uint32_t kHdrBytes = 16;
+constexpr uint32_t kFlagFlush = 1;  // this run ends the CTA's part of its tile row
+constexpr uint32_t kFlagLast = 2;   // last run of the CTA
+constexpr uint32_t kFlagError = 4;  // schedule error: consumers stop
 
-  __device__ bool init(uint64_t u, const GemvParams& p) {
+struct RunCursor {
+  uint32_t r, c, s, left;
+
+  __device__ bool init(uint64_t u, uint32_t n, const GemvParams& p) {
+    left = n;
     if (p.plan == nullptr) {
       const uint64_t per_row = static_cast<uint64_t>(p.C) * p.prefix;
       r = static_cast<uint32_t>(u / per_row);
       const uint64_t rem = u - static_cast<uint64_t>(r) * per_row;
       c = static_cast<uint32_t>(rem / p.prefix);
       s = static_cast<uint32_t>(rem - static_cast<uint64_t>(c) * p.prefix);
-      d = p.prefix;
       return true;
     }
     r = row_of_unit(u, p.plan, p.R, 0);
     uint64_t off = u - p.plan[r];
     for (c = 0; c < p.C; ++c) {
-      d = clamp_depth(p.depth[static_cast<uint64_t>(r) * p.C + c], p.stage_count);
+      const uint32_t d = clamp_depth(p.depth[static_cast<uint64_t>(r) * p.C + c], p.stage_count);
       if (off < d) {
         s = static_cast<uint32_t>(off);
         return true;
@@ -198,85 +213,110 @@ struct Cursor {
     return false;  // plan and depth map disagree
   }
 
-  __device__ void advance(const GemvParams& p) {
-    if (++s < d) return;
+  // Next run; false when the schedule walks past the last tile row (inconsistent plan).
+  __device__ bool next(const GemvParams& p, uint32_t& rr, uint32_t& cc, uint32_t& s0, uint32_t& s1,
+                       uint32_t& flags) {
+    if (r >= p.R) return false;
+    const uint32_t d = p.plan == nullptr ? p.prefix : clamp_depth(p.depth[static_cast<uint64_t>(r) * p.C + c], p.stage_count);
+    rr = r;
+    cc = c;
+    s0 = s;
+    s1 = min(d, s + left);
+    left -= s1 - s0;
     s = 0;
+    flags = 0;
     if (++c == p.C) {
       c = 0;
       ++r;
+      flags |= kFlagFlush;
     }
-    if (p.plan != nullptr && r < p.R) d = clamp_depth(p.depth[static_cast<uint64_t>(r) * p.C + c], p.stage_count);
-  }
-
-  __device__ const uint8_t* record(const GemvParams& p) const {
-    return p.planes[s] + (static_cast<uint64_t>(r) * p.C + c) * kRecordBytes;
+    if (left == 0) flags |= kFlagFlush | kFlagLast;
+    return true;
   }
 };
 
-struct Pipe {
-  uint8_t* ring;
-  uint8_t* xring;
+struct Ring {
+  uint8_t* base;
   uint64_t* full;
   uint64_t* empty;
-  uint64_t* xfull;
-  uint64_t* xempty;
+  uint32_t slots, stride;
 };
 
-__device__ void gemv_producer(const GemvParams& p, const Pipe& pp, uint64_t u0, uint32_t n) {
+__device__ void gemv_producer(const GemvParams& p, const Ring& ring, uint64_t u0, uint32_t n) {
   const uint64_t stream_policy = policy_evict_first();
   const uint64_t keep_policy = policy_evict_last();
-  constexpr uint32_t NS = 1u << kRingLog2;
-  Cursor cur;
-  if (!cur.init(u0, p)) {
+  RunCursor rc;
+  uint32_t k = 0;
+  if (!rc.init(u0, n, p)) {
     atomicOr(p.error, HQB_DEVERR_DEPTH);
-    return;  // nothing issued
+    uint32_t* hdr = reinterpret_cast<uint32_t*>(ring.base);
+    hdr[0] = hdr[1] = 0;
+    hdr[2] = (kFlagLast | kFlagError) << 16;
+    mbar_arrive(&ring.full[0]);  // a header-only phase tells the consumers to stop
+    return;
   }
-  // Prologue: weight records do not depend on the preceding kernel (see
-  // HQB_FLAG_PDL), so fill the ring before waiting for it.
-  const uint32_t pre = min(n, NS);
-  uint32_t issued = 0, tiles = 0;
-  bool ok = true;
-  Cursor pc = cur;
-  for (; issued < pre; ++issued) {
-    if (pc.r >= p.R) {  // only reachable when a depth plan disagrees with its map
+  // Prologue: weight records do not depend on the preceding kernel (HQB_FLAG_PDL), so
+  // fill the ring with them before waiting for it; activations follow the wait.
+  uint32_t r, c, s0, s1, flags = 0;
+  bool last = false, ok = true;
+  for (; k < ring.slots && !last; ++k) {
+    uint8_t* slot = ring.base + k * ring.stride;
+    if (!rc.next(p, r, c, s0, s1, flags)) {
       atomicOr(p.error, HQB_DEVERR_DEPTH);
+      flags = kFlagLast | kFlagError;
+      s1 = s0 = 0;
       ok = false;
-      break;
     }
-    mbar_expect_tx(&pp.full[issued], kRecordBytes);
-    bulk_load(pp.ring + issued * kRecordBytes, pc.record(p), kRecordBytes, &pp.full[issued], stream_policy);
-    pc.advance(p);
+    last = (flags & kFlagLast) != 0;
+    uint32_t* hdr = reinterpret_cast<uint32_t*>(slot);
+    hdr[0] = r;
+    hdr[1] = c;
+    hdr[2] = (s1 - s0) | (flags << 16);
+    mbar_expect_tx(&ring.full[k], ok ? p.xslot_bytes + (s1 - s0) * kRecordBytes : 0);
+    for (uint32_t s = s0; s < s1; ++s)
+      bulk_load(slot + kHdrBytes + p.xslot_bytes + (s - s0) * kRecordBytes,
+                p.planes[s] + (static_cast<uint64_t>(r) * p.C + c) * kRecordBytes, kRecordBytes, &ring.full[k],
+                stream_policy);
   }
+  const uint32_t pre = k;
   griddep_wait();
-  for (uint32_t i = 0; ok && i < n; ++i) {
-    if (cur.r >= p.R) {
+  for (uint32_t j = 0; j < pre; ++j) {
+    uint8_t* slot = ring.base + j * ring.stride;
+    if ((reinterpret_cast<const uint32_t*>(slot)[2] >> 16) & kFlagError) break;  // header-only slot
+    const uint32_t cj = reinterpret_cast<const uint32_t*>(slot)[1];
+    bulk_load(slot + kHdrBytes, p.xfrag + static_cast<uint64_t>(cj) * p.xslot_bytes, p.xslot_bytes, &ring.full[j],
+              keep_policy);
+  }
+  while (!last && ok) {
+    const uint32_t i = k % ring.slots;
+    uint8_t* slot = ring.base + i * ring.stride;
+    if (!mbar_wait(&ring.empty[i], ((k / ring.slots) - 1) & 1, p.error)) break;
+    uint32_t* hdr = reinterpret_cast<uint32_t*>(slot);
+    if (!rc.next(p, r, c, s0, s1, flags)) {
       atomicOr(p.error, HQB_DEVERR_DEPTH);
+      hdr[2] = (kFlagLast | kFlagError) << 16;
+      mbar_arrive(&ring.full[i]);
+      ++k;
       break;
     }
-    if (i == 0 || cur.s == 0) {
-      const uint32_t xs = tiles % kXRing;
-      if (tiles >= kXRing && !mbar_wait(&pp.xempty[xs], ((tiles / kXRing) - 1) & 1, p.error)) break;
-      mbar_expect_tx(&pp.xfull[xs], p.xslot_bytes);
-      bulk_load(pp.xring + xs * p.xslot_bytes, p.xfrag + static_cast<uint64_t>(cur.c) * p.xslot_bytes,
-                p.xslot_bytes, &pp.xfull[xs], keep_policy);
-      ++tiles;
-    }
-    if (i >= NS) {
-      const uint32_t slot = i & (NS - 1);
-      if (!mbar_wait(&pp.empty[slot], ((i >> kRingLog2) - 1) & 1, p.error)) break;
-      mbar_expect_tx(&pp.full[slot], kRecordBytes);
-      bulk_load(pp.ring + slot * kRecordBytes, cur.record(p), kRecordBytes, &pp.full[slot], stream_policy);
-      issued = i + 1;
-    }
-    cur.advance(p);
+    last = (flags & kFlagLast) != 0;
+    hdr[0] = r;
+    hdr[1] = c;
+    hdr[2] = (s1 - s0) | (flags << 16);
+    mbar_expect_tx(&ring.full[i], p.xslot_bytes + (s1 - s0) * kRecordBytes);
+    bulk_load(slot + kHdrBytes, p.xfrag + static_cast<uint64_t>(c) * p.xslot_bytes, p.xslot_bytes, &ring.full[i],
+              keep_policy);
+    for (uint32_t s = s0; s < s1; ++s)
+      bulk_load(slot + kHdrBytes + p.xslot_bytes + (s - s0) * kRecordBytes,
+                p.planes[s] + (static_cast<uint64_t>(r) * p.C + c) * kRecordBytes, kRecordBytes, &ring.full[i],
+                stream_policy);
+    ++k;
   }
   griddep_launch_dependents();
-  // Every bulk copy this CTA issued must land before the CTA may exit, whatever
-  // path led here (consumers may have left early on an error).
-  for (uint32_t j = issued > NS ? issued - NS : 0; j < issued; ++j)
-    mbar_wait(&pp.full[j & (NS - 1)], (j >> kRingLog2) & 1, p.error);
-  for (uint32_t t = tiles > kXRing ? tiles - kXRing : 0; t < tiles; ++t)
-    mbar_wait(&pp.xfull[t % kXRing], (t / kXRing) & 1, p.error);
+  // Every bulk copy this CTA issued must land before the CTA may exit, whatever path
+  // led here (consumers may have left early on an error).
+  for (uint32_t j = k > ring.slots ? k - ring.slots : 0; j < k; ++j)
+    mbar_wait(&ring.full[j % ring.slots], (j / ring.slots) & 1, p.error);
 }
 
 template <int NB>
@@ -306,21 +346,19 @@ __device__ __forceinline__ void store_out(const GemvParams& p, const float (&v)[
   }
 }
 
-// Finishes the contribution of this warp's 16 rows of tile row r.
-template <int NB>
-__device__ void flush_rows(const GemvParams& p, uint32_t r, const float (&y)[NB][4], uint32_t cta,
-                           uint64_t total, uint32_t ctas, uint32_t warp, uint32_t lane) {
+struct RowSplit {
+  uint32_t first, last;  // CTAs contributing to the tile row
+};
+
+__device__ __forceinline__ RowSplit row_split(const GemvParams& p, uint32_t r, uint64_t total, uint32_t ctas) {
   const uint64_t per_row = static_cast<uint64_t>(p.C) * p.prefix;
   const uint64_t rb = row_begin(r, p.plan, per_row), re = row_begin(r + 1, p.plan, per_row);
-  const uint32_t first = unit_owner(rb, total, ctas), last = unit_owner(re - 1, total, ctas);
-  const uint32_t g = lane >> 2, q = lane & 3;
-  const uint32_t rit0 = warp * 16 + g;
-  const uint32_t row0 = r * 128 + rit0;
-  if (first == last) {
-    store_out<NB>(p, y, row0, q);
-    return;
-  }
-  const uint32_t k = row_of_unit(unit_start(cta, total, ctas), p.plan, p.R, per_row) == r ? 0 : 1;
+  return RowSplit{unit_owner(rb, total, ctas), unit_owner(re - 1, total, ctas)};
+}
+
+template <int NB>
+__device__ __forceinline__ void publish_partial(const GemvParams& p, uint32_t cta, uint32_t k, const float (&y)[NB][4],
+                                                uint32_t rit0, uint32_t q) {
   float* part = p.partials + static_cast<uint64_t>(cta * 2 + k) * p.batch * 128;
 #pragma unroll
   for (int nb = 0; nb < NB; ++nb)
@@ -332,19 +370,20 @@ __device__ void flush_rows(const GemvParams& p, uint32_t r, const float (&y)[NB]
         part[b * 128 + rit0 + 8] = y[nb][2 + j];
       }
     }
-  __threadfence();
-  __syncwarp();
-  uint32_t ticket = 0;
-  if (lane == 0) ticket = atomicAdd(&p.counters[r * 8 + warp], 1u);
-  ticket = __shfl_sync(0xffffffffu, ticket, 0);
-  if (ticket != last - first) return;
-  __threadfence();
+}
+
+// Last arriver of a split tile row: sum the contributions in CTA order, add bias, store.
+template <int NB>
+__device__ void finish_split_row(const GemvParams& p, uint32_t r, RowSplit rs, uint64_t total, uint32_t ctas,
+                                 uint32_t warp, uint32_t lane) {
+  const uint64_t per_row = static_cast<uint64_t>(p.C) * p.prefix;
+  const uint32_t q = lane & 3, rit0 = warp * 16 + (lane >> 2);
   float sum[NB][4];
 #pragma unroll
   for (int nb = 0; nb < NB; ++nb)
 #pragma unroll
-    for (int k2 = 0; k2 < 4; ++k2) sum[nb][k2] = 0.0f;
-  for (uint32_t i = first; i <= last; ++i) {
+    for (int e = 0; e < 4; ++e) sum[nb][e] = 0.0f;
+  for (uint32_t i = rs.first; i <= rs.last; ++i) {
     const uint32_t ki = row_of_unit(unit_start(i, total, ctas), p.plan, p.R, per_row) == r ? 0 : 1;
     const float* src = p.partials + static_cast<uint64_t>(i * 2 + ki) * p.batch * 128;
 #pragma unroll
@@ -358,22 +397,17 @@ __device__ void flush_rows(const GemvParams& p, uint32_t r, const float (&y)[NB]
         }
       }
   }
-  store_out<NB>(p, sum, row0, q);
+  store_out<NB>(p, sum, r * 128 + rit0, q);
   if (lane == 0) p.counters[r * 8 + warp] = 0;  // cleared for the next launch
 }
 
-__device__ __forceinline__ uint32_t int2_pair(uint32_t w, uint32_t w_hi, int m) {
-  const int sh = 2 * (m & 3);
-  return (((m < 4) ? w : w_hi) & (0x00030003u << sh)) ^ (0x00020002u << sh);
-}
-
-// Tensor-core consumer state for one warp.
+// Activation fragments of one tile for this lane (batch rows g and g+8).
 template <int NB, int XL>
-struct MmaConsumer {
+struct XFrag {
   uint32_t bf[NB][XL][8][2];
   float f[NB][2], gsum[NB][2];
 
-  __device__ void load_x(const GemvParams& p, const uint8_t* slot, uint32_t lane) {
+  __device__ __forceinline__ void load(const GemvParams& p, const uint8_t* slot, uint32_t lane) {
     const uint32_t g = lane >> 2, q = lane & 3;
 #pragma unroll
     for (int nb = 0; nb < NB; ++nb) {
@@ -405,202 +439,266 @@ struct MmaConsumer {
       }
     }
   }
+};
 
-  __device__ __forceinline__ void tile_stage(const uint4 w, uint32_t sc, float (&y)[NB][4]) const {
-    const uint32_t h0 = w.x >> 8, h1 = w.y >> 8, h2 = w.z >> 8, h3 = w.w >> 8;
-    float acc[NB][2][4];
+__device__ __forceinline__ uint32_t int2_pair(uint32_t w, uint32_t w_hi, int m) {
+  const int sh = 2 * (m & 3);
+  return (((m < 4) ? w : w_hi) & (0x00030003u << sh)) ^ (0x00020002u << sh);
+}
+
+// LEN stages of one tile through the tensor cores: LEN independent accumulator chains.
+template <int NB, int XL, int LEN>
+__device__ __forceinline__ void mma_run(const XFrag<NB, XL>& xf, const uint4 (&w)[HQB_MAX_STAGES],
+                                        const uint32_t (&sc)[HQB_MAX_STAGES], uint32_t shift_mul, float (&y)[NB][4]) {
+  uint32_t hi[LEN][4];
+#pragma unroll
+  for (int j = 0; j < LEN; ++j) {
+    // w >> 8 as a high multiply: runs on the FMA pipe and leaves the ALU pipe to the decode
+    hi[j][0] = __umulhi(w[j].x, shift_mul);
+    hi[j][1] = __umulhi(w[j].y, shift_mul);
+    hi[j][2] = __umulhi(w[j].z, shift_mul);
+    hi[j][3] = __umulhi(w[j].w, shift_mul);
+  }
+  float acc[LEN][NB][4];
+#pragma unroll
+  for (int j = 0; j < LEN; ++j)
 #pragma unroll
     for (int nb = 0; nb < NB; ++nb)
 #pragma unroll
-      for (int k = 0; k < 2; ++k)
+      for (int e = 0; e < 4; ++e) acc[j][nb][e] = 0.0f;
 #pragma unroll
-        for (int e = 0; e < 4; ++e) acc[nb][k][e] = 0.0f;
+  for (int m = 0; m < 8; ++m) {
 #pragma unroll
-    for (int m = 0; m < 8; ++m) {
-      const uint32_t a0 = int2_pair(w.x, h0, m), a1 = int2_pair(w.y, h1, m);
-      const uint32_t a2 = int2_pair(w.z, h2, m), a3 = int2_pair(w.w, h3, m);
+    for (int j = 0; j < LEN; ++j) {
+      const uint32_t a0 = int2_pair(w[j].x, hi[j][0], m), a1 = int2_pair(w[j].y, hi[j][1], m);
+      const uint32_t a2 = int2_pair(w[j].z, hi[j][2], m), a3 = int2_pair(w[j].w, hi[j][3], m);
 #pragma unroll
       for (int nb = 0; nb < NB; ++nb)
 #pragma unroll
-        for (int l = 0; l < XL; ++l) mma_f16(acc[nb][m & 1], a0, a1, a2, a3, bf[nb][l][m][0], bf[nb][l][m][1]);
+        for (int l = 0; l < XL; ++l) mma_f16(acc[j][nb], a0, a1, a2, a3, xf.bf[nb][l][m][0], xf.bf[nb][l][m][1]);
     }
-    const float s_lo = half_bits_to_float(sc & 0xFFFFu), s_hi = half_bits_to_float(sc >> 16);
+  }
+#pragma unroll
+  for (int j = 0; j < LEN; ++j) {
+    const __half2 s2 = *reinterpret_cast<const __half2*>(&sc[j]);
+    const float s_lo = __low2float(s2), s_hi = __high2float(s2);
 #pragma unroll
     for (int nb = 0; nb < NB; ++nb) {
-      const float t0 = acc[nb][0][0] + acc[nb][1][0], t1 = acc[nb][0][1] + acc[nb][1][1];
-      const float t2 = acc[nb][0][2] + acc[nb][1][2], t3 = acc[nb][0][3] + acc[nb][1][3];
-      y[nb][0] = fmaf(s_lo, fmaf(t0, f[nb][0], -gsum[nb][0]), y[nb][0]);
-      y[nb][1] = fmaf(s_lo, fmaf(t1, f[nb][1], -gsum[nb][1]), y[nb][1]);
-      y[nb][2] = fmaf(s_hi, fmaf(t2, f[nb][0], -gsum[nb][0]), y[nb][2]);
-      y[nb][3] = fmaf(s_hi, fmaf(t3, f[nb][1], -gsum[nb][1]), y[nb][3]);
+      y[nb][0] = fmaf(s_lo, fmaf(acc[j][nb][0], xf.f[nb][0], -xf.gsum[nb][0]), y[nb][0]);
+      y[nb][1] = fmaf(s_lo, fmaf(acc[j][nb][1], xf.f[nb][1], -xf.gsum[nb][1]), y[nb][1]);
+      y[nb][2] = fmaf(s_hi, fmaf(acc[j][nb][2], xf.f[nb][0], -xf.gsum[nb][0]), y[nb][2]);
+      y[nb][3] = fmaf(s_hi, fmaf(acc[j][nb][3], xf.f[nb][1], -xf.gsum[nb][1]), y[nb][3]);
     }
   }
+}
 
-  __device__ __forceinline__ void finish(float (&)[NB][4], uint32_t) const {}
-};
-
-// CUDA-core consumer (comparison kernel): codes decoded to FP32 with an exponent
-// trick, FFMA per code and batch row.  Batch <= 8, FP16 activations.
-struct SimtConsumer {
-  const uint8_t* slot;
-  float xscale[8];  // 2^e of the current tile per batch row
-  float part[2][8];
-
-  __device__ void reset() {
+// CUDA-core comparison consumer: each code decoded to FP32 with an exponent trick and
+// one FFMA per code and batch row; partial column sums per lane are reduced across the
+// lane quad when a tile row is finished.  Batch <= 8, FP16 activations.
+__device__ __forceinline__ void simt_unit(const GemvParams& p, const uint8_t* xslot, uint32_t lane, const uint4 w,
+                                          uint32_t sc, float (&part)[2][8]) {
+  const uint32_t q = lane & 3;
+  const __half2 s2 = *reinterpret_cast<const __half2*>(&sc);
+  const float s_lo = __low2float(s2), s_hi = __high2float(s2);
 #pragma unroll
-    for (int h = 0; h < 2; ++h)
+  for (uint32_t b = 0; b < 8; ++b) {
+    if (b >= p.batch) break;
+    const float xsc = lds_f2(xslot + p.batch * 256 + b * 8).x * 0x1p-24f;  // 2^e of the tile
+    const uint8_t* src = xslot + (b * 4 + q) * 64;
+    uint32_t hx[16];
 #pragma unroll
-      for (int b = 0; b < 8; ++b) part[h][b] = 0.0f;
+    for (int v = 0; v < 4; ++v) {
+      const uint4 t = lds128(src + 16 * v);
+      hx[4 * v] = t.x;
+      hx[4 * v + 1] = t.y;
+      hx[4 * v + 2] = t.z;
+      hx[4 * v + 3] = t.w;
+    }
+    float d0 = 0.0f, d1 = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      const int m = i & 7, which = i >> 3;
+      const int idx = m * 4 + which;  // half index inside (b, q)
+      const uint32_t hb = (idx & 1) ? (hx[idx >> 1] >> 16) : (hx[idx >> 1] & 0xFFFFu);
+      const float xv = half_bits_to_float(hb) * static_cast<float>(1 << (2 * (m & 3)));
+      const uint32_t wg = i < 16 ? w.x : w.z, wh = i < 16 ? w.y : w.w;
+      const int sh = 2 * (i & 15);
+      const float cg = __uint_as_float(0x4B000000u | (((wg >> sh) & 3u) ^ 2u)) - 8388610.0f;
+      const float ch = __uint_as_float(0x4B000000u | (((wh >> sh) & 3u) ^ 2u)) - 8388610.0f;
+      d0 = fmaf(cg, xv, d0);
+      d1 = fmaf(ch, xv, d1);
+    }
+    part[0][b] = fmaf(s_lo * xsc, d0, part[0][b]);
+    part[1][b] = fmaf(s_hi * xsc, d1, part[1][b]);
   }
+}
 
-  __device__ void load_x(const GemvParams& p, const uint8_t* s, uint32_t) {
-    slot = s;
+__device__ __forceinline__ void simt_finish(float (&part)[2][8], float (&y)[1][4], uint32_t lane) {
+  const uint32_t q = lane & 3;
+#pragma unroll
+  for (int h = 0; h < 2; ++h)
+#pragma unroll
+    for (int b = 0; b < 8; ++b) {
+      float v = part[h][b];
+      v += __shfl_xor_sync(0xffffffffu, v, 1);
+      v += __shfl_xor_sync(0xffffffffu, v, 2);
+      part[h][b] = v;
+    }
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    float v0 = 0.0f, v1 = 0.0f;
 #pragma unroll
     for (int b = 0; b < 8; ++b)
-      xscale[b] = b < static_cast<int>(p.batch) ? lds_f2(s + p.batch * 256 + b * 8).x * 0x1p-24f : 0.0f;
-  }
-
-  __device__ __forceinline__ void tile_stage(const GemvParams& p, uint32_t lane, const uint4 w, uint32_t sc) {
-    const uint32_t q = lane & 3;
-    const float s_lo = half_bits_to_float(sc & 0xFFFFu), s_hi = half_bits_to_float(sc >> 16);
-#pragma unroll
-    for (uint32_t b = 0; b < 8; ++b) {
-      if (b >= p.batch) break;
-      const uint8_t* src = slot + (b * 4 + q) * 64;
-      uint32_t hx[16];
-#pragma unroll
-      for (int v = 0; v < 4; ++v) {
-        const uint4 t = lds128(src + 16 * v);
-        hx[4 * v] = t.x;
-        hx[4 * v + 1] = t.y;
-        hx[4 * v + 2] = t.z;
-        hx[4 * v + 3] = t.w;
+      if (static_cast<uint32_t>(b) == 2 * q + j) {
+        v0 = part[0][b];
+        v1 = part[1][b];
       }
-      float d0 = 0.0f, d1 = 0.0f;
-#pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const int m = i & 7, which = i >> 3;
-        const int idx = m * 4 + which;  // half index inside (b, q)
-        const uint32_t hb = (idx & 1) ? (hx[idx >> 1] >> 16) : (hx[idx >> 1] & 0xFFFFu);
-        const float xv = half_bits_to_float(hb) * static_cast<float>(1 << (2 * (m & 3)));
-        const uint32_t wg = i < 16 ? w.x : w.z, wh = i < 16 ? w.y : w.w;
-        const int sh = 2 * (i & 15);
-        const float cg = __uint_as_float(0x4B000000u | (((wg >> sh) & 3u) ^ 2u)) - 8388610.0f;
-        const float ch = __uint_as_float(0x4B000000u | (((wh >> sh) & 3u) ^ 2u)) - 8388610.0f;
-        d0 = fmaf(cg, xv, d0);
-        d1 = fmaf(ch, xv, d1);
-      }
-      part[0][b] = fmaf(s_lo * xscale[b], d0, part[0][b]);
-      part[1][b] = fmaf(s_hi * xscale[b], d1, part[1][b]);
-    }
+    y[0][j] = v0;
+    y[0][2 + j] = v1;
   }
-
-  // Reduce the quad's column partials and move to the tensor-core output layout.
-  __device__ void finish(float (&y)[1][4], uint32_t lane) {
-    const uint32_t q = lane & 3;
 #pragma unroll
-    for (int h = 0; h < 2; ++h)
+  for (int h = 0; h < 2; ++h)
 #pragma unroll
-      for (int b = 0; b < 8; ++b) {
-        float v = part[h][b];
-        v += __shfl_xor_sync(0xffffffffu, v, 1);
-        v += __shfl_xor_sync(0xffffffffu, v, 2);
-        part[h][b] = v;
-      }
-#pragma unroll
-    for (int j = 0; j < 2; ++j) {
-      float v0 = 0.0f, v1 = 0.0f;
-#pragma unroll
-      for (int b = 0; b < 8; ++b)
-        if (static_cast<uint32_t>(b) == 2 * q + j) {
-          v0 = part[0][b];
-          v1 = part[1][b];
-        }
-      y[0][j] = v0;
-      y[0][2 + j] = v1;
-    }
-    reset();
-  }
-};
+    for (int b = 0; b < 8; ++b) part[h][b] = 0.0f;
+}
 
 template <int NB, int XL, bool SIMT>
-__global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_constant__ GemvParams p) {
+__global__ void __launch_bounds__(kGemvThreads, (NB == 1 && XL == 1 && !SIMT) ? kMaxCtasPerSm : 1)
+    gemv_kernel(const __grid_constant__ GemvParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
-  constexpr uint32_t NS = 1u << kRingLog2;
-  const uint32_t ctas = gridDim.x, cta = blockIdx.x;
   const uint64_t total = p.plan != nullptr ? static_cast<uint64_t>(p.plan[p.R]) : p.total;
+  // Mixed depth launches the full grid (the unit count lives on the device); both
+  // modes partition over min(grid, units) CTAs so equal unit counts split equally.
+  const uint32_t ctas = static_cast<uint32_t>(total < gridDim.x ? total : gridDim.x), cta = blockIdx.x;
+  if (cta >= ctas) return;
   const uint64_t u0 = unit_start(cta, total, ctas), u1 = unit_start(cta + 1, total, ctas);
-  if (u0 >= u1) return;
   const uint32_t n = static_cast<uint32_t>(u1 - u0);
 
-  Pipe pp;
-  pp.ring = smem;
-  pp.xring = smem + NS * kRecordBytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(pp.xring + kXRing * p.xslot_bytes);
-  pp.full = bars;
-  pp.empty = bars + NS;
-  pp.xfull = bars + 2 * NS;
-  pp.xempty = bars + 2 * NS + kXRing;
+  Ring ring;
+  ring.base = smem;
+  ring.slots = p.ring_slots;
+  ring.stride = p.slot_stride;
+  ring.full = reinterpret_cast<uint64_t*>(smem + ring.slots * ring.stride);
+  ring.empty = ring.full + ring.slots;
   const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
-    for (uint32_t i = 0; i < NS; ++i) {
-      mbar_init(&pp.full[i], 1);
-      mbar_init(&pp.empty[i], kConsumerWarps);
-    }
-    for (uint32_t i = 0; i < kXRing; ++i) {
-      mbar_init(&pp.xfull[i], 1);
-      mbar_init(&pp.xempty[i], kConsumerWarps);
+    for (uint32_t i = 0; i < ring.slots; ++i) {
+      mbar_init(&ring.full[i], 1);
+      mbar_init(&ring.empty[i], kConsumerWarps * 32);
     }
     fence_barrier_init();
   }
   __syncthreads();
 
   if (warp == kConsumerWarps) {
-    if (lane == 0) gemv_producer(p, pp, u0, n);
+    if (lane == 0) gemv_producer(p, ring, u0, n);
     return;
   }
 
-  Cursor cur;
-  if (!cur.init(u0, p)) return;  // producer records the error
-  griddep_wait();
-  using Consumer = typename std::conditional<SIMT, SimtConsumer, MmaConsumer<NB, XL>>::type;
-  Consumer cons;
-  if constexpr (SIMT) cons.reset();
+  const uint32_t g = lane >> 2, q = lane & 3, rit0 = warp * 16 + g;
+  const uint64_t per_row = static_cast<uint64_t>(p.C) * p.prefix;
+  const uint32_t first_row = row_of_unit(u0, p.plan, p.R, per_row);
   float y[NB][4];
+  float part[2][8];
 #pragma unroll
   for (int nb = 0; nb < NB; ++nb)
 #pragma unroll
-    for (int k = 0; k < 4; ++k) y[nb][k] = 0.0f;
-  const uint32_t g = lane >> 2;
-  uint32_t tiles = 0;
-  for (uint32_t i = 0; i < n; ++i) {
-    if (cur.r >= p.R) return;  // inconsistent depth plan: the producer records it
-    if (i == 0 || cur.s == 0) {
-      const uint32_t xs = tiles % kXRing;
-      if (!mbar_wait(&pp.xfull[xs], (tiles / kXRing) & 1, p.error)) return;
-      cons.load_x(p, pp.xring + xs * p.xslot_bytes, lane);
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&pp.xempty[xs]);
-      ++tiles;
+    for (int e = 0; e < 4; ++e) y[nb][e] = 0.0f;
+  if constexpr (SIMT) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h)
+#pragma unroll
+      for (int b = 0; b < 8; ++b) part[h][b] = 0.0f;
+  }
+  bool split_first = false, split_last = false;
+  uint32_t last_row = first_row;
+  griddep_wait();
+  for (uint32_t k = 0;; ++k) {
+    const uint32_t i = k % ring.slots;
+    if (!mbar_wait(&ring.full[i], (k / ring.slots) & 1, p.error)) return;
+    const uint8_t* slot = ring.base + i * ring.stride;
+    const uint4 hdr = lds128(slot);
+    const uint32_t len = hdr.z & 0xFFFFu, flags = hdr.z >> 16;
+    if (flags & kFlagError) {
+      mbar_arrive(&ring.empty[i]);
+      return;
     }
-    const uint32_t slot = i & (NS - 1);
-    if (!mbar_wait(&pp.full[slot], (i >> kRingLog2) & 1, p.error)) return;
-    const uint8_t* rec = pp.ring + slot * kRecordBytes + warp * kRowBlockBytes;
-    const uint4 w = lds128(rec + lane * 16);
-    const uint32_t sc = lds32(rec + 512 + g * 4);
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&pp.empty[slot]);
-    if constexpr (SIMT) cons.tile_stage(p, lane, w, sc);
-    else cons.tile_stage(w, sc, y);
-    const uint32_t r_now = cur.r;
-    cur.advance(p);
-    if (i + 1 == n || cur.r != r_now) {
-      if constexpr (SIMT) cons.finish(y, lane);
-      flush_rows<NB>(p, r_now, y, cta, total, ctas, warp, lane);
+    const uint8_t* xs = slot + kHdrBytes;
+    const uint8_t* rec = xs + p.xslot_bytes + warp * kRowBlockBytes;
+    uint4 w[HQB_MAX_STAGES];
+    uint32_t sc[HQB_MAX_STAGES];
+#pragma unroll
+    for (uint32_t j = 0; j < HQB_MAX_STAGES; ++j) {
+      if (j < len) {
+        w[j] = lds128(rec + j * kRecordBytes + lane * 16);
+        sc[j] = lds32(rec + j * kRecordBytes + 512 + g * 4);
+      }
+    }
+    if constexpr (SIMT) {
+#pragma unroll
+      for (uint32_t j = 0; j < HQB_MAX_STAGES; ++j)
+        if (j < len) simt_unit(p, xs, lane, w[j], sc[j], part);
+      mbar_arrive(&ring.empty[i]);
+    } else {
+      XFrag<NB, XL> xf;
+      xf.load(p, xs, lane);
+      mbar_arrive(&ring.empty[i]);  // every lane has its data in registers
+      switch (len) {
+        case 1: mma_run<NB, XL, 1>(xf, w, sc, p.shift_mul, y); break;
+        case 2: mma_run<NB, XL, 2>(xf, w, sc, p.shift_mul, y); break;
+        case 3: mma_run<NB, XL, 3>(xf, w, sc, p.shift_mul, y); break;
+        default: mma_run<NB, XL, 4>(xf, w, sc, p.shift_mul, y); break;
+      }
+    }
+    if (flags & kFlagFlush) {
+      if constexpr (SIMT) simt_finish(part, reinterpret_cast<float(&)[1][4]>(y), lane);
+      const uint32_t r = hdr.x;
+      const RowSplit rs = row_split(p, r, total, ctas);
+      if (rs.first == rs.last) {
+        store_out<NB>(p, y, r * 128 + rit0, q);  // the whole tile row is this CTA's: no fix-up
+      } else if (r == first_row && !split_first) {
+        // Plain stores now; the fence and the arrival ticket wait for the CTA's end so
+        // no fence stalls the stream.
+        split_first = true;
+        publish_partial<NB>(p, cta, 0, y, rit0, q);
+      } else {
+        split_last = true;
+        last_row = r;
+        publish_partial<NB>(p, cta, r == first_row ? 0 : 1, y, rit0, q);
+      }
 #pragma unroll
       for (int nb = 0; nb < NB; ++nb)
 #pragma unroll
-        for (int k = 0; k < 4; ++k) y[nb][k] = 0.0f;
+        for (int e = 0; e < 4; ++e) y[nb][e] = 0.0f;
+    }
+    if (flags & kFlagLast) break;
+  }
+  if (!split_first && !split_last) return;
+  // Split tile rows: publish partials, one fence, one ticket per row; the last
+  // contributor of a row finishes it.
+  __threadfence();
+  __syncwarp();
+  uint32_t t_first = 0, t_last = 0;
+  if (lane == 0) {
+    if (split_first) t_first = atomicAdd(&p.counters[first_row * 8 + warp], 1u);
+    if (split_last) t_last = atomicAdd(&p.counters[last_row * 8 + warp], 1u);
+  }
+  t_first = __shfl_sync(0xffffffffu, t_first, 0);
+  t_last = __shfl_sync(0xffffffffu, t_last, 0);
+  bool fence_done = false;
+  if (split_first) {
+    const RowSplit rs = row_split(p, first_row, total, ctas);
+    if (t_first == rs.last - rs.first) {
+      __threadfence();
+      fence_done = true;
+      finish_split_row<NB>(p, first_row, rs, total, ctas, warp, lane);
+    }
+  }
+  if (split_last) {
+    const RowSplit rs = row_split(p, last_row, total, ctas);
+    if (t_last == rs.last - rs.first) {
+      if (!fence_done) __threadfence();
+      finish_split_row<NB>(p, last_row, rs, total, ctas, warp, lane);
     }
   }
 }
@@ -757,8 +855,25 @@ GemvKernel pick_kernel(uint32_t nb, uint32_t xl, bool simt) {
   return xl == 1 ? gemv_kernel<2, 1, false> : gemv_kernel<2, 2, false>;
 }
 
-uint32_t gemv_smem_bytes(uint32_t xslot) {
-  return (1u << kRingLog2) * kRecordBytes + kXRing * xslot + (2 * (1u << kRingLog2) + 2 * kXRing) * 8;
+struct RingShape {
+  uint32_t slots, stride, smem;
+};
+
+// Ring geometry: a slot holds one run of up to `cap` stages of a tile; enough slots to
+// keep about kUnitsInFlight tile-stages in flight within the shared-memory budget.
+RingShape ring_shape(uint32_t xslot, uint32_t cap) {
+  RingShape r{};
+  r.stride = static_cast<uint32_t>(round_up(kHdrBytes + xslot + cap * kRecordBytes, 16));
+  r.slots = std::max<uint32_t>(2, std::min<uint32_t>(std::max<uint32_t>(1, kUnitsInFlight / cap), kSmemBudget / r.stride));
+  r.smem = r.slots * r.stride + 2 * r.slots * 8;
+  return r;
+}
+
+uint32_t gemv_smem_cap() {
+  uint32_t m = 0;
+  for (uint32_t cap = 1; cap <= HQB_MAX_STAGES; ++cap)
+    m = std::max(m, ring_shape(xslot_bytes_for(HQB_MAX_BATCH, 2), cap).smem);
+  return std::max(m, kSmemBudget + 1024);
 }
 
 // Resident CTAs per SM for a kernel variant at a given shared-memory size (cached).
@@ -775,11 +890,19 @@ int ctas_per_sm(GemvKernel k, uint32_t smem, int device) {
   std::lock_guard<std::mutex> lock(mu);
   for (int i = 0; i < used; ++i)
     if (cache[i].k == k && cache[i].smem == smem && cache[i].device == device) return cache[i].ctas;
+  // The attribute is a per-kernel maximum: set it once to the largest size any batch
+  // needs, so a later smaller request can never lower it below a cached larger one.
+  const uint32_t smem_cap = gemv_smem_cap();
   if (cudaFuncSetAttribute(reinterpret_cast<const void*>(k), cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           static_cast<int>(smem)) != cudaSuccess)
+                           static_cast<int>(smem_cap)) != cudaSuccess) {
+    cudaGetLastError();
     return 0;
+  }
   int n = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k, kGemvThreads, smem) != cudaSuccess) return 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k, kGemvThreads, smem) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
   n = std::min<int>(n, kMaxCtasPerSm);
   if (used < 64) cache[used++] = Entry{k, smem, device, n};
   return n;
@@ -935,7 +1058,10 @@ HQB_API int hqb_gemv_ex(const hqb_plane_matrix* m, uint32_t prefix, const uint8_
   const uint8_t* xfrag = static_cast<const uint8_t*>(x);
   if (!x_prepared) {
     e = launch_prep(x, x_dtype, m->cols, batch, ws + L.xfrag, st);
-    if (e != cudaSuccess) return e;
+    if (e != cudaSuccess) {
+      cudaGetLastError();
+      return e;
+    }
     xfrag = ws + L.xfrag;
   }
   GemvParams p{};
@@ -960,12 +1086,15 @@ HQB_API int hqb_gemv_ex(const hqb_plane_matrix* m, uint32_t prefix, const uint8_
   const uint64_t tiles = static_cast<uint64_t>(m->grid_rows) * m->grid_cols;
   p.total = mixed ? 0 : tiles * prefix;
   const GemvKernel k = pick_kernel(batch > 8 ? 2 : 1, xl, simt);
-  const uint32_t smem = gemv_smem_bytes(p.xslot_bytes);
+  const RingShape rs = ring_shape(p.xslot_bytes, mixed ? m->stage_count : prefix);
+  p.ring_slots = rs.slots;
+  p.slot_stride = rs.stride;
+  p.shift_mul = 1u << 24;
+  const uint32_t smem = rs.smem;
   const int per_sm = ctas_per_sm(k, smem, device);
   if (per_sm <= 0) return cudaErrorLaunchOutOfResources;
   uint64_t grid = static_cast<uint64_t>(sms) * per_sm;
-  const uint64_t units = mixed ? tiles : p.total;  // mixed: at least one unit per tile
-  grid = std::max<uint64_t>(1, std::min<uint64_t>(grid, units));
+  if (!mixed) grid = std::max<uint64_t>(1, std::min<uint64_t>(grid, p.total));
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(static_cast<unsigned>(grid));
   cfg.blockDim = dim3(kGemvThreads);
@@ -979,7 +1108,10 @@ HQB_API int hqb_gemv_ex(const hqb_plane_matrix* m, uint32_t prefix, const uint8_
     cfg.numAttrs = 1;
   }
   e = cudaLaunchKernelEx(&cfg, k, p);
-  if (e != cudaSuccess) return e;
+  if (e != cudaSuccess) {
+    cudaGetLastError();  // do not leave a refused launch pending for the next call
+    return e;
+  }
   return cudaGetLastError();
 }
 

@@ -315,3 +315,36 @@ class RawMatrix:
                                            _ptr(x), x.shape[0], _ptr(bias), _ptr(y), _stream(stream)),
               "hqb_raw_linear_ordered")
         return y
+
+
+# ---- output-row sharding across ranks --------------------------------------------------
+
+def shard_rows(rows: int, world: int, rank: int) -> tuple[int, int]:
+    """Tile-row aligned contiguous output rows of one rank: (first row, row count).
+
+    Whole 128-row tiles are dealt out as evenly as possible, so every rank's shard is
+    itself a valid plane matrix and the ranks' slices tile [0, rows) exactly."""
+    if world < 1 or not 0 <= rank < world:
+        raise ValueError("invalid rank/world")
+    tiles = -(-rows // TILE)
+    t0, t1 = tiles * rank // world, tiles * (rank + 1) // world
+    r0, r1 = t0 * TILE, min(t1 * TILE, rows)
+    return r0, max(0, r1 - r0)
+
+
+def shard_pad_rows(rows: int, world: int) -> int:
+    """Per-rank slot size of the gathered output (the largest shard, whole tiles)."""
+    return -(-(-(-rows // TILE)) // world) * TILE
+
+
+def slice_stage_rows(codes, bits, cols: int, r0: int, nrows: int):
+    """Row-shard one matrix's reference-layout stages (codes row-major, scales
+    tile-row major): returns the (codes, fp16 bits) slices of rows [r0, r0+nrows)."""
+    kpad = -(-cols // TILE) * TILE
+    per_row = kpad // 4
+    nt = -(-nrows // TILE)
+    c = [x[r0 * per_row:(r0 + nt * TILE) * per_row] for x in codes]
+    per_tile_row = (kpad // TILE) * TILE
+    t0 = r0 // TILE
+    b = [x[t0 * per_tile_row:(t0 + nt) * per_tile_row] for x in bits]
+    return c, b

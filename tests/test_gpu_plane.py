@@ -160,7 +160,7 @@ def test_depth_plan_flags_bad_entries():
     depth = torch.tensor([[0, 2], [5, 1]], dtype=torch.uint8, device="cuda")
     plan = hqb.DepthPlan(depth, 4)
     assert int(plan.flags.item()) & hqb.DEVERR_DEPTH
-    assert plan.plan.cpu().tolist() == [0, 3, 5]  # clamped to [1, 4]
+    assert plan.plan.cpu().tolist() == [0, 3, 8]  # 0 -> 1 and 5 -> 4
 
 
 def test_repack_flags_bad_scales():
