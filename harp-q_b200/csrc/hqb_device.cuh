@@ -125,18 +125,6 @@ __device__ __forceinline__ float2 lds_f2(const void* p) {
   return v;
 }
 
-// Two signed int2 codes at position j (0..7) of each 16-bit half of w, as FP16
-// subnormals: half = (code + 2) · 4^(j%4) · 2^-24.  Positions 4..7 are read from
-// w >> 8 (pass it as `w_hi`).  One LOP3 per register.
-template <int J>
-__device__ __forceinline__ uint32_t int2_pair_subnormal(uint32_t w, uint32_t w_hi) {
-  constexpr int kShift = 2 * (J & 3);
-  constexpr uint32_t kMask = 0x00030003u << kShift;
-  constexpr uint32_t kFlip = 0x00020002u << kShift;
-  const uint32_t src = (J < 4) ? w : w_hi;
-  return (src & kMask) ^ kFlip;
-}
-
 __device__ __forceinline__ float half_bits_to_float(uint32_t bits16) {
   return __half2float(__ushort_as_half(static_cast<unsigned short>(bits16)));
 }

@@ -11,7 +11,8 @@
 // Plane record of one (tile, stage), HQB_TILE_RECORD_BYTES = 8 x 544:
 //   row block rb (tile rows 16rb..16rb+15) at rb*544:
 //     [0, 512)   32 slots of 16 B, slot t = 4g+q holds four 32-bit code words
-//                  w0 = row 16rb+g,   columns 32q..32q+15     (2 bits/code, LSB first)
+//                  w0 = row 16rb+g,   columns 32q..32q+15     (2 bits/code, LSB first,
+//                                                              stored as code + 2)
 //                  w1 = row 16rb+g+8, columns 32q..32q+15
 //                  w2 = row 16rb+g,   columns 32q+16..32q+31
 //                  w3 = row 16rb+g+8, columns 32q+16..32q+31
@@ -20,8 +21,8 @@
 //     [512, 544) 8 pairs {scale(row 16rb+g), scale(row 16rb+g+8)} as raw FP16 bits.
 //
 // Tensor-core decode: code pair j of each 16-bit half (positions 0..3 of w, 4..7 of
-// w >> 8) becomes the FP16 subnormal (code+2)·4^(j%4)·2^-24 with one LOP3 (mask, then
-// flip bit 1).  The B operand holds x·2^-e·4^-(j%4) (per-tile exponent e), so every
+// w >> 8) becomes the FP16 subnormal (code+2)·4^(j%4)·2^-24 with one AND (the plane
+// stores code + 2).  The B operand holds x·2^-e·4^-(j%4) (per-tile exponent e), so every
 // product is (code+2)·x·2^(-24-e) and the FP32 accumulator of one tile-stage is
 // 2^(-24-e)·Σ(code+2)·x.  The epilogue applies f = 2^(24+e), subtracts the
 // row-independent 2·Σx term and multiplies by the row's FP16 scale.
@@ -47,7 +48,7 @@ constexpr uint32_t kConsumerWarps = 8;
 constexpr uint32_t kGemvThreads = (kConsumerWarps + 1) * 32;
 constexpr uint32_t kUnitsInFlight = 12;     // tile-stages buffered per CTA (52 KB)
 constexpr uint32_t kSmemBudget = 100 * 1024;  // ring bytes per CTA, two CTAs per SM
-constexpr uint32_t kMaxCtasPerSm = 2;
+constexpr uint32_t kMaxCtasPerSm = 4;  // bound on resident CTAs per SM (sizes the partials)
 
 static_assert(kRecordBytes == 8 * kRowBlockBytes, "record = 8 row blocks");
 
@@ -59,7 +60,6 @@ struct GemvParams {
   const void* bias;
   void* y;
   float* partials;     // [G][2][batch][128]
-  uint32_t* counters;  // [R][8]
   int* error;
   uint64_t total;      // units (uniform); mixed reads plan[R]
   uint32_t rows;
@@ -71,6 +71,9 @@ struct GemvParams {
   uint32_t ring_slots;   // ring slots (runs) per CTA
   uint32_t slot_stride;  // header + activation fragments + max-run records
   uint32_t shift_mul;    // 2^24: w >> 8 computed as a high multiply
+  uint32_t pdl;          // launched as a programmatic dependent
+  uint32_t x_resident;   // all activation fragments staged once per CTA (else one per slot)
+  uint32_t slot_x_bytes; // activation bytes carried by each slot (0 when resident)
   int bias_dtype;
   int y_dtype;
 };
@@ -103,9 +106,11 @@ __global__ void __launch_bounds__(256) repack_kernel(const uint8_t* __restrict__
                    : (uint32_t)src[0] | ((uint32_t)src[1] << 8) | ((uint32_t)src[2] << 16) |
                          ((uint32_t)src[3] << 24);
       const uint32_t valid = cols - col0;
-      if (valid < 16) w &= (1u << (2 * valid)) - 1u;  // clear codes of padded columns
+      if (valid < 16) w &= (1u << (2 * valid)) - 1u;  // padded columns get code 0
     }
-    words[i] = w;
+    // Store every 2-bit field as (code + 2) in [0, 3] (two's-complement raw XOR 0b10):
+    // the tensor-core decode is then a single AND per register.
+    words[i] = w ^ 0xAAAAAAAAu;
   }
   uint8_t* rec = plane + static_cast<uint64_t>(tile) * kRecordBytes + rb * kRowBlockBytes;
   *reinterpret_cast<uint4*>(rec + lane * 16) = make_uint4(words[0], words[1], words[2], words[3]);
@@ -237,86 +242,124 @@ struct RunCursor {
 
 struct Ring {
   uint8_t* base;
+  uint8_t* xres;  // resident activation fragments (x_resident)
   uint64_t* full;
   uint64_t* empty;
+  uint64_t* xbar;
   uint32_t slots, stride;
 };
 
-__device__ void gemv_producer(const GemvParams& p, const Ring& ring, uint64_t u0, uint32_t n) {
+// The producer warp: lane 0 walks the schedule, writes the slot header and arms the
+// slot's barrier with the byte count; then lanes 0..len-1 issue one stage record each
+// and lane 31 the tile's activation fragments, so a slot costs one warp step rather
+// than a serial chain of copies on one thread.
+__device__ void gemv_producer(const GemvParams& p, const Ring& ring, uint64_t u0, uint32_t n, uint32_t lane) {
   const uint64_t stream_policy = policy_evict_first();
   const uint64_t keep_policy = policy_evict_last();
   RunCursor rc;
-  uint32_t k = 0;
-  if (!rc.init(u0, n, p)) {
-    atomicOr(p.error, HQB_DEVERR_DEPTH);
-    uint32_t* hdr = reinterpret_cast<uint32_t*>(ring.base);
-    hdr[0] = hdr[1] = 0;
-    hdr[2] = (kFlagLast | kFlagError) << 16;
-    mbar_arrive(&ring.full[0]);  // a header-only phase tells the consumers to stop
+  bool ok = true;
+  if (lane == 0) ok = rc.init(u0, n, p);
+  ok = __shfl_sync(0xffffffffu, ok, 0);
+  if (!ok) {
+    if (lane == 0) {
+      atomicOr(p.error, HQB_DEVERR_DEPTH);
+      uint32_t* hdr = reinterpret_cast<uint32_t*>(ring.base);
+      hdr[0] = hdr[1] = 0;
+      hdr[2] = (kFlagLast | kFlagError) << 16;
+      mbar_arrive(&ring.full[0]);  // a header-only phase tells the consumers to stop
+    }
     return;
   }
-  // Prologue: weight records do not depend on the preceding kernel (HQB_FLAG_PDL), so
-  // fill the ring with them before waiting for it; activations follow the wait.
-  uint32_t r, c, s0, s1, flags = 0;
-  bool last = false, ok = true;
-  for (; k < ring.slots && !last; ++k) {
-    uint8_t* slot = ring.base + k * ring.stride;
-    if (!rc.next(p, r, c, s0, s1, flags)) {
-      atomicOr(p.error, HQB_DEVERR_DEPTH);
-      flags = kFlagLast | kFlagError;
-      s1 = s0 = 0;
-      ok = false;
-    }
-    last = (flags & kFlagLast) != 0;
-    uint32_t* hdr = reinterpret_cast<uint32_t*>(slot);
-    hdr[0] = r;
-    hdr[1] = c;
-    hdr[2] = (s1 - s0) | (flags << 16);
-    mbar_expect_tx(&ring.full[k], ok ? p.xslot_bytes + (s1 - s0) * kRecordBytes : 0);
-    for (uint32_t s = s0; s < s1; ++s)
-      bulk_load(slot + kHdrBytes + p.xslot_bytes + (s - s0) * kRecordBytes,
-                p.planes[s] + (static_cast<uint64_t>(r) * p.C + c) * kRecordBytes, kRecordBytes, &ring.full[k],
-                stream_policy);
+  // With programmatic dependent launch the activation fragments may still be written
+  // by the preceding kernel: weight records go first, activations after the wait.
+  const bool defer_x = p.pdl != 0;
+  bool x_pending = defer_x;  // prologue activations not yet issued
+  if (p.x_resident && lane == 0) {
+    mbar_expect_tx(ring.xbar, static_cast<uint32_t>(p.C) * p.xslot_bytes);
+    if (!defer_x) bulk_load(ring.xres, p.xfrag, static_cast<uint32_t>(p.C) * p.xslot_bytes, ring.xbar, keep_policy);
   }
-  const uint32_t pre = k;
-  griddep_wait();
-  for (uint32_t j = 0; j < pre; ++j) {
-    uint8_t* slot = ring.base + j * ring.stride;
-    if ((reinterpret_cast<const uint32_t*>(slot)[2] >> 16) & kFlagError) break;  // header-only slot
-    const uint32_t cj = reinterpret_cast<const uint32_t*>(slot)[1];
-    bulk_load(slot + kHdrBytes, p.xfrag + static_cast<uint64_t>(cj) * p.xslot_bytes, p.xslot_bytes, &ring.full[j],
-              keep_policy);
-  }
-  while (!last && ok) {
+  __syncwarp();
+  uint32_t k = 0;
+  bool last = false;
+  while (!last) {
     const uint32_t i = k % ring.slots;
     uint8_t* slot = ring.base + i * ring.stride;
-    if (!mbar_wait(&ring.empty[i], ((k / ring.slots) - 1) & 1, p.error)) break;
-    uint32_t* hdr = reinterpret_cast<uint32_t*>(slot);
-    if (!rc.next(p, r, c, s0, s1, flags)) {
-      atomicOr(p.error, HQB_DEVERR_DEPTH);
-      hdr[2] = (kFlagLast | kFlagError) << 16;
-      mbar_arrive(&ring.full[i]);
-      ++k;
-      break;
+    if (k == ring.slots && x_pending) {
+      x_pending = false;
+      griddep_wait();
+      if (p.x_resident) {
+        if (lane == 0)
+          bulk_load(ring.xres, p.xfrag, static_cast<uint32_t>(p.C) * p.xslot_bytes, ring.xbar, keep_policy);
+      } else
+      for (uint32_t j = lane; j < ring.slots; j += 32) {  // activations of the prologue slots
+        uint8_t* sj = ring.base + j * ring.stride;
+        const uint32_t* hj = reinterpret_cast<const uint32_t*>(sj);
+        if ((hj[2] >> 16) & kFlagError) continue;
+        bulk_load(sj + kHdrBytes, p.xfrag + static_cast<uint64_t>(hj[1]) * p.xslot_bytes, p.xslot_bytes,
+                  &ring.full[j], keep_policy);
+      }
     }
+    uint32_t r = 0, c = 0, s0 = 0, s1 = 0, flags = 0;
+    bool waited = true, valid = true;
+    if (lane == 0) {
+      if (k >= ring.slots) waited = mbar_wait(&ring.empty[i], ((k / ring.slots) - 1) & 1, p.error);
+      if (waited) {
+        valid = rc.next(p, r, c, s0, s1, flags);
+        uint32_t* hdr = reinterpret_cast<uint32_t*>(slot);
+        if (!valid) {
+          atomicOr(p.error, HQB_DEVERR_DEPTH);
+          flags = kFlagLast | kFlagError;
+          s0 = s1 = 0;
+        }
+        hdr[0] = r;
+        hdr[1] = c;
+        hdr[2] = (s1 - s0) | (flags << 16);
+        mbar_expect_tx(&ring.full[i], valid ? p.slot_x_bytes + (s1 - s0) * kRecordBytes : 0);
+      }
+    }
+    waited = __shfl_sync(0xffffffffu, waited, 0);
+    if (!waited) break;
+    r = __shfl_sync(0xffffffffu, r, 0);
+    c = __shfl_sync(0xffffffffu, c, 0);
+    s0 = __shfl_sync(0xffffffffu, s0, 0);
+    s1 = __shfl_sync(0xffffffffu, s1, 0);
+    flags = __shfl_sync(0xffffffffu, flags, 0);
+    valid = (flags & kFlagError) == 0;
     last = (flags & kFlagLast) != 0;
-    hdr[0] = r;
-    hdr[1] = c;
-    hdr[2] = (s1 - s0) | (flags << 16);
-    mbar_expect_tx(&ring.full[i], p.xslot_bytes + (s1 - s0) * kRecordBytes);
-    bulk_load(slot + kHdrBytes, p.xfrag + static_cast<uint64_t>(c) * p.xslot_bytes, p.xslot_bytes, &ring.full[i],
-              keep_policy);
-    for (uint32_t s = s0; s < s1; ++s)
-      bulk_load(slot + kHdrBytes + p.xslot_bytes + (s - s0) * kRecordBytes,
-                p.planes[s] + (static_cast<uint64_t>(r) * p.C + c) * kRecordBytes, kRecordBytes, &ring.full[i],
-                stream_policy);
+    __syncwarp();  // the barrier is armed before any copy can complete on it
+    if (valid) {
+      if (lane < s1 - s0)
+        bulk_load(slot + kHdrBytes + p.slot_x_bytes + lane * kRecordBytes,
+                  p.planes[s0 + lane] + (static_cast<uint64_t>(r) * p.C + c) * kRecordBytes, kRecordBytes,
+                  &ring.full[i], stream_policy);
+      if (lane == 31 && !x_pending && !p.x_resident)
+        bulk_load(slot + kHdrBytes, p.xfrag + static_cast<uint64_t>(c) * p.xslot_bytes, p.xslot_bytes,
+                  &ring.full[i], keep_policy);
+    }
     ++k;
   }
-  griddep_launch_dependents();
+  if (x_pending) {  // schedules of at most ring.slots runs end before the wait above
+    x_pending = false;
+    griddep_wait();
+    if (p.x_resident) {
+      if (lane == 0)
+        bulk_load(ring.xres, p.xfrag, static_cast<uint32_t>(p.C) * p.xslot_bytes, ring.xbar, keep_policy);
+    } else
+    for (uint32_t j = lane; j < k; j += 32) {
+      uint8_t* sj = ring.base + j * ring.stride;
+      const uint32_t* hj = reinterpret_cast<const uint32_t*>(sj);
+      if ((hj[2] >> 16) & kFlagError) continue;
+      bulk_load(sj + kHdrBytes, p.xfrag + static_cast<uint64_t>(hj[1]) * p.xslot_bytes, p.xslot_bytes, &ring.full[j],
+                keep_policy);
+    }
+  }
   // Every bulk copy this CTA issued must land before the CTA may exit, whatever path
   // led here (consumers may have left early on an error).
-  for (uint32_t j = k > ring.slots ? k - ring.slots : 0; j < k; ++j)
-    mbar_wait(&ring.full[j % ring.slots], (j / ring.slots) & 1, p.error);
+  if (lane == 0) {
+    for (uint32_t j = k > ring.slots ? k - ring.slots : 0; j < k; ++j)
+      mbar_wait(&ring.full[j % ring.slots], (j / ring.slots) & 1, p.error);
+    if (p.x_resident) mbar_wait(ring.xbar, 0, p.error);
+  }
 }
 
 template <int NB>
@@ -372,35 +415,6 @@ __device__ __forceinline__ void publish_partial(const GemvParams& p, uint32_t ct
     }
 }
 
-// Last arriver of a split tile row: sum the contributions in CTA order, add bias, store.
-template <int NB>
-__device__ void finish_split_row(const GemvParams& p, uint32_t r, RowSplit rs, uint64_t total, uint32_t ctas,
-                                 uint32_t warp, uint32_t lane) {
-  const uint64_t per_row = static_cast<uint64_t>(p.C) * p.prefix;
-  const uint32_t q = lane & 3, rit0 = warp * 16 + (lane >> 2);
-  float sum[NB][4];
-#pragma unroll
-  for (int nb = 0; nb < NB; ++nb)
-#pragma unroll
-    for (int e = 0; e < 4; ++e) sum[nb][e] = 0.0f;
-  for (uint32_t i = rs.first; i <= rs.last; ++i) {
-    const uint32_t ki = row_of_unit(unit_start(i, total, ctas), p.plan, p.R, per_row) == r ? 0 : 1;
-    const float* src = p.partials + static_cast<uint64_t>(i * 2 + ki) * p.batch * 128;
-#pragma unroll
-    for (int nb = 0; nb < NB; ++nb)
-#pragma unroll
-      for (int j = 0; j < 2; ++j) {
-        const uint32_t b = 2 * q + j + 8 * nb;
-        if (b < p.batch) {
-          sum[nb][j] += __ldcg(src + b * 128 + rit0);
-          sum[nb][2 + j] += __ldcg(src + b * 128 + rit0 + 8);
-        }
-      }
-  }
-  store_out<NB>(p, sum, r * 128 + rit0, q);
-  if (lane == 0) p.counters[r * 8 + warp] = 0;  // cleared for the next launch
-}
-
 // Activation fragments of one tile for this lane (batch rows g and g+8).
 template <int NB, int XL>
 struct XFrag {
@@ -441,9 +455,10 @@ struct XFrag {
   }
 };
 
+// Code pair m (position m of each 16-bit half) as two FP16 subnormals (code+2)·4^(m%4)·2^-24:
+// the plane stores code+2, so one AND extracts both.
 __device__ __forceinline__ uint32_t int2_pair(uint32_t w, uint32_t w_hi, int m) {
-  const int sh = 2 * (m & 3);
-  return (((m < 4) ? w : w_hi) & (0x00030003u << sh)) ^ (0x00020002u << sh);
+  return ((m < 4) ? w : w_hi) & (0x00030003u << (2 * (m & 3)));
 }
 
 // LEN stages of one tile through the tensor cores: LEN independent accumulator chains.
@@ -523,8 +538,8 @@ __device__ __forceinline__ void simt_unit(const GemvParams& p, const uint8_t* xs
       const float xv = half_bits_to_float(hb) * static_cast<float>(1 << (2 * (m & 3)));
       const uint32_t wg = i < 16 ? w.x : w.z, wh = i < 16 ? w.y : w.w;
       const int sh = 2 * (i & 15);
-      const float cg = __uint_as_float(0x4B000000u | (((wg >> sh) & 3u) ^ 2u)) - 8388610.0f;
-      const float ch = __uint_as_float(0x4B000000u | (((wh >> sh) & 3u) ^ 2u)) - 8388610.0f;
+      const float cg = __uint_as_float(0x4B000000u | ((wg >> sh) & 3u)) - 8388610.0f;
+      const float ch = __uint_as_float(0x4B000000u | ((wh >> sh) & 3u)) - 8388610.0f;
       d0 = fmaf(cg, xv, d0);
       d1 = fmaf(ch, xv, d1);
     }
@@ -563,13 +578,14 @@ __device__ __forceinline__ void simt_finish(float (&part)[2][8], float (&y)[1][4
 }
 
 template <int NB, int XL, bool SIMT>
-__global__ void __launch_bounds__(kGemvThreads, (NB == 1 && XL == 1 && !SIMT) ? kMaxCtasPerSm : 1)
+__global__ void __launch_bounds__(kGemvThreads, (NB == 1 && XL == 1 && !SIMT) ? 2 : 1)
     gemv_kernel(const __grid_constant__ GemvParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   const uint64_t total = p.plan != nullptr ? static_cast<uint64_t>(p.plan[p.R]) : p.total;
   // Mixed depth launches the full grid (the unit count lives on the device); both
   // modes partition over min(grid, units) CTAs so equal unit counts split equally.
   const uint32_t ctas = static_cast<uint32_t>(total < gridDim.x ? total : gridDim.x), cta = blockIdx.x;
+  griddep_launch_dependents();  // the split-row fix-up may be scheduled; it waits for this grid
   if (cta >= ctas) return;
   const uint64_t u0 = unit_start(cta, total, ctas), u1 = unit_start(cta + 1, total, ctas);
   const uint32_t n = static_cast<uint32_t>(u1 - u0);
@@ -578,20 +594,23 @@ __global__ void __launch_bounds__(kGemvThreads, (NB == 1 && XL == 1 && !SIMT) ? 
   ring.base = smem;
   ring.slots = p.ring_slots;
   ring.stride = p.slot_stride;
-  ring.full = reinterpret_cast<uint64_t*>(smem + ring.slots * ring.stride);
+  ring.xres = smem + ring.slots * ring.stride;
+  ring.full = reinterpret_cast<uint64_t*>(ring.xres + (p.x_resident ? p.C * p.xslot_bytes : 0));
   ring.empty = ring.full + ring.slots;
+  ring.xbar = ring.empty + ring.slots;
   const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
     for (uint32_t i = 0; i < ring.slots; ++i) {
       mbar_init(&ring.full[i], 1);
       mbar_init(&ring.empty[i], kConsumerWarps * 32);
     }
+    mbar_init(ring.xbar, 1);
     fence_barrier_init();
   }
   __syncthreads();
 
   if (warp == kConsumerWarps) {
-    if (lane == 0) gemv_producer(p, ring, u0, n);
+    gemv_producer(p, ring, u0, n, lane);
     return;
   }
 
@@ -610,9 +629,8 @@ __global__ void __launch_bounds__(kGemvThreads, (NB == 1 && XL == 1 && !SIMT) ? 
 #pragma unroll
       for (int b = 0; b < 8; ++b) part[h][b] = 0.0f;
   }
-  bool split_first = false, split_last = false;
-  uint32_t last_row = first_row;
   griddep_wait();
+  if (p.x_resident && !mbar_wait(ring.xbar, 0, p.error)) return;
   for (uint32_t k = 0;; ++k) {
     const uint32_t i = k % ring.slots;
     if (!mbar_wait(&ring.full[i], (k / ring.slots) & 1, p.error)) return;
@@ -623,8 +641,8 @@ __global__ void __launch_bounds__(kGemvThreads, (NB == 1 && XL == 1 && !SIMT) ? 
       mbar_arrive(&ring.empty[i]);
       return;
     }
-    const uint8_t* xs = slot + kHdrBytes;
-    const uint8_t* rec = xs + p.xslot_bytes + warp * kRowBlockBytes;
+    const uint8_t* xs = p.x_resident ? ring.xres + hdr.y * p.xslot_bytes : slot + kHdrBytes;
+    const uint8_t* rec = slot + kHdrBytes + p.slot_x_bytes + warp * kRowBlockBytes;
     uint4 w[HQB_MAX_STAGES];
     uint32_t sc[HQB_MAX_STAGES];
 #pragma unroll
@@ -655,15 +673,10 @@ __global__ void __launch_bounds__(kGemvThreads, (NB == 1 && XL == 1 && !SIMT) ? 
       const uint32_t r = hdr.x;
       const RowSplit rs = row_split(p, r, total, ctas);
       if (rs.first == rs.last) {
-        store_out<NB>(p, y, r * 128 + rit0, q);  // the whole tile row is this CTA's: no fix-up
-      } else if (r == first_row && !split_first) {
-        // Plain stores now; the fence and the arrival ticket wait for the CTA's end so
-        // no fence stalls the stream.
-        split_first = true;
-        publish_partial<NB>(p, cta, 0, y, rit0, q);
+        store_out<NB>(p, y, r * 128 + rit0, q);  // the whole tile row is this CTA's
       } else {
-        split_last = true;
-        last_row = r;
+        // A split row: plain stores of this CTA's part; fixup_kernel adds the parts in
+        // CTA order once the whole grid has finished (no fence or atomic here).
         publish_partial<NB>(p, cta, r == first_row ? 0 : 1, y, rit0, q);
       }
 #pragma unroll
@@ -673,33 +686,203 @@ __global__ void __launch_bounds__(kGemvThreads, (NB == 1 && XL == 1 && !SIMT) ? 
     }
     if (flags & kFlagLast) break;
   }
-  if (!split_first && !split_last) return;
-  // Split tile rows: publish partials, one fence, one ticket per row; the last
-  // contributor of a row finishes it.
-  __threadfence();
-  __syncwarp();
-  uint32_t t_first = 0, t_last = 0;
-  if (lane == 0) {
-    if (split_first) t_first = atomicAdd(&p.counters[first_row * 8 + warp], 1u);
-    if (split_last) t_last = atomicAdd(&p.counters[last_row * 8 + warp], 1u);
+}
+
+// --------------------------------------------------------------------------------------
+// Streaming GEMV (the batch <= 16 path whenever the activation fragments of a whole
+// row fit in shared memory).  No producer warp and no ring: warp w owns rows
+// 16w..16w+15 of every tile in the CTA's unit range and loads its own 544-byte
+// row-block of each tile-stage straight into registers, kPrefetch units ahead, with
+// 16-byte non-caching global loads.  The CTA's activation fragments are staged in
+// shared memory once.  Partition, row flush and split-row fix-up are the ring kernel's.
+
+constexpr int kPrefetch = 4;
+constexpr uint32_t kStreamThreads = kConsumerWarps * 32;
+
+struct UnitCursor {
+  uint32_t r, c, s, d;
+
+  __device__ bool init(uint64_t u, const GemvParams& p) {
+    if (p.plan == nullptr) {
+      const uint64_t per_row = static_cast<uint64_t>(p.C) * p.prefix;
+      r = static_cast<uint32_t>(u / per_row);
+      const uint64_t rem = u - static_cast<uint64_t>(r) * per_row;
+      c = static_cast<uint32_t>(rem / p.prefix);
+      s = static_cast<uint32_t>(rem - static_cast<uint64_t>(c) * p.prefix);
+      d = p.prefix;
+      return true;
+    }
+    r = row_of_unit(u, p.plan, p.R, 0);
+    uint64_t off = u - p.plan[r];
+    for (c = 0; c < p.C; ++c) {
+      d = clamp_depth(p.depth[static_cast<uint64_t>(r) * p.C + c], p.stage_count);
+      if (off < d) {
+        s = static_cast<uint32_t>(off);
+        return true;
+      }
+      off -= d;
+    }
+    return false;
   }
-  t_first = __shfl_sync(0xffffffffu, t_first, 0);
-  t_last = __shfl_sync(0xffffffffu, t_last, 0);
-  bool fence_done = false;
-  if (split_first) {
-    const RowSplit rs = row_split(p, first_row, total, ctas);
-    if (t_first == rs.last - rs.first) {
-      __threadfence();
-      fence_done = true;
-      finish_split_row<NB>(p, first_row, rs, total, ctas, warp, lane);
+
+  __device__ __forceinline__ void advance(const GemvParams& p) {
+    if (++s < d) return;
+    s = 0;
+    if (++c == p.C) {
+      c = 0;
+      ++r;
+    }
+    if (p.plan != nullptr && r < p.R) d = clamp_depth(p.depth[static_cast<uint64_t>(r) * p.C + c], p.stage_count);
+  }
+};
+
+// This lane's 16 code bytes and scale pair of one tile-stage (read once: no L1 allocation).
+__device__ __forceinline__ void load_unit(const GemvParams& p, const UnitCursor& u, uint32_t warp, uint32_t lane,
+                                          uint4& w, uint32_t& sc) {
+  const uint8_t* rec =
+      p.planes[u.s] + (static_cast<uint64_t>(u.r) * p.C + u.c) * kRecordBytes + warp * kRowBlockBytes;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(w.x), "=r"(w.y), "=r"(w.z), "=r"(w.w)
+               : "l"(rec + lane * 16));
+  asm volatile("ld.global.nc.L1::no_allocate.u32 %0, [%1];" : "=r"(sc) : "l"(rec + 512 + (lane >> 2) * 4));
+}
+
+template <int NB, int XL>
+__device__ __forceinline__ void mma_unit(const XFrag<NB, XL>& xf, const uint4 w, uint32_t sc, uint32_t shift_mul,
+                                         float (&y)[NB][4]) {
+  const uint32_t h0 = __umulhi(w.x, shift_mul), h1 = __umulhi(w.y, shift_mul);
+  const uint32_t h2 = __umulhi(w.z, shift_mul), h3 = __umulhi(w.w, shift_mul);
+  float acc[NB][4];
+#pragma unroll
+  for (int nb = 0; nb < NB; ++nb)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) acc[nb][e] = 0.0f;
+#pragma unroll
+  for (int m = 0; m < 8; ++m) {
+    const uint32_t a0 = int2_pair(w.x, h0, m), a1 = int2_pair(w.y, h1, m);
+    const uint32_t a2 = int2_pair(w.z, h2, m), a3 = int2_pair(w.w, h3, m);
+#pragma unroll
+    for (int nb = 0; nb < NB; ++nb)
+#pragma unroll
+      for (int l = 0; l < XL; ++l) mma_f16(acc[nb], a0, a1, a2, a3, xf.bf[nb][l][m][0], xf.bf[nb][l][m][1]);
+  }
+  const __half2 s2 = *reinterpret_cast<const __half2*>(&sc);
+  const float s_lo = __low2float(s2), s_hi = __high2float(s2);
+#pragma unroll
+  for (int nb = 0; nb < NB; ++nb) {
+    y[nb][0] = fmaf(s_lo, fmaf(acc[nb][0], xf.f[nb][0], -xf.gsum[nb][0]), y[nb][0]);
+    y[nb][1] = fmaf(s_lo, fmaf(acc[nb][1], xf.f[nb][1], -xf.gsum[nb][1]), y[nb][1]);
+    y[nb][2] = fmaf(s_hi, fmaf(acc[nb][2], xf.f[nb][0], -xf.gsum[nb][0]), y[nb][2]);
+    y[nb][3] = fmaf(s_hi, fmaf(acc[nb][3], xf.f[nb][1], -xf.gsum[nb][1]), y[nb][3]);
+  }
+}
+
+template <int NB, int XL>
+__global__ void __launch_bounds__(kStreamThreads, (NB == 1 && XL == 1) ? 2 : 1)
+    gemv_stream_kernel(const __grid_constant__ GemvParams p) {
+  extern __shared__ __align__(16) uint8_t xres[];  // activation fragments, indexed by tile column
+  const uint64_t total = p.plan != nullptr ? static_cast<uint64_t>(p.plan[p.R]) : p.total;
+  const uint32_t ctas = static_cast<uint32_t>(total < gridDim.x ? total : gridDim.x), cta = blockIdx.x;
+  griddep_launch_dependents();  // the split-row fix-up may be scheduled; it waits for this grid
+  if (cta >= ctas) return;
+  const uint64_t u0 = unit_start(cta, total, ctas), u1 = unit_start(cta + 1, total, ctas);
+  const uint32_t n = static_cast<uint32_t>(u1 - u0);
+  const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, q = lane & 3;
+  const uint32_t rit0 = warp * 16 + g;
+
+  UnitCursor fetch, cons, lastu;
+  if (!fetch.init(u0, p) || !lastu.init(u1 - 1, p)) {
+    if (threadIdx.x == 0) atomicOr(p.error, HQB_DEVERR_DEPTH);
+    return;
+  }
+  cons = fetch;
+  // Weight records do not depend on the preceding kernel: start them before the wait.
+  uint4 w[kPrefetch];
+  uint32_t sc[kPrefetch];
+#pragma unroll
+  for (int j = 0; j < kPrefetch; ++j) {
+    if (static_cast<uint32_t>(j) < n) {
+      load_unit(p, fetch, warp, lane, w[j], sc[j]);
+      fetch.advance(p);
     }
   }
-  if (split_last) {
-    const RowSplit rs = row_split(p, last_row, total, ctas);
-    if (t_last == rs.last - rs.first) {
-      if (!fence_done) __threadfence();
-      finish_split_row<NB>(p, last_row, rs, total, ctas, warp, lane);
+  griddep_wait();
+  // Activation fragments of the tile columns this CTA touches (all of them when its
+  // range crosses a tile row).
+  {
+    const uint32_t c_lo = cons.r == lastu.r ? cons.c : 0, c_hi = cons.r == lastu.r ? lastu.c : p.C - 1;
+    const uint4* src = reinterpret_cast<const uint4*>(p.xfrag + static_cast<uint64_t>(c_lo) * p.xslot_bytes);
+    uint4* dst = reinterpret_cast<uint4*>(xres + c_lo * p.xslot_bytes);
+    const uint32_t chunks = (c_hi - c_lo + 1) * p.xslot_bytes / 16;
+    for (uint32_t t = threadIdx.x; t < chunks; t += kStreamThreads) dst[t] = __ldcg(src + t);
+  }
+  __syncthreads();
+
+  const uint64_t per_row = static_cast<uint64_t>(p.C) * p.prefix;
+  const uint32_t first_row = row_of_unit(u0, p.plan, p.R, per_row);
+  float y[NB][4];
+#pragma unroll
+  for (int nb = 0; nb < NB; ++nb)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) y[nb][e] = 0.0f;
+  XFrag<NB, XL> xf;
+  uint32_t x_col = 0xFFFFFFFFu;
+  for (uint32_t i = 0; i < n; i += kPrefetch) {
+#pragma unroll
+    for (int j = 0; j < kPrefetch; ++j) {
+      if (i + j >= n) break;
+      if (cons.c != x_col) {
+        xf.load(p, xres + cons.c * p.xslot_bytes, lane);
+        x_col = cons.c;
+      }
+      mma_unit<NB, XL>(xf, w[j], sc[j], p.shift_mul, y);
+      if (i + j + kPrefetch < n) {
+        load_unit(p, fetch, warp, lane, w[j], sc[j]);
+        fetch.advance(p);
+      }
+      const uint32_t r = cons.r;
+      cons.advance(p);
+      if (i + j + 1 == n || cons.r != r) {
+        const RowSplit rs = row_split(p, r, total, ctas);
+        if (rs.first == rs.last) store_out<NB>(p, y, r * 128 + rit0, q);
+        else publish_partial<NB>(p, cta, r == first_row ? 0 : 1, y, rit0, q);
+#pragma unroll
+        for (int nb = 0; nb < NB; ++nb)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) y[nb][e] = 0.0f;
+      }
     }
+  }
+}
+
+// Split tile rows: the parts of the contributing CTAs, summed in CTA order, plus
+// bias.  Launched as a programmatic dependent of the GEMV; griddepcontrol.wait makes
+// the GEMV's stores visible.  One block per tile row; whole rows exit at once.
+__global__ void __launch_bounds__(256) fixup_kernel(const __grid_constant__ GemvParams p, uint32_t grid) {
+  griddep_wait();
+  griddep_launch_dependents();
+  const uint64_t total = p.plan != nullptr ? static_cast<uint64_t>(p.plan[p.R]) : p.total;
+  const uint32_t ctas = static_cast<uint32_t>(total < grid ? total : grid);
+  const uint32_t r = blockIdx.x;
+  if (r >= p.R || total == 0) return;
+  const RowSplit rs = row_split(p, r, total, ctas);
+  if (rs.first == rs.last) return;
+  const uint64_t per_row = static_cast<uint64_t>(p.C) * p.prefix;
+  for (uint32_t e = threadIdx.x; e < p.batch * 128; e += blockDim.x) {
+    const uint32_t b = e >> 7, rit = e & 127;
+    const uint32_t row = r * 128 + rit;
+    if (row >= p.rows) continue;
+    float sum = 0.0f;
+    for (uint32_t i = rs.first; i <= rs.last; ++i) {
+      const uint32_t ki = row_of_unit(unit_start(i, total, ctas), p.plan, p.R, per_row) == r ? 0 : 1;
+      sum += p.partials[(static_cast<uint64_t>(i * 2 + ki) * p.batch + b) * 128 + rit];
+    }
+    if (p.bias != nullptr)
+      sum += p.bias_dtype == HQB_F16 ? __half2float(static_cast<const __half*>(p.bias)[row])
+                                     : static_cast<const float*>(p.bias)[row];
+    const uint64_t o = static_cast<uint64_t>(b) * p.rows + row;
+    if (p.y_dtype == HQB_F16) static_cast<__half*>(p.y)[o] = __float2half_rn(sum);
+    else static_cast<float*>(p.y)[o] = sum;
   }
 }
 
@@ -742,8 +925,7 @@ __global__ void __launch_bounds__(256) decode_kernel(hqb_plane_matrix m, uint32_
 #pragma unroll
       for (uint32_t s = 0; s < HQB_MAX_STAGES; ++s) {
         if (s >= d) break;
-        const uint32_t raw = (words[s][i] >> (2 * k)) & 3u;
-        const float code = static_cast<float>(raw >= 2 ? static_cast<int>(raw) - 4 : static_cast<int>(raw));
+        const float code = static_cast<float>(static_cast<int>((words[s][i] >> (2 * k)) & 3u) - 2);
         wsum = __fadd_rn(wsum, __fmul_rn(code, sc[s][i & 1]));
       }
       out[row * m.cols + col0 + k] = wsum;
@@ -819,13 +1001,14 @@ int device_sm_count(int device) {
 namespace {
 
 struct WsLayout {
-  uint64_t counters, partials, xfrag, total;
+  uint64_t partials, xfrag, total;
 };
 
+// [error word][split-row partials: G x 2 x batch x 128 FP32][prepared activations]
 WsLayout ws_layout(uint32_t R, uint32_t C, uint32_t batch, uint32_t xl, int sms) {
+  (void)R;
   WsLayout L{};
-  L.counters = 256;
-  L.partials = L.counters + round_up(static_cast<uint64_t>(R) * 8 * 4, 256);
+  L.partials = 256;
   const uint64_t gmax = static_cast<uint64_t>(sms) * kMaxCtasPerSm;
   L.xfrag = L.partials + round_up(gmax * 2 * batch * 128 * 4, 256);
   L.total = L.xfrag + round_up(static_cast<uint64_t>(C) * xslot_bytes_for(batch, xl), 256);
@@ -849,6 +1032,11 @@ bool stage_planes_ok(const hqb_plane_matrix* m, uint32_t needed) {
 
 using GemvKernel = void (*)(GemvParams);
 
+GemvKernel pick_stream_kernel(uint32_t nb, uint32_t xl) {
+  if (nb == 1) return xl == 1 ? gemv_stream_kernel<1, 1> : gemv_stream_kernel<1, 2>;
+  return xl == 1 ? gemv_stream_kernel<2, 1> : gemv_stream_kernel<2, 2>;
+}
+
 GemvKernel pick_kernel(uint32_t nb, uint32_t xl, bool simt) {
   if (simt) return gemv_kernel<1, 1, true>;
   if (nb == 1) return xl == 1 ? gemv_kernel<1, 1, false> : gemv_kernel<1, 2, false>;
@@ -861,23 +1049,29 @@ struct RingShape {
 
 // Ring geometry: a slot holds one run of up to `cap` stages of a tile; enough slots to
 // keep about kUnitsInFlight tile-stages in flight within the shared-memory budget.
-RingShape ring_shape(uint32_t xslot, uint32_t cap) {
+// slot_x: activation bytes per slot (0 when the whole activation set is resident);
+// resident: bytes of that set.
+RingShape ring_shape(uint32_t slot_x, uint32_t cap, uint32_t resident) {
   RingShape r{};
-  r.stride = static_cast<uint32_t>(round_up(kHdrBytes + xslot + cap * kRecordBytes, 16));
+  r.stride = static_cast<uint32_t>(round_up(kHdrBytes + slot_x + cap * kRecordBytes, 16));
   r.slots = std::max<uint32_t>(2, std::min<uint32_t>(std::max<uint32_t>(1, kUnitsInFlight / cap), kSmemBudget / r.stride));
-  r.smem = r.slots * r.stride + 2 * r.slots * 8;
+  r.smem = r.slots * r.stride + resident + (2 * r.slots + 1) * 8;
   return r;
 }
+
+constexpr uint32_t kXResidentMax = 64 * 1024;
 
 uint32_t gemv_smem_cap() {
   uint32_t m = 0;
   for (uint32_t cap = 1; cap <= HQB_MAX_STAGES; ++cap)
-    m = std::max(m, ring_shape(xslot_bytes_for(HQB_MAX_BATCH, 2), cap).smem);
+    m = std::max(m, ring_shape(xslot_bytes_for(HQB_MAX_BATCH, 2), cap, 0).smem);
+  for (uint32_t cap = 1; cap <= HQB_MAX_STAGES; ++cap)
+    m = std::max(m, ring_shape(0, cap, kXResidentMax).smem);
   return std::max(m, kSmemBudget + 1024);
 }
 
 // Resident CTAs per SM for a kernel variant at a given shared-memory size (cached).
-int ctas_per_sm(GemvKernel k, uint32_t smem, int device) {
+int ctas_per_sm(GemvKernel k, uint32_t smem, int device, uint32_t threads) {
   struct Entry {
     GemvKernel k;
     uint32_t smem;
@@ -899,7 +1093,7 @@ int ctas_per_sm(GemvKernel k, uint32_t smem, int device) {
     return 0;
   }
   int n = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k, kGemvThreads, smem) != cudaSuccess) {
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k, static_cast<int>(threads), smem) != cudaSuccess) {
     cudaGetLastError();
     return 0;
   }
@@ -1072,7 +1266,6 @@ HQB_API int hqb_gemv_ex(const hqb_plane_matrix* m, uint32_t prefix, const uint8_
   p.bias = bias;
   p.y = y;
   p.error = reinterpret_cast<int*>(ws);
-  p.counters = reinterpret_cast<uint32_t*>(ws + L.counters);
   p.partials = reinterpret_cast<float*>(ws + L.partials);
   p.rows = static_cast<uint32_t>(m->rows);
   p.R = m->grid_rows;
@@ -1085,19 +1278,28 @@ HQB_API int hqb_gemv_ex(const hqb_plane_matrix* m, uint32_t prefix, const uint8_
   p.y_dtype = y_dtype;
   const uint64_t tiles = static_cast<uint64_t>(m->grid_rows) * m->grid_cols;
   p.total = mixed ? 0 : tiles * prefix;
-  const GemvKernel k = pick_kernel(batch > 8 ? 2 : 1, xl, simt);
-  const RingShape rs = ring_shape(p.xslot_bytes, mixed ? m->stage_count : prefix);
+  const bool streaming = !simt && static_cast<uint64_t>(m->grid_cols) * p.xslot_bytes <= kXResidentMax &&
+                         !(flags & HQB_FLAG_RING);
+  const GemvKernel k =
+      streaming ? pick_stream_kernel(batch > 8 ? 2 : 1, xl) : pick_kernel(batch > 8 ? 2 : 1, xl, simt);
+  const uint64_t x_all = static_cast<uint64_t>(m->grid_cols) * p.xslot_bytes;
+  p.x_resident = x_all <= kXResidentMax ? 1u : 0u;
+  p.slot_x_bytes = p.x_resident ? 0u : p.xslot_bytes;
+  const RingShape rs = ring_shape(p.slot_x_bytes, mixed ? m->stage_count : prefix,
+                                  p.x_resident ? static_cast<uint32_t>(x_all) : 0u);
   p.ring_slots = rs.slots;
   p.slot_stride = rs.stride;
   p.shift_mul = 1u << 24;
-  const uint32_t smem = rs.smem;
-  const int per_sm = ctas_per_sm(k, smem, device);
+  p.pdl = (flags & HQB_FLAG_PDL) ? 1u : 0u;
+  const uint32_t smem = streaming ? static_cast<uint32_t>(x_all) : rs.smem;
+  const uint32_t threads = streaming ? kStreamThreads : kGemvThreads;
+  const int per_sm = ctas_per_sm(k, smem, device, threads);
   if (per_sm <= 0) return cudaErrorLaunchOutOfResources;
   uint64_t grid = static_cast<uint64_t>(sms) * per_sm;
   if (!mixed) grid = std::max<uint64_t>(1, std::min<uint64_t>(grid, p.total));
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(static_cast<unsigned>(grid));
-  cfg.blockDim = dim3(kGemvThreads);
+  cfg.blockDim = dim3(threads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
@@ -1111,6 +1313,20 @@ HQB_API int hqb_gemv_ex(const hqb_plane_matrix* m, uint32_t prefix, const uint8_
   if (e != cudaSuccess) {
     cudaGetLastError();  // do not leave a refused launch pending for the next call
     return e;
+  }
+  // Split tile rows exist whenever more than one CTA shares the work.
+  if (mixed || std::min<uint64_t>(grid, p.total) > 1) {
+    cudaLaunchConfig_t fc{};
+    fc.gridDim = dim3(m->grid_rows);
+    fc.blockDim = dim3(256);
+    fc.stream = st;
+    fc.attrs = attr;
+    fc.numAttrs = 1;
+    e = cudaLaunchKernelEx(&fc, fixup_kernel, p, static_cast<uint32_t>(grid));
+    if (e != cudaSuccess) {
+      cudaGetLastError();
+      return e;
+    }
   }
   return cudaGetLastError();
 }

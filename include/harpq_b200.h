@@ -44,6 +44,7 @@ extern "C" {
 /* hqb_gemv_ex flags */
 #define HQB_FLAG_PDL 1u  /* launch with programmatic dependent launch (see hqb_gemv_ex) */
 #define HQB_FLAG_SIMT 2u /* CUDA-core decode+FFMA consumer instead of tensor-core mma */
+#define HQB_FLAG_RING 4u /* force the bulk-copy ring pipeline (comparison/diagnostics) */
 
 /* Fast-path tiling: 128x128 tiles, one scale group per tile row (group 128). */
 #define HQB_TILE 128
@@ -136,12 +137,13 @@ HQB_API int hqb_prepare_x(const void* x, int x_dtype, uint64_t cols, uint32_t ba
 
 /* ---- workspace ------------------------------------------------------------------- */
 
-/* Scratch bytes a GEMV on m with this batch needs on `device`: an error word, per
- * row-block arrival counters, split-row partial sums and a prepared-activation area. */
+/* Scratch bytes a GEMV on m with this batch needs on `device`: an error word,
+ * split-row partial sums and a prepared-activation area.  Calls that overlap on the
+ * GPU must not share a workspace. */
 HQB_API uint64_t hqb_workspace_bytes(const hqb_plane_matrix* m, uint32_t batch, int x_dtype,
                                      int device);
-/* Clears a workspace (required once after allocation and after any reported device
- * error).  GEMVs leave it cleared for the next call. */
+/* Clears a workspace's error word (once after allocation and after a reported device
+ * error). */
 HQB_API int hqb_workspace_init(void* workspace, uint64_t bytes, void* stream);
 /* Copies the workspace error word (HQB_DEVERR_* bits) to *host_flags, synchronously. */
 HQB_API int hqb_workspace_error(const void* workspace, int* host_flags, void* stream);
