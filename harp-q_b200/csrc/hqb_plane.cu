@@ -855,6 +855,176 @@ __global__ void __launch_bounds__(kStreamThreads, (NB == 1 && XL == 1) ? 2 : 1)
   }
 }
 
+// --------------------------------------------------------------------------------------
+// Uniform-depth streaming GEMV: the same per-warp streaming as gemv_stream_kernel with
+// the depth D a compile-time constant.  The plane is tile-major, so the CTA walks
+// consecutive tile indices (the next tile is always +4352 bytes, also across a tile
+// row) and each tile's D stages become D independent tensor-core chains.  kTilesAhead
+// tiles of records are kept in flight in registers.
+
+template <int D>
+struct TilesAhead {
+  static constexpr int value = D == 1 ? 8 : (D == 2 ? 4 : (D == 3 ? 3 : 2));
+};
+
+// Activation fragments with no lane branches: lanes whose batch row does not exist read
+// a zero block instead (zero points at 256 zero bytes).
+template <int NB, int XL>
+__device__ __forceinline__ void load_xfrag(XFrag<NB, XL>& xf, const GemvParams& p, const uint8_t* slot,
+                                           const uint8_t* zero, uint32_t lane) {
+  const uint32_t g = lane >> 2, q = lane & 3;
+#pragma unroll
+  for (int nb = 0; nb < NB; ++nb) {
+    const uint32_t b = g + 8 * nb;
+#pragma unroll
+    for (int l = 0; l < XL; ++l) {
+      const uint8_t* src = b < p.batch ? slot + l * p.batch * 256 + (b * 4 + q) * 64 : zero + q * 64;
+#pragma unroll
+      for (int v = 0; v < 4; ++v) {
+        const uint4 t = lds128(src + 16 * v);
+        xf.bf[nb][l][2 * v][0] = t.x;
+        xf.bf[nb][l][2 * v][1] = t.y;
+        xf.bf[nb][l][2 * v + 1][0] = t.z;
+        xf.bf[nb][l][2 * v + 1][1] = t.w;
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const uint32_t bb = 2 * q + j + 8 * nb;
+      const float2 fg = lds_f2(bb < p.batch ? slot + p.batch * 256 * XL + bb * 8 : zero);
+      xf.f[nb][j] = fg.x;
+      xf.gsum[nb][j] = fg.y;
+    }
+  }
+}
+
+template <int NB, int XL, int D>
+__global__ void __launch_bounds__(kStreamThreads, (NB == 1 && XL == 1) ? 2 : 1)
+    gemv_uniform_kernel(const __grid_constant__ GemvParams p) {
+  constexpr int R = TilesAhead<D>::value;
+  extern __shared__ __align__(16) uint8_t xres[];  // [C x xslot activation fragments][256 B zeros]
+  const uint64_t total = p.total;
+  const uint32_t ctas = static_cast<uint32_t>(total < gridDim.x ? total : gridDim.x), cta = blockIdx.x;
+  griddep_launch_dependents();  // the split-row fix-up may be scheduled; it waits for this grid
+  if (cta >= ctas) return;
+  const uint64_t u0 = unit_start(cta, total, ctas), u1 = unit_start(cta + 1, total, ctas);
+  const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, q = lane & 3;
+  const uint32_t rit0 = warp * 16 + g;
+  // tiles [t0, t_end], first tile from stage s0, last tile up to stage s_last (exclusive)
+  const uint32_t t0 = static_cast<uint32_t>(u0 / D), s0 = static_cast<uint32_t>(u0 % D);
+  const uint32_t t_end = static_cast<uint32_t>((u1 - 1) / D), s_last = static_cast<uint32_t>((u1 - 1) % D) + 1;
+  const uint32_t ntiles = t_end - t0 + 1;
+  constexpr uint32_t kFull = (1u << D) - 1u;
+  const uint32_t mask_first = kFull & ~((1u << s0) - 1u), mask_last = (1u << s_last) - 1u;
+  const uint8_t* base[D];
+#pragma unroll
+  for (int s = 0; s < D; ++s) base[s] = p.planes[s] + warp * kRowBlockBytes + lane * 16;
+  const uint32_t sc_lane = 512 - lane * 16 + g * 4;  // scale pair offset relative to this lane's codes
+
+  uint4 w[R][D];
+  uint32_t sc[R][D];
+  auto fetch = [&](int slot, uint32_t k) {  // tile t0 + k into register slot
+    const uint64_t off = static_cast<uint64_t>(t0 + k) * kRecordBytes;
+    const uint32_t mask = (k == 0 ? mask_first : kFull) & (k == ntiles - 1 ? mask_last : kFull);
+#pragma unroll
+    for (int s = 0; s < D; ++s) {
+      if (mask & (1u << s)) {
+        const uint8_t* a = base[s] + off;
+        asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                     : "=r"(w[slot][s].x), "=r"(w[slot][s].y), "=r"(w[slot][s].z), "=r"(w[slot][s].w)
+                     : "l"(a));
+        asm volatile("ld.global.nc.L1::no_allocate.u32 %0, [%1];" : "=r"(sc[slot][s]) : "l"(a + sc_lane));
+      }
+    }
+  };
+#pragma unroll
+  for (int j = 0; j < R; ++j)
+    if (static_cast<uint32_t>(j) < ntiles) fetch(j, j);
+  griddep_wait();
+  {  // activation fragments of the tile columns this CTA touches, and the zero block
+    const uint32_t c_first = t0 % p.C, c_last = t_end % p.C;
+    const bool one_row = t0 / p.C == t_end / p.C;
+    const uint32_t c_lo = one_row ? c_first : 0, c_hi = one_row ? c_last : p.C - 1;
+    const uint4* src = reinterpret_cast<const uint4*>(p.xfrag + static_cast<uint64_t>(c_lo) * p.xslot_bytes);
+    uint4* dst = reinterpret_cast<uint4*>(xres + c_lo * p.xslot_bytes);
+    const uint32_t chunks = (c_hi - c_lo + 1) * p.xslot_bytes / 16;
+    for (uint32_t t = threadIdx.x; t < chunks; t += kStreamThreads) dst[t] = __ldcg(src + t);
+    if (threadIdx.x < 16)
+      reinterpret_cast<uint4*>(xres + p.C * p.xslot_bytes)[threadIdx.x] = make_uint4(0u, 0u, 0u, 0u);
+  }
+  __syncthreads();
+  const uint8_t* zero = xres + p.C * p.xslot_bytes;
+  const uint32_t first_row = t0 / p.C;
+  uint32_t col = t0 % p.C, row = first_row;
+  float y[NB][4];
+#pragma unroll
+  for (int nb = 0; nb < NB; ++nb)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) y[nb][e] = 0.0f;
+  for (uint32_t k0 = 0; k0 < ntiles; k0 += R) {
+#pragma unroll
+    for (int j = 0; j < R; ++j) {
+      const uint32_t k = k0 + j;
+      if (k >= ntiles) break;
+      XFrag<NB, XL> xf;
+      load_xfrag<NB, XL>(xf, p, xres + col * p.xslot_bytes, zero, lane);
+      const uint32_t mask = (k == 0 ? mask_first : kFull) & (k == ntiles - 1 ? mask_last : kFull);
+      // D independent chains
+      uint32_t hi[D][4];
+      float acc[D][NB][4];
+#pragma unroll
+      for (int s = 0; s < D; ++s) {
+        hi[s][0] = __umulhi(w[j][s].x, p.shift_mul);
+        hi[s][1] = __umulhi(w[j][s].y, p.shift_mul);
+        hi[s][2] = __umulhi(w[j][s].z, p.shift_mul);
+        hi[s][3] = __umulhi(w[j][s].w, p.shift_mul);
+#pragma unroll
+        for (int nb = 0; nb < NB; ++nb)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) acc[s][nb][e] = 0.0f;
+      }
+#pragma unroll
+      for (int m = 0; m < 8; ++m) {
+#pragma unroll
+        for (int s = 0; s < D; ++s) {
+          if (D > 1 && !(mask & (1u << s))) continue;
+          const uint32_t a0 = int2_pair(w[j][s].x, hi[s][0], m), a1 = int2_pair(w[j][s].y, hi[s][1], m);
+          const uint32_t a2 = int2_pair(w[j][s].z, hi[s][2], m), a3 = int2_pair(w[j][s].w, hi[s][3], m);
+#pragma unroll
+          for (int nb = 0; nb < NB; ++nb)
+#pragma unroll
+            for (int l = 0; l < XL; ++l) mma_f16(acc[s][nb], a0, a1, a2, a3, xf.bf[nb][l][m][0], xf.bf[nb][l][m][1]);
+        }
+      }
+#pragma unroll
+      for (int s = 0; s < D; ++s) {
+        if (D > 1 && !(mask & (1u << s))) continue;
+        const __half2 s2 = *reinterpret_cast<const __half2*>(&sc[j][s]);
+        const float s_lo = __low2float(s2), s_hi = __high2float(s2);
+#pragma unroll
+        for (int nb = 0; nb < NB; ++nb) {
+          y[nb][0] = fmaf(s_lo, fmaf(acc[s][nb][0], xf.f[nb][0], -xf.gsum[nb][0]), y[nb][0]);
+          y[nb][1] = fmaf(s_lo, fmaf(acc[s][nb][1], xf.f[nb][1], -xf.gsum[nb][1]), y[nb][1]);
+          y[nb][2] = fmaf(s_hi, fmaf(acc[s][nb][2], xf.f[nb][0], -xf.gsum[nb][0]), y[nb][2]);
+          y[nb][3] = fmaf(s_hi, fmaf(acc[s][nb][3], xf.f[nb][1], -xf.gsum[nb][1]), y[nb][3]);
+        }
+      }
+      if (k + R < ntiles) fetch(j, k + R);
+      if (++col == p.C || k + 1 == ntiles) {
+        const RowSplit rs = row_split(p, row, total, ctas);
+        if (rs.first == rs.last) store_out<NB>(p, y, row * 128 + rit0, q);
+        else publish_partial<NB>(p, cta, row == first_row ? 0 : 1, y, rit0, q);
+#pragma unroll
+        for (int nb = 0; nb < NB; ++nb)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) y[nb][e] = 0.0f;
+        col = 0;
+        ++row;
+      }
+    }
+  }
+}
+
 // Split tile rows: the parts of the contributing CTAs, summed in CTA order, plus
 // bias.  Launched as a programmatic dependent of the GEMV; griddepcontrol.wait makes
 // the GEMV's stores visible.  One block per tile row; whole rows exit at once.
@@ -1031,6 +1201,21 @@ bool stage_planes_ok(const hqb_plane_matrix* m, uint32_t needed) {
 }
 
 using GemvKernel = void (*)(GemvParams);
+
+template <int NB, int XL>
+GemvKernel pick_uniform_depth(uint32_t d) {
+  switch (d) {
+    case 1: return gemv_uniform_kernel<NB, XL, 1>;
+    case 2: return gemv_uniform_kernel<NB, XL, 2>;
+    case 3: return gemv_uniform_kernel<NB, XL, 3>;
+    default: return gemv_uniform_kernel<NB, XL, 4>;
+  }
+}
+
+GemvKernel pick_uniform_kernel(uint32_t nb, uint32_t xl, uint32_t d) {
+  if (nb == 1) return xl == 1 ? pick_uniform_depth<1, 1>(d) : pick_uniform_depth<1, 2>(d);
+  return xl == 1 ? pick_uniform_depth<2, 1>(d) : pick_uniform_depth<2, 2>(d);
+}
 
 GemvKernel pick_stream_kernel(uint32_t nb, uint32_t xl) {
   if (nb == 1) return xl == 1 ? gemv_stream_kernel<1, 1> : gemv_stream_kernel<1, 2>;
@@ -1280,8 +1465,9 @@ HQB_API int hqb_gemv_ex(const hqb_plane_matrix* m, uint32_t prefix, const uint8_
   p.total = mixed ? 0 : tiles * prefix;
   const bool streaming = !simt && static_cast<uint64_t>(m->grid_cols) * p.xslot_bytes <= kXResidentMax &&
                          !(flags & HQB_FLAG_RING);
-  const GemvKernel k =
-      streaming ? pick_stream_kernel(batch > 8 ? 2 : 1, xl) : pick_kernel(batch > 8 ? 2 : 1, xl, simt);
+  const GemvKernel k = !streaming ? pick_kernel(batch > 8 ? 2 : 1, xl, simt)
+                       : mixed    ? pick_stream_kernel(batch > 8 ? 2 : 1, xl)
+                                  : pick_uniform_kernel(batch > 8 ? 2 : 1, xl, prefix);
   const uint64_t x_all = static_cast<uint64_t>(m->grid_cols) * p.xslot_bytes;
   p.x_resident = x_all <= kXResidentMax ? 1u : 0u;
   p.slot_x_bytes = p.x_resident ? 0u : p.xslot_bytes;
@@ -1291,7 +1477,7 @@ HQB_API int hqb_gemv_ex(const hqb_plane_matrix* m, uint32_t prefix, const uint8_
   p.slot_stride = rs.stride;
   p.shift_mul = 1u << 24;
   p.pdl = (flags & HQB_FLAG_PDL) ? 1u : 0u;
-  const uint32_t smem = streaming ? static_cast<uint32_t>(x_all) : rs.smem;
+  const uint32_t smem = streaming ? static_cast<uint32_t>(x_all) + 256 : rs.smem;
   const uint32_t threads = streaming ? kStreamThreads : kGemvThreads;
   const int per_sm = ctas_per_sm(k, smem, device, threads);
   if (per_sm <= 0) return cudaErrorLaunchOutOfResources;
