@@ -22,7 +22,6 @@ import argparse
 import json
 import os
 import statistics
-import subprocess
 import sys
 import threading
 import time
@@ -109,59 +108,94 @@ def make_layer(rows, cols, std, seed, device):
 # clocks
 
 class ClockSampler:
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    """SM clock and clock-event reasons sampled through NVML (read-only queries) on a
+    background thread every ~2 ms while the benchmark runs.  summary() reports the
+    samples taken inside the timed region [t0, t1] (host monotonic time); when the
+    region is too short for any sample it falls back to the whole measurement phase
+    and says so in "window"."""
+
+    REASONS = (("hw_slowdown", "nvmlClocksEventReasonHwSlowdown"),
+               ("hw_thermal_slowdown", "nvmlClocksEventReasonHwThermalSlowdown"),
+               ("sw_thermal_slowdown", "nvmlClocksEventReasonSwThermalSlowdown"),
+               ("sw_power_cap", "nvmlClocksEventReasonSwPowerCap"),
+               ("hw_power_brake_slowdown", "nvmlClocksEventReasonHwPowerBrakeSlowdown"))
 
     def __init__(self, device_index: int):
-        visible = os.environ.get("CUDA_VISIBLE_DEVICES")
-        ids = [v.strip() for v in visible.split(",")] if visible else []
-        self.idx = ids[device_index] if device_index < len(ids) else str(device_index)
-        self.proc = None
-        self.lines: list[str] = []
+        self.device_index = device_index
+        self.samples: list[tuple[float, int, int]] = []
+        self.max_mhz = None
+        self.error = None
+        self._stop = threading.Event()
+        self._thread = None
+        self.nv = None
+        self.handle = None
+
+    def _open(self):
+        import pynvml as nv
+
+        nv.nvmlInit()
+        self.nv = nv
+        handle = None
+        try:
+            props = torch.cuda.get_device_properties(self.device_index)
+            bus = f"{props.pci_domain_id:08X}:{props.pci_bus_id:02X}:{props.pci_device_id:02X}.0"
+            handle = nv.nvmlDeviceGetHandleByPciBusId(bus)
+        except Exception:  # older torch without PCI ids: map through CUDA_VISIBLE_DEVICES
+            visible = os.environ.get("CUDA_VISIBLE_DEVICES")
+            ids = [v.strip() for v in visible.split(",")] if visible else []
+            idx = ids[self.device_index] if self.device_index < len(ids) else str(self.device_index)
+            handle = (nv.nvmlDeviceGetHandleByUUID(idx) if not idx.isdigit()
+                      else nv.nvmlDeviceGetHandleByIndex(int(idx)))
+        self.handle = handle
+        self.max_mhz = nv.nvmlDeviceGetMaxClockInfo(handle, nv.NVML_CLOCK_SM)
+
+    def _run(self):
+        nv, h = self.nv, self.handle
+        while not self._stop.is_set():
+            try:
+                mhz = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+                reasons = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+            except Exception as exc:  # keep the benchmark running; report the failure
+                self.error = str(exc)
+                return
+            self.samples.append((time.monotonic(), mhz, reasons))
+            self._stop.wait(0.002)
 
     def __enter__(self):
         try:
-            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "100"],
-                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.thread = threading.Thread(target=self._read, daemon=True)
-            self.thread.start()
-        except OSError:
-            self.proc = None
+            self._open()
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+        except Exception as exc:
+            self.error = str(exc)
         return self
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
-
     def __exit__(self, *exc):
-        if self.proc is not None:
-            self.proc.terminate()
+        self._stop.set()
+        if self._thread is not None:
+            self._thread.join(timeout=5)
+        if self.nv is not None:
             try:
-                self.proc.wait(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
+                self.nv.nvmlShutdown()
+            except Exception:
+                pass
 
-    def summary(self) -> dict:
-        sm, mx, reasons = [], [], set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in self.lines:
-            parts = [p.strip() for p in line.split(",")]
-            if len(parts) < 9:
-                continue
-            try:
-                sm.append(float(parts[1]))
-                mx.append(float(parts[2]))
-            except ValueError:
-                continue
-            for name, val in zip(names, parts[5:9]):
-                if val.lower() == "active":
+    def summary(self, t0: float, t1: float) -> dict:
+        inside = [s for s in self.samples if t0 <= s[0] <= t1]
+        window = "timed region"
+        if not inside:
+            inside, window = self.samples, "measurement phase (timed region shorter than one sample)"
+        if not inside:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": 0,
+                    "error": self.error or "no samples"}
+        reasons = set()
+        for _, _, mask in inside:
+            for name, attr in self.REASONS:
+                if mask & getattr(self.nv, attr, 0):
                     reasons.add(name)
-        if not sm:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
-                "samples": len(sm)}
+        return {"sm_mhz": statistics.median(s[1] for s in inside), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(reasons), "samples": len(inside), "window": window,
+                "sm_mhz_min": min(s[1] for s in inside)}
 
 
 # ---------------------------------------------------------------------------------------
@@ -217,7 +251,10 @@ def run_ours(args, rank, world, device):
                                      dtype=torch.float16, device=device) for L in layers}
     ws_bytes = max(L["copies"][0].workspace_bytes(1, hqb.F16) for L in layers)
     ws = hqb.Workspace(ws_bytes, device)
-    launches_per_step = len(srcs) + len(layers)
+    # per step: one activation preparation per distinct input, and the launches of each
+    # layer's GEMV (the library's own dispatch rule)
+    launches_per_step = len(srcs) + sum(L["copies"][0].gemv_launches(1, hqb.F16, prefix, x_prepared=True)
+                                        for L in layers)
 
     def gather(L):
         if world == 1:
@@ -235,6 +272,10 @@ def run_ours(args, rank, world, device):
             pm.gemv(x_dev[L["src"]], prefix=prefix, out=y_loc[L["name"]], workspace=ws,
                     x_prepared=xfrag[L["src"]], flags=hqb.FLAG_PDL)
             gather(L)
+
+    # clocks are sampled from warm-up to the end of the e2e leg; the summary keeps the
+    # samples that fall inside the timed region
+    clk = ClockSampler(torch.cuda.current_device()).__enter__()
 
     # warm-up (also JIT/driver setup)
     for i in range(max(3, args.warmup)):
@@ -260,16 +301,17 @@ def run_ours(args, rank, world, device):
 
     # ---- timed region: K steps
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(torch.cuda.current_device()) as clk:
-        barrier()
-        start.record()
-        for i in range(args.steps):
-            if use_graph:
-                graphs[i % ncopies].replay()
-            else:
-                step(i % ncopies)
-        end.record()
-        barrier()
+    barrier()
+    t_timed0 = time.monotonic()
+    start.record()
+    for i in range(args.steps):
+        if use_graph:
+            graphs[i % ncopies].replay()
+        else:
+            step(i % ncopies)
+    end.record()
+    barrier()
+    t_timed1 = time.monotonic()
     ms = start.elapsed_time(end)
     ms_max = ms
     if world > 1:
@@ -282,26 +324,40 @@ def run_ours(args, rank, world, device):
         total_bytes = sum(algorithmic_bytes(L["rows"], L["cols"], prefix) for L in layers)
     value = total_bytes / (ms_per_step * 1e-3) / 1e9
 
-    # ---- per-kernel roofline: GEMV launches timed alone with events on this stream
-    per_layer_ms = {L["name"]: [] for L in layers}
-    for i in range(max(6, ncopies)):
-        for L in layers:
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record()
-            L["copies"][i % ncopies].gemv(x_dev[L["src"]], prefix=prefix, out=y_loc[L["name"]], workspace=ws,
-                                          x_prepared=xfrag[L["src"]])
-            e1.record()
-            per_layer_ms[L["name"]].append((e0, e1))
-    torch.cuda.synchronize()
+    # ---- per-kernel roofline: each layer's GEMV launched back to back (PDL) inside one
+    # CUDA graph over its rotating weight copies; CUDA events on the launching stream
+    # around graph replays give the average duration of one launch
     kern = {}
     tot_b, tot_ms = 0, 0.0
+    per_graph = 4 * ncopies
     for L in layers:
-        times = sorted(a.elapsed_time(b) for a, b in per_layer_ms[L["name"]][2:])
-        med = statistics.median(times)
+        g = torch.cuda.CUDAGraph()
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            for i in range(2):
+                L["copies"][i % ncopies].gemv(x_dev[L["src"]], prefix=prefix, out=y_loc[L["name"]], workspace=ws,
+                                              x_prepared=xfrag[L["src"]], flags=hqb.FLAG_PDL)
+        torch.cuda.current_stream().wait_stream(side)
+        with torch.cuda.graph(g):
+            for i in range(per_graph):
+                L["copies"][i % ncopies].gemv(x_dev[L["src"]], prefix=prefix, out=y_loc[L["name"]], workspace=ws,
+                                              x_prepared=xfrag[L["src"]], flags=hqb.FLAG_PDL)
+        for _ in range(3):
+            g.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(5):
+            g.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        per_launch_ms = e0.elapsed_time(e1) / (5 * per_graph)
+        del g
         b = algorithmic_bytes(L["nrows"], L["cols"], prefix)
-        kern[L["name"]] = {"us": round(med * 1e3, 3), "gbs": round(b / (med * 1e-3) / 1e9, 1)}
+        kern[L["name"]] = {"us": round(per_launch_ms * 1e3, 3), "gbs": round(b / (per_launch_ms * 1e-3) / 1e9, 1)}
         tot_b += b
-        tot_ms += med
+        tot_ms += per_launch_ms
     achieved = tot_b / (tot_ms * 1e-3) / 1e9
 
     # ---- e2e through the public API: pinned host x -> device, GEMVs, device -> host y
@@ -335,6 +391,7 @@ def run_ours(args, rank, world, device):
     h2d = sum(x.numel() * 2 for x in host_x.values())
     d2h = sum(y.numel() * 2 for y in host_y.values())
 
+    clk.__exit__(None, None, None)
     flags = ws.error_flags()
     result = {
         "metric": METRIC,
@@ -361,7 +418,7 @@ def run_ours(args, rank, world, device):
         "e2e": {"value": round(total_bytes / (e2e_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
                 "us_per_step": round(e2e_ms * 1e3, 2), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
         "gpu_launches": launches_per_step * args.steps,
-        "clocks": clk.summary(),
+        "clocks": clk.summary(t_timed0, t_timed1),
         "device_error_flags": flags,
     }
     peaks = {}
@@ -375,9 +432,10 @@ def run_ours(args, rank, world, device):
                           "frac": round(achieved / peak, 4),
                           "peak_source": "measured" if "hbm_gbs" in peaks else "fallback",
                           "traffic": None if traffic is None else round(traffic * tot_b / len(layers)),
-                          "kernel": "hqb::gemv_kernel<1,1,false>",
-                          "achieved_note": "algorithmic bytes of all GEMV launches / sum of their median "
-                                           "CUDA-event durations"}
+                          "kernel": f"hqb::gemv_uniform_kernel<1,1,{prefix}> (+ hqb::fixup_kernel of split rows)",
+                          "achieved_note": "algorithmic bytes of one launch per layer / sum of the layers' "
+                                           "average launch durations (CUDA events around graphs of back-to-back "
+                                           "launches)"}
     return result
 
 
@@ -453,12 +511,14 @@ def time_reference(name, steps, warmup, device, threads=None, budget_s=None):
 
 def run_reference_arm(args, device):
     name = args.workload
-    r = time_reference(name, args.steps, max(1, min(args.warmup, 2)), device)
+    # each step is one full pass of the workload on the host cores; the run stops
+    # after the step that crosses 60 s so that it ends within a few minutes
+    r = time_reference(name, args.steps, max(1, min(args.warmup, 2)), device, budget_s=60.0)
     prefix, layers, _ = WORKLOADS[name]
     return {"metric": METRIC, "impl": "reference", "value": r["value"], "unit": "GB/s", "n_gpus": args.gpus,
             "steps": r["steps_timed"], "warmup": args.warmup, "ms_per_step": round(r["ms_per_step"], 3),
             "us_per_layer": round(r["ms_per_step"] * 1e3 / len(layers), 1), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "int2 codes x FP32 scales, FP32 x/y (reference C++)",
+            "scaling": "strong", "vs_baseline": None, "dtype": "int2 codes x FP32 scales, FP32 x/y (reference C++)",
             "data": "synthetic, the product arm's weights (same seeds and quantizer)",
             "config": {"workload": name, "prefix": prefix, "batch": 1},
             "cpu_baseline": {k: r[k] for k in ("value", "unit", "cores", "kind", "sample")},
@@ -470,7 +530,7 @@ def run_reference_arm(args, device):
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser(description=__doc__)
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", default="auto", choices=["auto", *WORKLOADS])

@@ -60,6 +60,7 @@ struct GemvParams {
   const void* bias;
   void* y;
   float* partials;     // [G][2][batch][128]
+  uint32_t* counters;  // [R] split-row arrival counts (zero between launches)
   int* error;
   uint64_t total;      // units (uniform); mixed reads plan[R]
   uint32_t rows;
@@ -898,48 +899,122 @@ __device__ __forceinline__ void load_xfrag(XFrag<NB, XL>& xf, const GemvParams& 
   }
 }
 
+// Sum of split tile row r over its contributing CTAs first..last in CTA order, plus
+// bias (the same arithmetic as fixup_kernel).  Run by every thread of the CTA that
+// finished the row last; partials are read through L2.
+template <int NB>
+__device__ __noinline__ void reduce_split_row(const GemvParams& p, uint32_t r, uint32_t first, uint32_t last,
+                                              uint32_t first_slot) {
+  const uint64_t cta_stride = 2ull * p.batch * 128;
+  for (uint32_t e = threadIdx.x; e < p.batch * 128; e += kStreamThreads) {
+    const uint32_t b = e >> 7, rit = e & 127, row = r * 128 + rit;
+    if (row >= p.rows) continue;
+    const float* src = p.partials + static_cast<uint64_t>(b) * 128 + rit;
+    float sum = 0.0f;
+    sum += __ldcg(src + first * cta_stride + first_slot * p.batch * 128);
+    uint32_t i = first + 1;
+    for (; i + 4 <= last + 1; i += 4) {
+      const float v0 = __ldcg(src + i * cta_stride), v1 = __ldcg(src + (i + 1) * cta_stride);
+      const float v2 = __ldcg(src + (i + 2) * cta_stride), v3 = __ldcg(src + (i + 3) * cta_stride);
+      sum += v0;
+      sum += v1;
+      sum += v2;
+      sum += v3;
+    }
+    for (; i <= last; ++i) sum += __ldcg(src + i * cta_stride);
+    if (p.bias != nullptr)
+      sum += p.bias_dtype == HQB_F16 ? __half2float(static_cast<const __half*>(p.bias)[row])
+                                     : static_cast<const float*>(p.bias)[row];
+    const uint64_t o = static_cast<uint64_t>(b) * p.rows + row;
+    if (p.y_dtype == HQB_F16) static_cast<__half*>(p.y)[o] = __float2half_rn(sum);
+    else static_cast<float*>(p.y)[o] = sum;
+  }
+}
+
+// End of tile row r for this CTA (units [u0, u1)).  A row wholly inside the range is
+// stored.  A split row is published as this CTA's part; the contributor that arrives
+// last (per-row counter, reset by that contributor) sums all parts.  Nothing waits.
+// CTA-uniform: every thread calls it at the same point.
+template <int NB>
+__device__ __forceinline__ void finish_row(const GemvParams& p, uint32_t r, uint64_t units_per_row, uint64_t u0,
+                                           uint64_t u1, uint64_t total, uint32_t ctas, uint32_t cta,
+                                           const float (&y)[NB][4], uint32_t rit0, uint32_t q, uint32_t* s_info) {
+  const uint64_t rb = static_cast<uint64_t>(r) * units_per_row, re = rb + units_per_row;
+  if (rb >= u0 && re <= u1) {
+    store_out<NB>(p, y, r * 128 + rit0, q);
+    return;
+  }
+  publish_partial<NB>(p, cta, rb <= u0 ? 0u : 1u, y, rit0, q);
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const uint32_t first = unit_owner(rb, total, ctas), last = unit_owner(re - 1, total, ctas);
+    const uint32_t old = atomicAdd(p.counters + r, 1u);
+    uint32_t info = 0;
+    if (old == last - first) {  // every other contributor has published
+      p.counters[r] = 0u;         // ready for the next launch
+      info = 1u | (unit_start(first, total, ctas) < rb ? 2u : 0u);
+      s_info[1] = first;
+      s_info[2] = last;
+    }
+    s_info[0] = info;
+    __threadfence();
+  }
+  __syncthreads();
+  const uint32_t info = s_info[0];
+  if (info & 1u) reduce_split_row<NB>(p, r, s_info[1], s_info[2], info >> 1);
+}
+
 template <int NB, int XL, int D>
 __global__ void __launch_bounds__(kStreamThreads, (NB == 1 && XL == 1) ? 2 : 1)
     gemv_uniform_kernel(const __grid_constant__ GemvParams p) {
   constexpr int R = TilesAhead<D>::value;
+  constexpr uint32_t kFull = (1u << D) - 1u;
   extern __shared__ __align__(16) uint8_t xres[];  // [C x xslot activation fragments][256 B zeros]
+  __shared__ uint32_t s_info[3];
   const uint64_t total = p.total;
   const uint32_t ctas = static_cast<uint32_t>(total < gridDim.x ? total : gridDim.x), cta = blockIdx.x;
-  griddep_launch_dependents();  // the split-row fix-up may be scheduled; it waits for this grid
+  griddep_launch_dependents();  // a following PDL kernel may be scheduled; it waits for this grid
   if (cta >= ctas) return;
   const uint64_t u0 = unit_start(cta, total, ctas), u1 = unit_start(cta + 1, total, ctas);
   const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, q = lane & 3;
   const uint32_t rit0 = warp * 16 + g;
-  // tiles [t0, t_end], first tile from stage s0, last tile up to stage s_last (exclusive)
+  // tiles t0..t0+ntiles-1; the first starts at stage s0, the last ends before stage s_end
   const uint32_t t0 = static_cast<uint32_t>(u0 / D), s0 = static_cast<uint32_t>(u0 % D);
-  const uint32_t t_end = static_cast<uint32_t>((u1 - 1) / D), s_last = static_cast<uint32_t>((u1 - 1) % D) + 1;
+  const uint32_t t_end = static_cast<uint32_t>((u1 - 1) / D), s_end = static_cast<uint32_t>((u1 - 1) % D) + 1;
   const uint32_t ntiles = t_end - t0 + 1;
-  constexpr uint32_t kFull = (1u << D) - 1u;
-  const uint32_t mask_first = kFull & ~((1u << s0) - 1u), mask_last = (1u << s_last) - 1u;
-  const uint8_t* base[D];
+  const uint32_t mask_first = kFull & ~((1u << s0) - 1u), mask_last = (1u << s_end) - 1u;
+  const uint8_t* cb[D];
 #pragma unroll
-  for (int s = 0; s < D; ++s) base[s] = p.planes[s] + warp * kRowBlockBytes + lane * 16;
-  const uint32_t sc_lane = 512 - lane * 16 + g * 4;  // scale pair offset relative to this lane's codes
+  for (int s = 0; s < D; ++s)
+    cb[s] = p.planes[s] + static_cast<uint64_t>(t0) * kRecordBytes + warp * kRowBlockBytes + lane * 16;
+  const uint32_t sc_off = 512 - lane * 16 + g * 4;  // this lane's scale pair, relative to its codes
 
+  // Register ring of R tiles x D stages.  A stage outside the CTA's units gets scale 0
+  // (codes 0): its products are finite and its contribution is exactly zero.
   uint4 w[R][D];
   uint32_t sc[R][D];
-  auto fetch = [&](int slot, uint32_t k) {  // tile t0 + k into register slot
-    const uint64_t off = static_cast<uint64_t>(t0 + k) * kRecordBytes;
-    const uint32_t mask = (k == 0 ? mask_first : kFull) & (k == ntiles - 1 ? mask_last : kFull);
+  auto load_tile = [&](int slot, uint32_t k, uint32_t mask) {
+    const uint64_t off = static_cast<uint64_t>(k) * kRecordBytes;
 #pragma unroll
     for (int s = 0; s < D; ++s) {
-      if (mask & (1u << s)) {
-        const uint8_t* a = base[s] + off;
+      if (D == 1 || (mask & (1u << s))) {
+        const uint8_t* a = cb[s] + off;
         asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
                      : "=r"(w[slot][s].x), "=r"(w[slot][s].y), "=r"(w[slot][s].z), "=r"(w[slot][s].w)
                      : "l"(a));
-        asm volatile("ld.global.nc.L1::no_allocate.u32 %0, [%1];" : "=r"(sc[slot][s]) : "l"(a + sc_lane));
+        asm volatile("ld.global.nc.L1::no_allocate.u32 %0, [%1];" : "=r"(sc[slot][s]) : "l"(a + sc_off));
+      } else {
+        w[slot][s] = make_uint4(0u, 0u, 0u, 0u);
+        sc[slot][s] = 0u;
       }
     }
   };
 #pragma unroll
-  for (int j = 0; j < R; ++j)
-    if (static_cast<uint32_t>(j) < ntiles) fetch(j, j);
+  for (int j = 0; j < R; ++j) {
+    if (static_cast<uint32_t>(j) < ntiles)
+      load_tile(j, j, (j == 0 ? mask_first : kFull) & (static_cast<uint32_t>(j) == ntiles - 1 ? mask_last : kFull));
+  }
   griddep_wait();
   {  // activation fragments of the tile columns this CTA touches, and the zero block
     const uint32_t c_first = t0 % p.C, c_last = t_end % p.C;
@@ -954,74 +1029,111 @@ __global__ void __launch_bounds__(kStreamThreads, (NB == 1 && XL == 1) ? 2 : 1)
   }
   __syncthreads();
   const uint8_t* zero = xres + p.C * p.xslot_bytes;
-  const uint32_t first_row = t0 / p.C;
-  uint32_t col = t0 % p.C, row = first_row;
+  const uint64_t units_per_row = static_cast<uint64_t>(p.C) * D;
+  uint32_t row = t0 / p.C, col = t0 % p.C;
+  uint32_t left = p.C - col;  // tiles of the current row still ahead (may run past ntiles)
   float y[NB][4];
 #pragma unroll
   for (int nb = 0; nb < NB; ++nb)
 #pragma unroll
     for (int e = 0; e < 4; ++e) y[nb][e] = 0.0f;
-  for (uint32_t k0 = 0; k0 < ntiles; k0 += R) {
+
+  // Tensor-core part of one tile from ring slot j: D independent MMA chains (two for
+  // D == 1), accumulators zeroed here.
+  constexpr int CH = D == 1 ? 2 : D;
+  auto mma_tile = [&](int j, const XFrag<NB, XL>& xf, float (&acc)[CH][NB][4]) {
+    uint32_t hi[D][4];
+#pragma unroll
+    for (int s = 0; s < D; ++s) {
+      hi[s][0] = __umulhi(w[j][s].x, p.shift_mul);
+      hi[s][1] = __umulhi(w[j][s].y, p.shift_mul);
+      hi[s][2] = __umulhi(w[j][s].z, p.shift_mul);
+      hi[s][3] = __umulhi(w[j][s].w, p.shift_mul);
+    }
+#pragma unroll
+    for (int c = 0; c < CH; ++c)
+#pragma unroll
+      for (int nb = 0; nb < NB; ++nb)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc[c][nb][e] = 0.0f;
+#pragma unroll
+    for (int m = 0; m < 8; ++m) {
+#pragma unroll
+      for (int s = 0; s < D; ++s) {
+        const int c = D == 1 ? (m & 1) : s;
+        const uint32_t a0 = int2_pair(w[j][s].x, hi[s][0], m), a1 = int2_pair(w[j][s].y, hi[s][1], m);
+        const uint32_t a2 = int2_pair(w[j][s].z, hi[s][2], m), a3 = int2_pair(w[j][s].w, hi[s][3], m);
+#pragma unroll
+        for (int nb = 0; nb < NB; ++nb)
+#pragma unroll
+          for (int l = 0; l < XL; ++l) mma_f16(acc[c][nb], a0, a1, a2, a3, xf.bf[nb][l][m][0], xf.bf[nb][l][m][1]);
+      }
+    }
+  };
+  // Scale epilogue of one tile into y.
+  auto epi_tile = [&](int j, const XFrag<NB, XL>& xf, float (&acc)[CH][NB][4]) {
+    if (D == 1) {
+#pragma unroll
+      for (int nb = 0; nb < NB; ++nb)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc[0][nb][e] += acc[CH - 1][nb][e];
+    }
+#pragma unroll
+    for (int s = 0; s < D; ++s) {
+      const __half2 s2 = *reinterpret_cast<const __half2*>(&sc[j][s]);
+      const float s_lo = __low2float(s2), s_hi = __high2float(s2);
+#pragma unroll
+      for (int nb = 0; nb < NB; ++nb) {
+        y[nb][0] = fmaf(s_lo, fmaf(acc[s][nb][0], xf.f[nb][0], -xf.gsum[nb][0]), y[nb][0]);
+        y[nb][1] = fmaf(s_lo, fmaf(acc[s][nb][1], xf.f[nb][1], -xf.gsum[nb][1]), y[nb][1]);
+        y[nb][2] = fmaf(s_hi, fmaf(acc[s][nb][2], xf.f[nb][0], -xf.gsum[nb][0]), y[nb][2]);
+        y[nb][3] = fmaf(s_hi, fmaf(acc[s][nb][3], xf.f[nb][1], -xf.gsum[nb][1]), y[nb][3]);
+      }
+    }
+  };
+  // After tile k: the row may end (its last tile, or the CTA's last tile).
+  auto advance = [&](uint32_t k) {
+    ++col;
+    if (--left == 0 || k + 1 == ntiles) {
+      finish_row<NB>(p, row, units_per_row, u0, u1, total, ctas, cta, y, rit0, q, s_info);
+#pragma unroll
+      for (int nb = 0; nb < NB; ++nb)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) y[nb][e] = 0.0f;
+      ++row;
+      col = 0;
+      left = p.C;
+    }
+  };
+  auto refill = [&](int j, uint32_t k) {  // slot j, just consumed by tile k
+    const uint32_t kn = k + R;
+    if (kn < ntiles) load_tile(j, kn, kn == ntiles - 1 ? mask_last : kFull);
+  };
+
+  uint32_t k0 = 0;
+  for (; k0 + R <= ntiles; k0 += R) {  // whole groups of R tiles
 #pragma unroll
     for (int j = 0; j < R; ++j) {
       const uint32_t k = k0 + j;
-      if (k >= ntiles) break;
       XFrag<NB, XL> xf;
       load_xfrag<NB, XL>(xf, p, xres + col * p.xslot_bytes, zero, lane);
-      const uint32_t mask = (k == 0 ? mask_first : kFull) & (k == ntiles - 1 ? mask_last : kFull);
-      // D independent chains
-      uint32_t hi[D][4];
-      float acc[D][NB][4];
-#pragma unroll
-      for (int s = 0; s < D; ++s) {
-        hi[s][0] = __umulhi(w[j][s].x, p.shift_mul);
-        hi[s][1] = __umulhi(w[j][s].y, p.shift_mul);
-        hi[s][2] = __umulhi(w[j][s].z, p.shift_mul);
-        hi[s][3] = __umulhi(w[j][s].w, p.shift_mul);
-#pragma unroll
-        for (int nb = 0; nb < NB; ++nb)
-#pragma unroll
-          for (int e = 0; e < 4; ++e) acc[s][nb][e] = 0.0f;
-      }
-#pragma unroll
-      for (int m = 0; m < 8; ++m) {
-#pragma unroll
-        for (int s = 0; s < D; ++s) {
-          if (D > 1 && !(mask & (1u << s))) continue;
-          const uint32_t a0 = int2_pair(w[j][s].x, hi[s][0], m), a1 = int2_pair(w[j][s].y, hi[s][1], m);
-          const uint32_t a2 = int2_pair(w[j][s].z, hi[s][2], m), a3 = int2_pair(w[j][s].w, hi[s][3], m);
-#pragma unroll
-          for (int nb = 0; nb < NB; ++nb)
-#pragma unroll
-            for (int l = 0; l < XL; ++l) mma_f16(acc[s][nb], a0, a1, a2, a3, xf.bf[nb][l][m][0], xf.bf[nb][l][m][1]);
-        }
-      }
-#pragma unroll
-      for (int s = 0; s < D; ++s) {
-        if (D > 1 && !(mask & (1u << s))) continue;
-        const __half2 s2 = *reinterpret_cast<const __half2*>(&sc[j][s]);
-        const float s_lo = __low2float(s2), s_hi = __high2float(s2);
-#pragma unroll
-        for (int nb = 0; nb < NB; ++nb) {
-          y[nb][0] = fmaf(s_lo, fmaf(acc[s][nb][0], xf.f[nb][0], -xf.gsum[nb][0]), y[nb][0]);
-          y[nb][1] = fmaf(s_lo, fmaf(acc[s][nb][1], xf.f[nb][1], -xf.gsum[nb][1]), y[nb][1]);
-          y[nb][2] = fmaf(s_hi, fmaf(acc[s][nb][2], xf.f[nb][0], -xf.gsum[nb][0]), y[nb][2]);
-          y[nb][3] = fmaf(s_hi, fmaf(acc[s][nb][3], xf.f[nb][1], -xf.gsum[nb][1]), y[nb][3]);
-        }
-      }
-      if (k + R < ntiles) fetch(j, k + R);
-      if (++col == p.C || k + 1 == ntiles) {
-        const RowSplit rs = row_split(p, row, total, ctas);
-        if (rs.first == rs.last) store_out<NB>(p, y, row * 128 + rit0, q);
-        else publish_partial<NB>(p, cta, row == first_row ? 0 : 1, y, rit0, q);
-#pragma unroll
-        for (int nb = 0; nb < NB; ++nb)
-#pragma unroll
-          for (int e = 0; e < 4; ++e) y[nb][e] = 0.0f;
-        col = 0;
-        ++row;
-      }
+      float acc[CH][NB][4];
+      mma_tile(j, xf, acc);
+      epi_tile(j, xf, acc);
+      refill(j, k);
+      advance(k);
     }
+  }
+#pragma unroll
+  for (int j = 0; j < R; ++j) {  // the last partial group (no more loads)
+    const uint32_t k = k0 + j;
+    if (k >= ntiles) break;
+    XFrag<NB, XL> xf;
+    load_xfrag<NB, XL>(xf, p, xres + col * p.xslot_bytes, zero, lane);
+    float acc[CH][NB][4];
+    mma_tile(j, xf, acc);
+    epi_tile(j, xf, acc);
+    advance(k);
   }
 }
 
@@ -1037,16 +1149,29 @@ __global__ void __launch_bounds__(256) fixup_kernel(const __grid_constant__ Gemv
   if (r >= p.R || total == 0) return;
   const RowSplit rs = row_split(p, r, total, ctas);
   if (rs.first == rs.last) return;
+  // CTA rs.first holds the row in its second slot when its range began in an earlier
+  // row; every later contributor starts inside this row (first slot).
   const uint64_t per_row = static_cast<uint64_t>(p.C) * p.prefix;
+  const uint64_t rb = row_begin(r, p.plan, per_row);
+  const uint32_t first_slot = unit_start(rs.first, total, ctas) < rb ? 1u : 0u;
+  const uint64_t cta_stride = 2ull * p.batch * 128;
   for (uint32_t e = threadIdx.x; e < p.batch * 128; e += blockDim.x) {
     const uint32_t b = e >> 7, rit = e & 127;
     const uint32_t row = r * 128 + rit;
     if (row >= p.rows) continue;
+    const float* src = p.partials + static_cast<uint64_t>(b) * 128 + rit;
     float sum = 0.0f;
-    for (uint32_t i = rs.first; i <= rs.last; ++i) {
-      const uint32_t ki = row_of_unit(unit_start(i, total, ctas), p.plan, p.R, per_row) == r ? 0 : 1;
-      sum += p.partials[(static_cast<uint64_t>(i * 2 + ki) * p.batch + b) * 128 + rit];
+    sum += src[rs.first * cta_stride + first_slot * p.batch * 128];
+    uint32_t i = rs.first + 1;
+    for (; i + 4 <= rs.last + 1; i += 4) {
+      const float v0 = src[i * cta_stride], v1 = src[(i + 1) * cta_stride];
+      const float v2 = src[(i + 2) * cta_stride], v3 = src[(i + 3) * cta_stride];
+      sum += v0;
+      sum += v1;
+      sum += v2;
+      sum += v3;
     }
+    for (; i <= rs.last; ++i) sum += src[i * cta_stride];
     if (p.bias != nullptr)
       sum += p.bias_dtype == HQB_F16 ? __half2float(static_cast<const __half*>(p.bias)[row])
                                      : static_cast<const float*>(p.bias)[row];
@@ -1171,14 +1296,16 @@ int device_sm_count(int device) {
 namespace {
 
 struct WsLayout {
-  uint64_t partials, xfrag, total;
+  uint64_t counters, partials, xfrag, total;
 };
 
-// [error word][split-row partials: G x 2 x batch x 128 FP32][prepared activations]
+// [error word][split-row counters: R uint32][split-row partials: G x 2 x batch x 128
+// FP32][prepared activations].  The error word and the counters must start at zero
+// (hqb_workspace_init); the counters return to zero at the end of every launch.
 WsLayout ws_layout(uint32_t R, uint32_t C, uint32_t batch, uint32_t xl, int sms) {
-  (void)R;
   WsLayout L{};
-  L.partials = 256;
+  L.counters = 256;
+  L.partials = L.counters + round_up(static_cast<uint64_t>(R) * 4, 256);
   const uint64_t gmax = static_cast<uint64_t>(sms) * kMaxCtasPerSm;
   L.xfrag = L.partials + round_up(gmax * 2 * batch * 128 * 4, 256);
   L.total = L.xfrag + round_up(static_cast<uint64_t>(C) * xslot_bytes_for(batch, xl), 256);
@@ -1452,6 +1579,7 @@ HQB_API int hqb_gemv_ex(const hqb_plane_matrix* m, uint32_t prefix, const uint8_
   p.y = y;
   p.error = reinterpret_cast<int*>(ws);
   p.partials = reinterpret_cast<float*>(ws + L.partials);
+  p.counters = reinterpret_cast<uint32_t*>(ws + L.counters);
   p.rows = static_cast<uint32_t>(m->rows);
   p.R = m->grid_rows;
   p.C = m->grid_cols;
@@ -1500,8 +1628,10 @@ HQB_API int hqb_gemv_ex(const hqb_plane_matrix* m, uint32_t prefix, const uint8_
     cudaGetLastError();  // do not leave a refused launch pending for the next call
     return e;
   }
-  // Split tile rows exist whenever more than one CTA shares the work.
-  if (mixed || std::min<uint64_t>(grid, p.total) > 1) {
+  // Split tile rows exist whenever more than one CTA shares the work; the uniform
+  // streaming kernel finishes them itself.
+  const bool uniform_streaming = streaming && !mixed;
+  if (!uniform_streaming && (mixed || std::min<uint64_t>(grid, p.total) > 1)) {
     cudaLaunchConfig_t fc{};
     fc.gridDim = dim3(m->grid_rows);
     fc.blockDim = dim3(256);

@@ -22,7 +22,7 @@ PKG = Path(__file__).resolve().parent
 LIB_PATH = PKG / "lib" / "libharpq_b200.so"
 
 F32, F16 = 0, 1
-FLAG_PDL, FLAG_SIMT = 1, 2
+FLAG_PDL, FLAG_SIMT, FLAG_RING = 1, 2, 4
 TILE = 128
 RECORD_BYTES = 4352
 MAX_STAGES = 4
@@ -256,6 +256,22 @@ class PlaneMatrix:
                                    ws.nbytes, flags, _stream(stream))
         check(status, "hqb_gemv_ex")
         return out
+
+    def gemv_launches(self, batch: int, x_dtype: int, prefix: int, mixed: bool = False, flags: int = 0,
+                      x_prepared: bool = False) -> int:
+        """Kernels one gemv() call launches, by the library's dispatch rule: activation
+        preparation unless x is prepared; the GEMV; and, unless the uniform streaming
+        kernel runs (it reduces split tile rows itself), the split-row fix-up."""
+        n = 0 if x_prepared else 1
+        if not mixed and prefix == 0:
+            return 1  # bias / zero fill only
+        xl = 2 if x_dtype == F32 else 1
+        xslot = -(-(batch * (256 * xl + 8)) // 16) * 16
+        streaming = not (flags & FLAG_SIMT) and self.grid_cols * xslot <= 64 * 1024 and not (flags & FLAG_RING)
+        n += 1
+        if not (streaming and not mixed):
+            n += 1
+        return n
 
     def decode(self, prefix: int | None = None, depth: torch.Tensor | None = None, stream=None) -> torch.Tensor:
         out = torch.empty(self.rows, self.cols, dtype=torch.float32, device=self.device)

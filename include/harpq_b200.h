@@ -142,8 +142,9 @@ HQB_API int hqb_prepare_x(const void* x, int x_dtype, uint64_t cols, uint32_t ba
  * GPU must not share a workspace. */
 HQB_API uint64_t hqb_workspace_bytes(const hqb_plane_matrix* m, uint32_t batch, int x_dtype,
                                      int device);
-/* Clears a workspace's error word (once after allocation and after a reported device
- * error). */
+/* Clears a workspace: its error word and its split-row counters must start at zero.
+ * Call once after allocation and after a reported device error; the counters return
+ * to zero at the end of every GEMV. */
 HQB_API int hqb_workspace_init(void* workspace, uint64_t bytes, void* stream);
 /* Copies the workspace error word (HQB_DEVERR_* bits) to *host_flags, synchronously. */
 HQB_API int hqb_workspace_error(const void* workspace, int* host_flags, void* stream);

@@ -142,13 +142,14 @@ def test_mixed_depth_against_oracle():
                     y_dtype=torch.float32).cpu().numpy()
         scalar = orc.linear_mixed(m, x, depth, bias)
         assert_close(y, scalar, 2e-4, 2e-4, f"mixed b{batch}")
-    # uniform depth map == uniform prefix
+    # a uniform depth map computes the uniform prefix (different kernels and FP32
+    # summation orders: equal within the FP32 contract)
     for p in (1, 4):
         u = hqb.DepthPlan(torch.full((gr, gc), p, dtype=torch.uint8, device="cuda"), 4)
         x = torch.randn(2, m.cols, device="cuda").half()
-        a = pm.gemv(x, depth=u, y_dtype=torch.float32)
-        b = pm.gemv(x, prefix=p, y_dtype=torch.float32)
-        assert torch.equal(a, b)
+        a = pm.gemv(x, depth=u, y_dtype=torch.float32).cpu().numpy()
+        b = pm.gemv(x, prefix=p, y_dtype=torch.float32).cpu().numpy()
+        assert_close(a, b, 2e-4, 2e-4, f"depth map of {p} vs prefix {p}")
 
 
 def test_depth_plan_flags_bad_entries():
