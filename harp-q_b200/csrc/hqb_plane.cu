@@ -1442,6 +1442,7 @@ HQB_API const char* hqb_status_string(int status) {
     case HQB_OK: return "success";
     case HQB_ERR_INVALID: return "invalid argument (nothing enqueued)";
     case HQB_ERR_UNSUPPORTED: return "geometry not supported by the plane layout";
+    case HQB_ERR_SCRATCH_LIMIT: return "work needs more scratch than HQB_NOALLOC_SCRATCH_BYTES (nothing enqueued)";
     default: return cudaGetErrorString(static_cast<cudaError_t>(status));
   }
 }

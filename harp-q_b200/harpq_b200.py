@@ -28,6 +28,8 @@ RECORD_BYTES = 4352
 MAX_STAGES = 4
 MAX_BATCH = 16
 DEVERR_SCALE, DEVERR_DEPTH, DEVERR_TIMEOUT = 1, 2, 4
+NOALLOC_SCRATCH_BYTES = 4 << 20
+ERR_SCRATCH_LIMIT = 20001
 
 u64, u32, i32, vp = ctypes.c_uint64, ctypes.c_uint32, ctypes.c_int, ctypes.c_void_p
 
@@ -66,6 +68,7 @@ EXPORTS = {
     "hqb_gemv_mixed": (i32, [ctypes.POINTER(PlaneMatrixC), vp, vp, vp, i32, u32, vp, i32, vp, i32, vp, u64, vp]),
     "hqb_gemv_ex": (i32, [ctypes.POINTER(PlaneMatrixC), u32, vp, vp, vp, i32, u32, i32, vp, i32, vp, i32, vp, u64,
                           u32, vp]),
+    "hqb_gemv_noalloc": (i32, [ctypes.POINTER(PlaneMatrixC), u32, vp, i32, u32, vp, i32, vp, i32, vp]),
     "hqb_decode_planes": (i32, [ctypes.POINTER(PlaneMatrixC), u32, vp, vp, u64, vp]),
     "hqb_raw_gemv": (i32, [ctypes.POINTER(Geometry), ctypes.POINTER(RawStage), u32, u32, vp, u64, vp, u64, vp, u64,
                            vp]),

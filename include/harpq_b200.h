@@ -192,6 +192,36 @@ HQB_API int hqb_gemv_ex(const hqb_plane_matrix* m, uint32_t prefix, const uint8_
                         void* y, int y_dtype, void* workspace, uint64_t workspace_bytes,
                         uint32_t flags, void* stream);
 
+/* ---- GEMV with a fixed scratch (no reference counterpart) --------------------------- */
+
+/* Size of the per-device scratch array built into the library for hqb_gemv_noalloc:
+ * 4 MiB.  On a 148-SM B200 that covers batch 1-4 for layers up to 28672 input columns,
+ * FP16 or FP32 activations (hqb_workspace_bytes gives the exact need). */
+#define HQB_NOALLOC_SCRATCH_BYTES (4u << 20)
+/* hqb_gemv_noalloc status when hqb_workspace_bytes(m, batch, x_dtype, device) exceeds
+ * HQB_NOALLOC_SCRATCH_BYTES; nothing is enqueued (use hqb_gemv with a workspace). */
+#define HQB_ERR_SCRATCH_LIMIT 20001
+
+/* hqb_gemv on the current device without a caller workspace and without allocating:
+ * the scratch is a fixed array in the library's device image, one per device.  For
+ * callers that cannot allocate device memory at the call: a host that binds only this
+ * library and holds no device allocator, and a decode step that must not allocate
+ * because cudaMalloc/cudaFree synchronize the device and fail once weights and caches
+ * fill the HBM.  The reference has no counterpart (its LaunchProgressiveGemv needs no
+ * scratch, progressive_gemv.cu:420-439; this library's GEMV does).
+ * - The first call on a device sets up: it resolves the array's address on that device
+ *   (cudaGetSymbolAddress) and enqueues a clear of the whole array on `stream`.  Make
+ *   that first call before any stream capture.
+ * - What must start at zero: the error word and the split-row counters (they return to
+ *   zero at the end of every call).  The rest is written before it is read.
+ * - One scratch per device: calls whose GPU work overlaps (other streams, other host
+ *   threads) race on it.  Order them on one stream or with events.
+ * - Device error bits land in the scratch's error word, which is not exposed; the
+ *   status returned is that of the launches. */
+HQB_API int hqb_gemv_noalloc(const hqb_plane_matrix* m, uint32_t prefix, const void* x,
+                             int x_dtype, uint32_t batch, const void* bias, int bias_dtype,
+                             void* y, int y_dtype, void* stream);
+
 /* Dense FP32 weights [rows][cols] decoded from planes, Σ_{s<d} code·scale summed in
  * stage order from 0.0f — bit-identical to DequantizePrefix
  * (native/src/stage_codec.cpp:254-272).  depth NULL: uniform prefix. */
