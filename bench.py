@@ -4,7 +4,8 @@ Workloads (seeded synthetic weights, FP16 activations):
   llama7b_block_p2   q,k,v,o 4096x4096; gate,up 11008x4096; down 4096x11008; prefix 2; 1 GPU
   llama70b_mlp_p3    gate,up 28672x8192; down 8192x28672; prefix 3; output rows sharded
                      over the ranks with an FP16 all-gather of each layer's output (NCCL)
-Default: llama7b_block_p2 at one GPU, llama70b_mlp_p3 when --gpus > 1.
+Default: llama7b_block_p2 at one GPU, llama70b_mlp_p3 when --gpus > 1.  The single_*
+workloads (one layer) serve profiling and per-shape checks.
 
 A step is one pass over every layer of the workload at batch 1.  `value` is the
 aggregate algorithmic HBM bytes (selected planes + scales + FP16 x + FP16 y, the
@@ -48,6 +49,8 @@ WORKLOADS = {
     "single_4096_p4": (4, [("w", 4096, 4096, "a")], 0.02),
     "single_11008_p1": (1, [("w", 11008, 4096, "a")], 0.02),
     "single_11008_p4": (4, [("w", 11008, 4096, "a")], 0.02),
+    "single_28672_p1": (1, [("w", 28672, 8192, "a")], 0.015),
+    "single_28672_p3": (3, [("w", 28672, 8192, "a")], 0.015),
 }
 
 
