@@ -868,18 +868,35 @@ struct TilesAhead {
   static constexpr int value = D == 1 ? 8 : (D == 2 ? 4 : (D == 3 ? 3 : 2));
 };
 
-// Activation fragments with no lane branches: lanes whose batch row does not exist read
-// a zero block instead (zero points at 256 zero bytes).
+// Per-lane byte offsets of the activation data inside one tile slot.  Lanes whose batch
+// row does not exist read the last real row instead: their MMA columns and epilogue
+// values are never stored, and copies of real data keep them finite.
 template <int NB, int XL>
-__device__ __forceinline__ void load_xfrag(XFrag<NB, XL>& xf, const GemvParams& p, const uint8_t* slot,
-                                           const uint8_t* zero, uint32_t lane) {
-  const uint32_t g = lane >> 2, q = lane & 3;
+struct XLane {
+  uint32_t frag[NB];    // B-fragment row of batch g + 8*nb (first of XL halves)
+  uint32_t fg[NB][2];   // {factor, correction} of batch 2q + j + 8*nb
+  uint32_t half_stride; // bytes between the XL halves (batch * 256)
+
+  __device__ __forceinline__ XLane(uint32_t batch, uint32_t lane) {
+    const uint32_t g = lane >> 2, q = lane & 3;
+    half_stride = batch * 256;
+#pragma unroll
+    for (int nb = 0; nb < NB; ++nb) {
+      const uint32_t b = min(g + 8 * nb, batch - 1);
+      frag[nb] = (b * 4 + q) * 64;
+#pragma unroll
+      for (int j = 0; j < 2; ++j) fg[nb][j] = batch * 256 * XL + min(2 * q + j + 8 * nb, batch - 1) * 8;
+    }
+  }
+};
+
+template <int NB, int XL>
+__device__ __forceinline__ void load_xfrag(XFrag<NB, XL>& xf, const XLane<NB, XL>& xl, const uint8_t* slot) {
 #pragma unroll
   for (int nb = 0; nb < NB; ++nb) {
-    const uint32_t b = g + 8 * nb;
 #pragma unroll
     for (int l = 0; l < XL; ++l) {
-      const uint8_t* src = b < p.batch ? slot + l * p.batch * 256 + (b * 4 + q) * 64 : zero + q * 64;
+      const uint8_t* src = slot + xl.frag[nb] + l * xl.half_stride;
 #pragma unroll
       for (int v = 0; v < 4; ++v) {
         const uint4 t = lds128(src + 16 * v);
@@ -891,8 +908,7 @@ __device__ __forceinline__ void load_xfrag(XFrag<NB, XL>& xf, const GemvParams& 
     }
 #pragma unroll
     for (int j = 0; j < 2; ++j) {
-      const uint32_t bb = 2 * q + j + 8 * nb;
-      const float2 fg = lds_f2(bb < p.batch ? slot + p.batch * 256 * XL + bb * 8 : zero);
+      const float2 fg = lds_f2(slot + xl.fg[nb][j]);
       xf.f[nb][j] = fg.x;
       xf.gsum[nb][j] = fg.y;
     }
@@ -970,7 +986,7 @@ __global__ void __launch_bounds__(kStreamThreads, (NB == 1 && XL == 1) ? 2 : 1)
     gemv_uniform_kernel(const __grid_constant__ GemvParams p) {
   constexpr int R = TilesAhead<D>::value;
   constexpr uint32_t kFull = (1u << D) - 1u;
-  extern __shared__ __align__(16) uint8_t xres[];  // [C x xslot activation fragments][256 B zeros]
+  extern __shared__ __align__(16) uint8_t xres[];  // [C x xslot activation fragments]
   __shared__ uint32_t s_info[3];
   const uint64_t total = p.total;
   const uint32_t ctas = static_cast<uint32_t>(total < gridDim.x ? total : gridDim.x), cta = blockIdx.x;
@@ -984,39 +1000,56 @@ __global__ void __launch_bounds__(kStreamThreads, (NB == 1 && XL == 1) ? 2 : 1)
   const uint32_t t_end = static_cast<uint32_t>((u1 - 1) / D), s_end = static_cast<uint32_t>((u1 - 1) % D) + 1;
   const uint32_t ntiles = t_end - t0 + 1;
   const uint32_t mask_first = kFull & ~((1u << s0) - 1u), mask_last = (1u << s_end) - 1u;
+  // Per-stage code and scale pointers of this lane, at the first tile of the group of R
+  // tiles that the next refills load; slot j of a group is at +j*4352 bytes.
+  // Deep prefixes derive the scale address from the code address (fewer registers).
+  constexpr bool kScalePtr = D <= 2;
+  constexpr int SB = kScalePtr ? D : 1;
   const uint8_t* cb[D];
+  const uint8_t* sb[SB];
+  const uint32_t lane_off = warp * kRowBlockBytes + lane * 16, scale_off = warp * kRowBlockBytes + 512 + g * 4;
+  const uint32_t scale_rel = scale_off - lane_off;
 #pragma unroll
-  for (int s = 0; s < D; ++s)
-    cb[s] = p.planes[s] + static_cast<uint64_t>(t0) * kRecordBytes + warp * kRowBlockBytes + lane * 16;
-  const uint32_t sc_off = 512 - lane * 16 + g * 4;  // this lane's scale pair, relative to its codes
+  for (int s = 0; s < D; ++s) {
+    cb[s] = p.planes[s] + static_cast<uint64_t>(t0) * kRecordBytes + lane_off;
+    if (kScalePtr) sb[s < SB ? s : 0] = p.planes[s] + static_cast<uint64_t>(t0) * kRecordBytes + scale_off;
+  }
 
   // Register ring of R tiles x D stages.  A stage outside the CTA's units gets scale 0
   // (codes 0): its products are finite and its contribution is exactly zero.
   uint4 w[R][D];
   uint32_t sc[R][D];
-  auto load_tile = [&](int slot, uint32_t k, uint32_t mask) {
-    const uint64_t off = static_cast<uint64_t>(k) * kRecordBytes;
+  auto load_tile = [&](int slot, uint32_t mask) {
 #pragma unroll
     for (int s = 0; s < D; ++s) {
       if (D == 1 || (mask & (1u << s))) {
-        const uint8_t* a = cb[s] + off;
+        const uint8_t* a = cb[s] + slot * kRecordBytes;
+        const uint8_t* as = kScalePtr ? sb[s < SB ? s : 0] + slot * kRecordBytes : a + scale_rel;
         asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
                      : "=r"(w[slot][s].x), "=r"(w[slot][s].y), "=r"(w[slot][s].z), "=r"(w[slot][s].w)
                      : "l"(a));
-        asm volatile("ld.global.nc.L1::no_allocate.u32 %0, [%1];" : "=r"(sc[slot][s]) : "l"(a + sc_off));
+        asm volatile("ld.global.nc.L1::no_allocate.u32 %0, [%1];" : "=r"(sc[slot][s]) : "l"(as));
       } else {
         w[slot][s] = make_uint4(0u, 0u, 0u, 0u);
         sc[slot][s] = 0u;
       }
     }
   };
+  auto next_group = [&]() {
+#pragma unroll
+    for (int s = 0; s < D; ++s) {
+      cb[s] += R * kRecordBytes;
+      if (kScalePtr) sb[s < SB ? s : 0] += R * kRecordBytes;
+    }
+  };
 #pragma unroll
   for (int j = 0; j < R; ++j) {
     if (static_cast<uint32_t>(j) < ntiles)
-      load_tile(j, j, (j == 0 ? mask_first : kFull) & (static_cast<uint32_t>(j) == ntiles - 1 ? mask_last : kFull));
+      load_tile(j, (j == 0 ? mask_first : kFull) & (static_cast<uint32_t>(j) == ntiles - 1 ? mask_last : kFull));
   }
+  next_group();
   griddep_wait();
-  {  // activation fragments of the tile columns this CTA touches, and the zero block
+  {  // activation fragments of the tile columns this CTA touches
     const uint32_t c_first = t0 % p.C, c_last = t_end % p.C;
     const bool one_row = t0 / p.C == t_end / p.C;
     const uint32_t c_lo = one_row ? c_first : 0, c_hi = one_row ? c_last : p.C - 1;
@@ -1024,14 +1057,13 @@ __global__ void __launch_bounds__(kStreamThreads, (NB == 1 && XL == 1) ? 2 : 1)
     uint4* dst = reinterpret_cast<uint4*>(xres + c_lo * p.xslot_bytes);
     const uint32_t chunks = (c_hi - c_lo + 1) * p.xslot_bytes / 16;
     for (uint32_t t = threadIdx.x; t < chunks; t += kStreamThreads) dst[t] = __ldcg(src + t);
-    if (threadIdx.x < 16)
-      reinterpret_cast<uint4*>(xres + p.C * p.xslot_bytes)[threadIdx.x] = make_uint4(0u, 0u, 0u, 0u);
   }
   __syncthreads();
-  const uint8_t* zero = xres + p.C * p.xslot_bytes;
+  const XLane<NB, XL> xlane(p.batch, lane);
   const uint64_t units_per_row = static_cast<uint64_t>(p.C) * D;
-  uint32_t row = t0 / p.C, col = t0 % p.C;
-  uint32_t left = p.C - col;  // tiles of the current row still ahead (may run past ntiles)
+  uint32_t row = t0 / p.C;
+  const uint8_t* xs = xres + (t0 % p.C) * p.xslot_bytes;  // activation slot of the current tile
+  uint32_t left = p.C - t0 % p.C;  // tiles of the current row still ahead (may run past ntiles)
   float y[NB][4];
 #pragma unroll
   for (int nb = 0; nb < NB; ++nb)
@@ -1039,7 +1071,7 @@ __global__ void __launch_bounds__(kStreamThreads, (NB == 1 && XL == 1) ? 2 : 1)
     for (int e = 0; e < 4; ++e) y[nb][e] = 0.0f;
 
   // Tensor-core part of one tile from ring slot j: D independent MMA chains (two for
-  // D == 1), accumulators zeroed here.
+  // D == 1); the first MMA of each chain starts from zero.
   constexpr int CH = D == 1 ? 2 : D;
   auto mma_tile = [&](int j, const XFrag<NB, XL>& xf, float (&acc)[CH][NB][4]) {
     uint32_t hi[D][4];
@@ -1051,22 +1083,20 @@ __global__ void __launch_bounds__(kStreamThreads, (NB == 1 && XL == 1) ? 2 : 1)
       hi[s][3] = __umulhi(w[j][s].w, p.shift_mul);
     }
 #pragma unroll
-    for (int c = 0; c < CH; ++c)
-#pragma unroll
-      for (int nb = 0; nb < NB; ++nb)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) acc[c][nb][e] = 0.0f;
-#pragma unroll
     for (int m = 0; m < 8; ++m) {
 #pragma unroll
       for (int s = 0; s < D; ++s) {
         const int c = D == 1 ? (m & 1) : s;
+        const bool first = D == 1 ? m < 2 : m == 0;
         const uint32_t a0 = int2_pair(w[j][s].x, hi[s][0], m), a1 = int2_pair(w[j][s].y, hi[s][1], m);
         const uint32_t a2 = int2_pair(w[j][s].z, hi[s][2], m), a3 = int2_pair(w[j][s].w, hi[s][3], m);
 #pragma unroll
         for (int nb = 0; nb < NB; ++nb)
 #pragma unroll
-          for (int l = 0; l < XL; ++l) mma_f16(acc[c][nb], a0, a1, a2, a3, xf.bf[nb][l][m][0], xf.bf[nb][l][m][1]);
+          for (int l = 0; l < XL; ++l) {
+            if (first && l == 0) mma_f16_zero(acc[c][nb], a0, a1, a2, a3, xf.bf[nb][l][m][0], xf.bf[nb][l][m][1]);
+            else mma_f16(acc[c][nb], a0, a1, a2, a3, xf.bf[nb][l][m][0], xf.bf[nb][l][m][1]);
+          }
       }
     }
   };
@@ -1093,7 +1123,7 @@ __global__ void __launch_bounds__(kStreamThreads, (NB == 1 && XL == 1) ? 2 : 1)
   };
   // After tile k: the row may end (its last tile, or the CTA's last tile).
   auto advance = [&](uint32_t k) {
-    ++col;
+    xs += p.xslot_bytes;
     if (--left == 0 || k + 1 == ntiles) {
       finish_row<NB>(p, row, units_per_row, u0, u1, total, ctas, cta, y, rit0, q, s_info);
 #pragma unroll
@@ -1101,13 +1131,16 @@ __global__ void __launch_bounds__(kStreamThreads, (NB == 1 && XL == 1) ? 2 : 1)
 #pragma unroll
         for (int e = 0; e < 4; ++e) y[nb][e] = 0.0f;
       ++row;
-      col = 0;
+      xs = xres;
       left = p.C;
     }
   };
-  auto refill = [&](int j, uint32_t k) {  // slot j, just consumed by tile k
-    const uint32_t kn = k + R;
-    if (kn < ntiles) load_tile(j, kn, kn == ntiles - 1 ? mask_last : kFull);
+  auto one_tile = [&](int j) {
+    XFrag<NB, XL> xf;
+    load_xfrag<NB, XL>(xf, xlane, xs);
+    float acc[CH][NB][4];
+    mma_tile(j, xf, acc);
+    epi_tile(j, xf, acc);
   };
 
   uint32_t k0 = 0;
@@ -1115,24 +1148,18 @@ __global__ void __launch_bounds__(kStreamThreads, (NB == 1 && XL == 1) ? 2 : 1)
 #pragma unroll
     for (int j = 0; j < R; ++j) {
       const uint32_t k = k0 + j;
-      XFrag<NB, XL> xf;
-      load_xfrag<NB, XL>(xf, p, xres + col * p.xslot_bytes, zero, lane);
-      float acc[CH][NB][4];
-      mma_tile(j, xf, acc);
-      epi_tile(j, xf, acc);
-      refill(j, k);
+      one_tile(j);
+      const uint32_t kn = k + R;  // refill slot j with tile kn (group base cb/sb)
+      if (kn < ntiles) load_tile(j, kn == ntiles - 1 ? mask_last : kFull);
       advance(k);
     }
+    next_group();
   }
 #pragma unroll
   for (int j = 0; j < R; ++j) {  // the last partial group (no more loads)
     const uint32_t k = k0 + j;
     if (k >= ntiles) break;
-    XFrag<NB, XL> xf;
-    load_xfrag<NB, XL>(xf, p, xres + col * p.xslot_bytes, zero, lane);
-    float acc[CH][NB][4];
-    mma_tile(j, xf, acc);
-    epi_tile(j, xf, acc);
+    one_tile(j);
     advance(k);
   }
 }
