@@ -204,12 +204,22 @@ class ClockSampler:
 # ---------------------------------------------------------------------------------------
 # our arm
 
+def group_bytes(members, cols, prefix, batch=1):
+    """Algorithmic bytes of one launch over row-stacked members sharing one input: the
+    selected planes and scales of every member, the input once, every output."""
+    rows = sum(m["nrows"] for m in members)
+    return (prefix * (rows * cols // 4 + rows * (-(-cols // 128)) * 2) + 2 * cols * batch
+            + 2 * rows * batch)
+
+
 def build_workload(name, rank, world, device, rotation_target):
+    """The workload's layers as launch groups.  Layers that share their input (q, k, v;
+    gate, up) are row-stacked into one plane matrix and run as one GEMV launch, as a
+    fused QKV / gate-up projection does; every other layer is its own launch."""
     import harpq_b200 as hqb
 
     prefix, layers, std = WORKLOADS[name]
-    built = []
-    step_bytes = 0
+    groups: dict = {}
     for li, (lname, rows, cols, src) in enumerate(layers):
         codes, bits = make_layer(rows, cols, std, 1000 + li, device)
         r0, nrows = (0, rows) if world == 1 else hqb.shard_rows(rows, world, rank)
@@ -219,62 +229,76 @@ def build_workload(name, rank, world, device, rotation_target):
             bits = [b.contiguous() for b in bits]
         pm = hqb.PlaneMatrix.from_stages(nrows, cols, codes, bits)
         del codes, bits
-        built.append({"name": lname, "rows": rows, "cols": cols, "src": src, "r0": r0, "nrows": nrows,
-                      "copies": [pm]})
-        step_bytes += algorithmic_bytes(nrows, cols, prefix)
+        g = groups.setdefault(src, {"src": src, "cols": cols, "members": [], "mats": []})
+        g["members"].append({"name": lname, "rows": rows, "r0": r0, "nrows": nrows})
+        g["mats"].append(pm)
+    built = []
+    for g in groups.values():
+        mats = g.pop("mats")
+        stacked = mats[0] if len(mats) == 1 else hqb.PlaneMatrix.stack(mats)
+        del mats
+        g["name"] = "+".join(m["name"] for m in g["members"])
+        g["nrows"] = stacked.rows
+        g["copies"] = [stacked]
+        g["bytes"] = group_bytes(g["members"], g["cols"], prefix)
+        # every rank gathers the same slot size: the largest stacked shard
+        shard_rows = []
+        for r in range(world):
+            sizes = [hqb.shard_rows(m["rows"], world, r)[1] if world > 1 else m["rows"] for m in g["members"]]
+            shard_rows.append(sum(-(-n // 128) * 128 for n in sizes[:-1]) + sizes[-1])
+        g["slot_rows"] = max(shard_rows)
+        built.append(g)
     torch.cuda.synchronize()
-    plane_bytes_step = sum(sum(p.numel() for p in L["copies"][0].planes[:prefix]) for L in built)
+    torch.cuda.empty_cache()
+    step_bytes = sum(g["bytes"] for g in built)
+    plane_bytes_step = sum(sum(p.numel() for p in g["copies"][0].planes[:prefix]) for g in built)
     ncopies = max(2, -(-rotation_target // max(1, plane_bytes_step)))
-    import harpq_b200 as hqb  # noqa: F811
-
-    for L in built:
-        base = L["copies"][0]
+    for g in built:
+        base = g["copies"][0]
         for _ in range(ncopies - 1):
             cp = hqb.PlaneMatrix(base.rows, base.cols)
             cp.planes = [p.clone() for p in base.planes]
-            L["copies"].append(cp)
+            g["copies"].append(cp)
     torch.cuda.synchronize()
-    return prefix, built, step_bytes, ncopies
+    n_layers = len(layers)
+    return prefix, built, step_bytes, ncopies, n_layers
 
 
 def run_ours(args, rank, world, device):
     import harpq_b200 as hqb
 
     name = args.workload
-    prefix, layers, step_bytes, ncopies = build_workload(name, rank, world, device, 3 * L2_BYTES)
-    srcs = {}
-    for L in layers:
-        srcs.setdefault(L["src"], L["cols"])
+    prefix, groups, step_bytes, ncopies, n_layers = build_workload(name, rank, world, device, 3 * L2_BYTES)
+    srcs = {g["src"]: g["cols"] for g in groups}
     gen = torch.Generator(device=device)
     gen.manual_seed(7)
     x_dev = {s: torch.randn(1, k, generator=gen, device=device).half() for s, k in srcs.items()}
     xfrag = {s: hqb.prepare_x(x_dev[s]) for s in srcs}
-    y_loc = {L["name"]: torch.empty(1, L["nrows"], dtype=torch.float16, device=device) for L in layers}
-    y_full = {L["name"]: torch.empty(world, hqb.shard_pad_rows(L["rows"], world) if world > 1 else L["rows"],
-                                     dtype=torch.float16, device=device) for L in layers}
-    ws_bytes = max(L["copies"][0].workspace_bytes(1, hqb.F16) for L in layers)
+    y_loc = {g["name"]: torch.empty(1, g["nrows"], dtype=torch.float16, device=device) for g in groups}
+    y_full = {g["name"]: torch.empty(world, g["slot_rows"], dtype=torch.float16, device=device) for g in groups}
+    ws_bytes = max(g["copies"][0].workspace_bytes(1, hqb.F16) for g in groups)
     ws = hqb.Workspace(ws_bytes, device)
     # per step: one activation preparation per distinct input, and the launches of each
-    # layer's GEMV (the library's own dispatch rule)
-    launches_per_step = len(srcs) + sum(L["copies"][0].gemv_launches(1, hqb.F16, prefix, x_prepared=True)
-                                        for L in layers)
+    # group's GEMV (the library's own dispatch rule)
+    launches_per_step = len(srcs) + sum(g["copies"][0].gemv_launches(1, hqb.F16, prefix, x_prepared=True)
+                                        for g in groups)
 
-    def gather(L):
+    def gather(g):
         if world == 1:
             return
-        n = L["nrows"]
-        pad = y_full[L["name"]].shape[1]
-        send = y_loc[L["name"]] if n == pad else torch.nn.functional.pad(y_loc[L["name"]], (0, pad - n))
-        torch.distributed.all_gather_into_tensor(y_full[L["name"]].view(-1), send.view(-1))
+        n = g["nrows"]
+        pad = g["slot_rows"]
+        send = y_loc[g["name"]] if n == pad else torch.nn.functional.pad(y_loc[g["name"]], (0, pad - n))
+        torch.distributed.all_gather_into_tensor(y_full[g["name"]].view(-1), send.view(-1))
 
     def step(copy, x_src=None):
         for s in srcs:
             hqb.prepare_x(x_dev[s] if x_src is None else x_src[s], out=xfrag[s])
-        for L in layers:
-            pm = L["copies"][copy]
-            pm.gemv(x_dev[L["src"]], prefix=prefix, out=y_loc[L["name"]], workspace=ws,
-                    x_prepared=xfrag[L["src"]], flags=hqb.FLAG_PDL)
-            gather(L)
+        for g in groups:
+            pm = g["copies"][copy]
+            pm.gemv(x_dev[g["src"]], prefix=prefix, out=y_loc[g["name"]], workspace=ws,
+                    x_prepared=xfrag[g["src"]], flags=hqb.FLAG_PDL)
+            gather(g)
 
     # clocks are sampled from warm-up to the end of the e2e leg; the summary keeps the
     # samples that fall inside the timed region
@@ -322,9 +346,8 @@ def run_ours(args, rank, world, device):
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
         ms_max = float(t.item())
     ms_per_step = ms_max / args.steps
-    total_bytes = step_bytes * world  # every rank streams its own shard
-    if world > 1:
-        total_bytes = sum(algorithmic_bytes(L["rows"], L["cols"], prefix) for L in layers)
+    # whole-job bytes: the full (unsharded) layers, each input once per group
+    total_bytes = sum(group_bytes([{"nrows": m["rows"]} for m in g["members"]], g["cols"], prefix) for g in groups)
     value = total_bytes / (ms_per_step * 1e-3) / 1e9
 
     # ---- per-kernel roofline: each layer's GEMV launched back to back (PDL) inside one
@@ -333,19 +356,19 @@ def run_ours(args, rank, world, device):
     kern = {}
     tot_b, tot_ms = 0, 0.0
     per_graph = 4 * ncopies
-    for L in layers:
+    for G in groups:
         g = torch.cuda.CUDAGraph()
         side = torch.cuda.Stream()
         side.wait_stream(torch.cuda.current_stream())
         with torch.cuda.stream(side):
             for i in range(2):
-                L["copies"][i % ncopies].gemv(x_dev[L["src"]], prefix=prefix, out=y_loc[L["name"]], workspace=ws,
-                                              x_prepared=xfrag[L["src"]], flags=hqb.FLAG_PDL)
+                G["copies"][i % ncopies].gemv(x_dev[G["src"]], prefix=prefix, out=y_loc[G["name"]], workspace=ws,
+                                              x_prepared=xfrag[G["src"]], flags=hqb.FLAG_PDL)
         torch.cuda.current_stream().wait_stream(side)
         with torch.cuda.graph(g):
             for i in range(per_graph):
-                L["copies"][i % ncopies].gemv(x_dev[L["src"]], prefix=prefix, out=y_loc[L["name"]], workspace=ws,
-                                              x_prepared=xfrag[L["src"]], flags=hqb.FLAG_PDL)
+                G["copies"][i % ncopies].gemv(x_dev[G["src"]], prefix=prefix, out=y_loc[G["name"]], workspace=ws,
+                                              x_prepared=xfrag[G["src"]], flags=hqb.FLAG_PDL)
         for _ in range(3):
             g.replay()
         torch.cuda.synchronize()
@@ -357,24 +380,25 @@ def run_ours(args, rank, world, device):
         torch.cuda.synchronize()
         per_launch_ms = e0.elapsed_time(e1) / (5 * per_graph)
         del g
-        b = algorithmic_bytes(L["nrows"], L["cols"], prefix)
-        kern[L["name"]] = {"us": round(per_launch_ms * 1e3, 3), "gbs": round(b / (per_launch_ms * 1e-3) / 1e9, 1)}
+        b = G["bytes"]
+        kern[G["name"]] = {"us": round(per_launch_ms * 1e3, 3), "gbs": round(b / (per_launch_ms * 1e-3) / 1e9, 1),
+                           "rows": G["nrows"], "cols": G["cols"]}
         tot_b += b
         tot_ms += per_launch_ms
     achieved = tot_b / (tot_ms * 1e-3) / 1e9
 
     # ---- e2e through the public API: pinned host x -> device, GEMVs, device -> host y
     host_x = {s: x_dev[s].cpu().pin_memory() for s in srcs}
-    host_y = {L["name"]: torch.empty_like(y_full[L["name"]] if world > 1 else y_loc[L["name"]], device="cpu").pin_memory()
-              for L in layers}
+    host_y = {g["name"]: torch.empty_like(y_full[g["name"]] if world > 1 else y_loc[g["name"]], device="cpu").pin_memory()
+              for g in groups}
     x_stage = {s: torch.empty_like(x_dev[s]) for s in srcs}
 
     def e2e_step(copy):
         for s in srcs:
             x_stage[s].copy_(host_x[s], non_blocking=True)
         step(copy, x_src=x_stage)
-        for L in layers:
-            host_y[L["name"]].copy_(y_full[L["name"]] if world > 1 else y_loc[L["name"]], non_blocking=True)
+        for g in groups:
+            host_y[g["name"]].copy_(y_full[g["name"]] if world > 1 else y_loc[g["name"]], non_blocking=True)
 
     for i in range(3):
         e2e_step(i % ncopies)
@@ -404,7 +428,7 @@ def run_ours(args, rank, world, device):
         "steps": args.steps,
         "warmup": args.warmup,
         "ms_per_step": round(ms_per_step, 5),
-        "us_per_layer": round(ms_per_step * 1e3 / len(layers), 3),
+        "us_per_layer": round(ms_per_step * 1e3 / n_layers, 3),
         "higher_is_better": True,
         "scaling": "strong",
         "vs_baseline": None,
@@ -412,7 +436,9 @@ def run_ours(args, rank, world, device):
         "data": "synthetic: seeded N(0,std) weights quantized by the reference LS int2 fit (GPU restatement), "
                 "seeded N(0,1) FP16 activations",
         "config": {"workload": name, "prefix": prefix, "batch": 1,
-                   "layers": [[L["name"], L["nrows"], L["cols"]] for L in layers],
+                   "layers": [[m["name"], m["rows"], g["cols"]] for g in groups for m in g["members"]],
+                   "launches": [[g["name"], g["nrows"], g["cols"]] for g in groups],
+                   "grouping": "layers sharing an input run as one row-stacked launch",
                    "parallelism": f"row-shard{world}+allgather" if world > 1 else "single",
                    "l2": f"{ncopies} rotating weight copies, {ncopies * step_bytes / 2**20:.0f} MiB > 3x L2",
                    "graph": use_graph},
@@ -434,9 +460,9 @@ def run_ours(args, rank, world, device):
     result["roofline"] = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                           "frac": round(achieved / peak, 4),
                           "peak_source": "measured" if "hbm_gbs" in peaks else "fallback",
-                          "traffic": None if traffic is None else round(traffic * tot_b / len(layers)),
+                          "traffic": None if traffic is None else round(traffic * tot_b / len(groups)),
                           "kernel": f"hqb::gemv_uniform_kernel<1,1,{prefix}> (+ hqb::fixup_kernel of split rows)",
-                          "achieved_note": "algorithmic bytes of one launch per layer / sum of the layers' "
+                          "achieved_note": "algorithmic bytes of one launch per group / sum of the groups' "
                                            "average launch durations (CUDA events around graphs of back-to-back "
                                            "launches)"}
     return result
@@ -488,7 +514,10 @@ def time_reference(name, steps, warmup, device, threads=None, budget_s=None):
     threads = threads or os.cpu_count() or 1
     prefix, mats, xs = reference_inputs(name, device)
     runners = [(lname, src, m, refcpu.ShardedReference(m, threads)) for lname, src, m in mats]
-    step_bytes = sum(algorithmic_bytes(m.rows, m.cols, prefix) for _, _, m, _ in runners)
+    by_src: dict = {}
+    for _, src, m, _ in runners:
+        by_src.setdefault(src, (m.cols, []))[1].append({"nrows": m.rows})
+    step_bytes = sum(group_bytes(members, cols, prefix) for cols, members in by_src.values())
 
     def one():
         for _, src, _, r in runners:

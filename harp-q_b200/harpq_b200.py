@@ -214,6 +214,37 @@ class PlaneMatrix:
         self.planes.append(plane)
 
     @classmethod
+    def stack(cls, mats: Sequence["PlaneMatrix"]) -> "PlaneMatrix":
+        """Row-stacked matrix of matrices with equal column counts.  Matrices that share
+        their input (q|k|v, gate|up) then run as one GEMV launch.  Tile records are
+        tile-row major, so stacking is concatenation of the plane buffers.  Member i's
+        outputs are rows [row_offsets[i], row_offsets[i] + member_rows[i]) of the result
+        (split_rows).  Offsets are multiples of 128: a member whose row count is not a
+        multiple of 128 keeps its zero padding rows inside the stack.  The stack holds
+        the stages that every member holds."""
+        if not mats:
+            raise ValueError("nothing to stack")
+        cols = mats[0].cols
+        if any(m.cols != cols for m in mats):
+            raise ValueError("stacked matrices need equal column counts")
+        offsets, r = [], 0
+        for m in mats:
+            offsets.append(r)
+            r += m.grid_rows * TILE
+        out = cls(offsets[-1] + mats[-1].rows, cols, device=mats[0].device)
+        stages = min(m.stage_count for m in mats)
+        out.planes = [torch.cat([m.planes[s] for m in mats]) for s in range(stages)]
+        out.row_offsets = offsets
+        out.member_rows = [m.rows for m in mats]
+        return out
+
+    def split_rows(self, y: torch.Tensor) -> list[torch.Tensor]:
+        """Views of each member's outputs in a stacked matrix's result [..., rows]."""
+        offsets = getattr(self, "row_offsets", [0])
+        rows = getattr(self, "member_rows", [self.rows])
+        return [y[..., o:o + n] for o, n in zip(offsets, rows)]
+
+    @classmethod
     def from_stages(cls, rows: int, cols: int, codes: Sequence[torch.Tensor], fp16_scale_bits: Sequence[torch.Tensor],
                     stream=None) -> "PlaneMatrix":
         m = cls(rows, cols, device=codes[0].device)

@@ -268,3 +268,28 @@ def test_pdl_launch_matches_plain_launch(rows, cols):
         torch.cuda.synchronize()
         assert torch.equal(a, b), f"p{p}"
     assert ws.error_flags() == 0
+
+
+def test_row_stacked_matrices_match_members():
+    """A row-stack of matrices that share their input (fused q|k|v style) computes every
+    member's GEMV in one launch; each member's slice equals its own GEMV, and padding
+    rows of a member inside the stack decode to zero."""
+    import harpq_b200 as hqb
+
+    rng = np.random.default_rng(77)
+    members = [random_matrix(rng, r, 300, stages=3) for r in (256, 200, 130)]
+    pms = [plane_matrix(m) for m in members]
+    stack = hqb.PlaneMatrix.stack(pms)
+    assert stack.row_offsets == [0, 256, 512] and stack.rows == 512 + 130
+    x = torch.from_numpy(rng.standard_normal((2, 300)).astype(np.float32)).cuda().half()
+    for p in (1, 3):
+        ys = stack.split_rows(stack.gemv(x, prefix=p, y_dtype=torch.float32))
+        for pm, m, got in zip(pms, members, ys):
+            want = pm.gemv(x, prefix=p, y_dtype=torch.float32)
+            assert_close(got.cpu().numpy(), want.cpu().numpy(), 2e-4, 2e-4, f"stacked member p{p}")
+            assert got.shape[-1] == m.rows
+    w = stack.decode(3).cpu().numpy()
+    assert w[:256].tobytes() == orc.dequantize_prefix(members[0], 3).tobytes()
+    assert w[256:456].tobytes() == orc.dequantize_prefix(members[1], 3).tobytes()
+    assert np.all(w[456:512] == 0.0)
+    assert w[512:].tobytes() == orc.dequantize_prefix(members[2], 3).tobytes()
