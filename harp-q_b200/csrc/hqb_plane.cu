@@ -57,6 +57,7 @@ struct GemvParams {
   const uint8_t* depth;  // [R][C] or null (uniform)
   const uint32_t* plan;  // [R+1] or null
   const uint8_t* xfrag;
+  const void* x_raw;   // raw activations [batch][cols] when the GEMV prepares them itself
   const void* bias;
   void* y;
   float* partials;     // [G][2][batch][128]
@@ -75,6 +76,9 @@ struct GemvParams {
   uint32_t pdl;          // launched as a programmatic dependent
   uint32_t x_resident;   // all activation fragments staged once per CTA (else one per slot)
   uint32_t slot_x_bytes; // activation bytes carried by each slot (0 when resident)
+  uint32_t cols;         // original columns (raw activation rows)
+  uint32_t x_vec;        // raw activation rows can be read as aligned 16-byte chunks
+  uint32_t raw_offset;   // shared-memory offset of the raw activation staging area
   int bias_dtype;
   int y_dtype;
 };
@@ -981,6 +985,104 @@ __device__ __forceinline__ void finish_row(const GemvParams& p, uint32_t r, uint
   if (info & 1u) reduce_split_row<NB>(p, r, s_info[1], s_info[2], info >> 1);
 }
 
+// 2^k as a float for -126 <= k <= 127 (normal range), from the IEEE-754 bit layout.
+__device__ __forceinline__ float exp2_int(int k) { return __int_as_float((k + 127) << 23); }
+
+// Tile columns a CTA needs: one range [a0, a1], plus [b0, b1] when its tiles wrap from
+// the end of one tile row into the start of the next without covering every column.
+struct ColRanges {
+  uint32_t a0, a1, b0, b1;  // b1 < b0: no second range
+  __device__ __forceinline__ uint32_t count() const { return (a1 - a0 + 1) + (b1 >= b0 ? b1 - b0 + 1 : 0); }
+  __device__ __forceinline__ uint32_t col(uint32_t i) const { return i <= a1 - a0 ? a0 + i : b0 + (i - (a1 - a0 + 1)); }
+};
+
+__device__ __forceinline__ ColRanges needed_columns(uint32_t t0, uint32_t t_end, uint32_t C) {
+  const uint32_t r0 = t0 / C, r1 = t_end / C, c0 = t0 - r0 * C, c1 = t_end - r1 * C;
+  if (r0 == r1) return ColRanges{c0, c1, 1, 0};
+  if (r1 == r0 + 1 && c1 + 1 < c0) return ColRanges{c0, C - 1, 0, c1};
+  return ColRanges{0, C - 1, 1, 0};
+}
+
+// Activation fragments of the needed tile columns, built from raw x (FP16 for XL 1,
+// FP32 for XL 2) by the CTA itself with the arithmetic of prep_x_kernel (same tile
+// exponent, same rounding, same summation order), so they are bit-identical to a
+// separately prepared buffer.  Raw rows are first staged in shared memory at `raw`
+// ([batch][C * 128], only the needed columns filled).
+template <int XL>
+__device__ __forceinline__ void build_xfrag_tiles(const GemvParams& p, uint8_t* xres, uint8_t* raw,
+                                                  const ColRanges& cr) {
+  using XT = typename std::conditional<XL == 1, __half, float>::type;
+  constexpr uint32_t ES = sizeof(XT);
+  const uint32_t ncol = cr.count(), span = p.C * 128;
+  const XT* x = static_cast<const XT*>(p.x_raw);
+  if (p.x_vec) {  // cols * ES is a multiple of 16: a chunk lies wholly inside or outside a row
+    constexpr uint32_t per_chunk = 16 / ES, chunks_col = 128 / per_chunk;
+    const uint32_t chunks_row = ncol * chunks_col;
+    for (uint32_t t = threadIdx.x; t < chunks_row * p.batch; t += kStreamThreads) {
+      const uint32_t b = t / chunks_row, i = t - b * chunks_row, ci = i / chunks_col;
+      const uint32_t col = cr.col(ci) * 128 + (i - ci * chunks_col) * per_chunk;
+      uint4 v = make_uint4(0u, 0u, 0u, 0u);
+      if (col < p.cols) v = __ldcg(reinterpret_cast<const uint4*>(x + static_cast<uint64_t>(b) * p.cols + col));
+      *reinterpret_cast<uint4*>(raw + (static_cast<uint64_t>(b) * span + col) * ES) = v;
+    }
+  } else {
+    const uint32_t per_row = ncol * 128;
+    for (uint32_t t = threadIdx.x; t < per_row * p.batch; t += kStreamThreads) {
+      const uint32_t b = t / per_row, i = t - b * per_row;
+      const uint32_t col = cr.col(i >> 7) * 128 + (i & 127);
+      XT v{};
+      if (col < p.cols) v = x[static_cast<uint64_t>(b) * p.cols + col];
+      reinterpret_cast<XT*>(raw)[static_cast<uint64_t>(b) * span + col] = v;
+    }
+  }
+  __syncthreads();
+  const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t m = lane & 7, which = (lane >> 3) & 3, jj = m & 3;  // lane + 32i has the same m, which
+  for (uint32_t item = warp; item < ncol * p.batch; item += kStreamThreads / 32) {
+    const uint32_t ci = item / p.batch, b = item - ci * p.batch, c = cr.col(ci);
+    const XT* rx = reinterpret_cast<const XT*>(raw) + static_cast<uint64_t>(b) * span + c * 128;
+    float v[4], a = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      if constexpr (XL == 1) v[i] = __half2float(rx[lane + 32 * i]);
+      else v[i] = rx[lane + 32 * i];
+      a = fmaxf(a, fabsf(v[i]));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
+    // tile exponent: the largest |x| lands in [2^14, 2^15); |x| >= 2^-24 is a normal float
+    int e = 0;
+    if (a > 0.0f) e = max(-100, min(100, ((__float_as_int(a) >> 23) & 0xff) - 127 - 14));
+    const float down = exp2_int(-e - 2 * static_cast<int>(jj)), up = exp2_int(2 * static_cast<int>(jj));
+    uint8_t* slot = xres + c * p.xslot_bytes;
+    float part[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {  // column lane + 32i: q = i
+      const float xs = v[i] * down;
+      const __half hi = __float2half_rn(xs);
+      float eff = __half2float(hi);
+      const uint32_t idx = (b * 4 + i) * 32 + m * 4 + which;
+      reinterpret_cast<__half*>(slot)[idx] = hi;
+      if constexpr (XL == 2) {
+        const __half lo = __float2half_rn(xs - eff);
+        eff += __half2float(lo);
+        reinterpret_cast<__half*>(slot + p.batch * 256)[idx] = lo;
+      }
+      part[i] = eff * up;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) part[i] += __shfl_xor_sync(0xffffffffu, part[i], o);
+    }
+    if (lane == 0) {
+      const float sum = (part[0] + part[1]) + (part[2] + part[3]);
+      *reinterpret_cast<float2*>(slot + p.batch * 256 * XL + b * 8) =
+          make_float2(exp2_int(24 + e), sum * exp2_int(e + 1));
+    }
+  }
+}
+
 template <int NB, int XL, int D>
 __global__ void __launch_bounds__(kStreamThreads, (NB == 1 && XL == 1) ? 2 : 1)
     gemv_uniform_kernel(const __grid_constant__ GemvParams p) {
@@ -1053,10 +1155,14 @@ __global__ void __launch_bounds__(kStreamThreads, (NB == 1 && XL == 1) ? 2 : 1)
     const uint32_t c_first = t0 % p.C, c_last = t_end % p.C;
     const bool one_row = t0 / p.C == t_end / p.C;
     const uint32_t c_lo = one_row ? c_first : 0, c_hi = one_row ? c_last : p.C - 1;
-    const uint4* src = reinterpret_cast<const uint4*>(p.xfrag + static_cast<uint64_t>(c_lo) * p.xslot_bytes);
-    uint4* dst = reinterpret_cast<uint4*>(xres + c_lo * p.xslot_bytes);
-    const uint32_t chunks = (c_hi - c_lo + 1) * p.xslot_bytes / 16;
-    for (uint32_t t = threadIdx.x; t < chunks; t += kStreamThreads) dst[t] = __ldcg(src + t);
+    if (p.x_raw != nullptr) {
+      build_xfrag_tiles<XL>(p, xres, xres + p.raw_offset, needed_columns(t0, t_end, p.C));
+    } else {
+      const uint4* src = reinterpret_cast<const uint4*>(p.xfrag + static_cast<uint64_t>(c_lo) * p.xslot_bytes);
+      uint4* dst = reinterpret_cast<uint4*>(xres + c_lo * p.xslot_bytes);
+      const uint32_t chunks = (c_hi - c_lo + 1) * p.xslot_bytes / 16;
+      for (uint32_t t = threadIdx.x; t < chunks; t += kStreamThreads) dst[t] = __ldcg(src + t);
+    }
   }
   __syncthreads();
   const XLane<NB, XL> xlane(p.batch, lane);
@@ -1399,6 +1505,8 @@ RingShape ring_shape(uint32_t slot_x, uint32_t cap, uint32_t resident) {
 }
 
 constexpr uint32_t kXResidentMax = 64 * 1024;
+// Shared memory for in-kernel activation preparation: fragments plus staged raw rows.
+constexpr uint64_t kFusedXMax = 96 * 1024;
 
 uint32_t gemv_smem_cap() {
   uint32_t m = 0;
@@ -1590,7 +1698,15 @@ HQB_API int hqb_gemv_ex(const hqb_plane_matrix* m, uint32_t prefix, const uint8_
   }
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   const uint8_t* xfrag = static_cast<const uint8_t*>(x);
-  if (!x_prepared) {
+  // The uniform streaming kernel prepares raw activations itself when they fit beside
+  // the fragments in shared memory (no separate preparation launch).
+  const uint32_t xslot = xslot_bytes_for(batch, xl);
+  const uint64_t x_all_bytes = static_cast<uint64_t>(m->grid_cols) * xslot;
+  const bool streaming_path = !simt && x_all_bytes <= kXResidentMax && !(flags & HQB_FLAG_RING);
+  const uint64_t raw_offset = round_up(x_all_bytes, 16);
+  const uint64_t raw_bytes = static_cast<uint64_t>(m->grid_cols) * 128 * batch * (xl == 1 ? 2 : 4);
+  const bool fuse_prep = !x_prepared && !mixed && streaming_path && raw_offset + raw_bytes <= kFusedXMax;
+  if (!x_prepared && !fuse_prep) {
     e = launch_prep(x, x_dtype, m->cols, batch, ws + L.xfrag, st);
     if (e != cudaSuccess) {
       cudaGetLastError();
@@ -1617,6 +1733,12 @@ HQB_API int hqb_gemv_ex(const hqb_plane_matrix* m, uint32_t prefix, const uint8_
   p.xslot_bytes = xslot_bytes_for(batch, xl);
   p.bias_dtype = bias_dtype;
   p.y_dtype = y_dtype;
+  p.cols = static_cast<uint32_t>(m->cols);
+  if (fuse_prep) {
+    p.x_raw = x;
+    p.raw_offset = static_cast<uint32_t>(raw_offset);
+    p.x_vec = ((reinterpret_cast<uintptr_t>(x) & 15u) == 0 && (m->cols * (xl == 1 ? 2 : 4)) % 16 == 0) ? 1u : 0u;
+  }
   const uint64_t tiles = static_cast<uint64_t>(m->grid_rows) * m->grid_cols;
   p.total = mixed ? 0 : tiles * prefix;
   const bool streaming = !simt && static_cast<uint64_t>(m->grid_cols) * p.xslot_bytes <= kXResidentMax &&
@@ -1633,7 +1755,9 @@ HQB_API int hqb_gemv_ex(const hqb_plane_matrix* m, uint32_t prefix, const uint8_
   p.slot_stride = rs.stride;
   p.shift_mul = 1u << 24;
   p.pdl = (flags & HQB_FLAG_PDL) ? 1u : 0u;
-  const uint32_t smem = streaming ? static_cast<uint32_t>(x_all) + 256 : rs.smem;
+  const uint32_t smem = !streaming ? rs.smem
+                       : fuse_prep ? static_cast<uint32_t>(raw_offset + raw_bytes)
+                                   : static_cast<uint32_t>(x_all) + 256;
   const uint32_t threads = streaming ? kStreamThreads : kGemvThreads;
   const int per_sm = ctas_per_sm(k, smem, device, threads);
   if (per_sm <= 0) return cudaErrorLaunchOutOfResources;

@@ -296,12 +296,17 @@ class PlaneMatrix:
         """Kernels one gemv() call launches, by the library's dispatch rule: activation
         preparation unless x is prepared; the GEMV; and, unless the uniform streaming
         kernel runs (it reduces split tile rows itself), the split-row fix-up."""
-        n = 0 if x_prepared else 1
         if not mixed and prefix == 0:
             return 1  # bias / zero fill only
         xl = 2 if x_dtype == F32 else 1
         xslot = -(-(batch * (256 * xl + 8)) // 16) * 16
         streaming = not (flags & FLAG_SIMT) and self.grid_cols * xslot <= 64 * 1024 and not (flags & FLAG_RING)
+        # the uniform streaming kernel prepares raw activations itself when fragments and
+        # staged raw rows fit its shared memory
+        raw_offset = -(-(self.grid_cols * xslot) // 16) * 16
+        raw_bytes = self.grid_cols * 128 * batch * (2 if xl == 1 else 4)
+        fused = streaming and not mixed and raw_offset + raw_bytes <= 96 * 1024
+        n = 0 if (x_prepared or fused) else 1
         n += 1
         if not (streaming and not mixed):
             n += 1

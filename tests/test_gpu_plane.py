@@ -293,3 +293,25 @@ def test_row_stacked_matrices_match_members():
     assert w[256:456].tobytes() == orc.dequantize_prefix(members[1], 3).tobytes()
     assert np.all(w[456:512] == 0.0)
     assert w[512:].tobytes() == orc.dequantize_prefix(members[2], 3).tobytes()
+
+
+@pytest.mark.parametrize("cols,xdt,misalign", [(300, torch.float16, False), (300, torch.float32, False),
+                                               (1000, torch.float16, False), (1000, torch.float16, True),
+                                               (1027, torch.float32, True), (4096, torch.float32, False)])
+def test_in_kernel_activation_prep_matches_prepared(cols, xdt, misalign):
+    """Raw activations prepared inside the GEMV (vector or scalar staging) give the
+    bit-identical result of a separately prepared buffer."""
+    import harpq_b200 as hqb
+
+    rng = np.random.default_rng(cols)
+    pm = plane_matrix(random_matrix(rng, 384, cols))
+    for batch in (1, 5, 12):
+        off = 1 if misalign else 0
+        buf = torch.randn(batch * cols + off, device="cuda").to(xdt)
+        buf[off:off + cols] *= 40.0  # a wide dynamic range inside tiles
+        x = buf[off:].view(batch, cols)
+        xf = hqb.prepare_x(x)
+        for p in (1, 4):
+            ya = pm.gemv(x, prefix=p, y_dtype=torch.float32, x_prepared=xf)
+            yb = pm.gemv(x, prefix=p, y_dtype=torch.float32)
+            assert torch.equal(ya, yb), (batch, p)
