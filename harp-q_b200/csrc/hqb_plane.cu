@@ -919,19 +919,72 @@ __device__ __forceinline__ void load_xfrag(XFrag<NB, XL>& xf, const XLane<NB, XL
   }
 }
 
-// Sum of split tile row r over its contributing CTAs first..last in CTA order, plus
-// bias (the same arithmetic as fixup_kernel).  Run by every thread of the CTA that
-// finished the row last; partials are read through L2.
+// A CTA's part of the split tile rows it touches: at most its first and its last row.
+struct SplitRows {
+  uint32_t row0, row1;
+  uint32_t count;
+};
+
+// End of tile row r for this CTA (units [u0, u1)).  A row wholly inside the range is
+// stored.  A split row is published as this CTA's part (slot 0 for the CTA's first
+// row, 1 for its last) and remembered; finish_split_rows completes it.  No fence and
+// no barrier here, so the stream of tiles goes on.
 template <int NB>
-__device__ __noinline__ void reduce_split_row(const GemvParams& p, uint32_t r, uint32_t first, uint32_t last,
-                                              uint32_t first_slot) {
+__device__ __forceinline__ void end_row(const GemvParams& p, uint32_t r, uint64_t units_per_row, uint64_t u0,
+                                        uint64_t u1, uint32_t cta, const float (&y)[NB][4], uint32_t rit0, uint32_t q,
+                                        SplitRows& split) {
+  const uint64_t rb = static_cast<uint64_t>(r) * units_per_row, re = rb + units_per_row;
+  if (rb >= u0 && re <= u1) {
+    store_out<NB>(p, y, r * 128 + rit0, q);
+    return;
+  }
+  publish_partial<NB>(p, cta, rb <= u0 ? 0u : 1u, y, rit0, q);
+  if (split.count == 0) split.row0 = r;
+  else split.row1 = r;
+  ++split.count;
+}
+
+// After the CTA's last tile: one fence and barrier, then one arrival per split row
+// (per-row counter; the contributor that arrives last resets it).  The last
+// contributor of a row sums the parts of all contributors in CTA order plus bias (the
+// arithmetic of fixup_kernel), reading them through L2.  Nothing waits on another CTA.
+template <int NB>
+__device__ __forceinline__ void finish_split_rows(const GemvParams& p, const SplitRows& split,
+                                                  uint64_t units_per_row, uint64_t total, uint32_t ctas,
+                                                  uint32_t* s_info) {
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    uint32_t n = 0;
+    for (uint32_t i = 0; i < split.count; ++i) {
+      const uint32_t r = i == 0 ? split.row0 : split.row1;
+      const uint64_t rb = static_cast<uint64_t>(r) * units_per_row, re = rb + units_per_row;
+      const uint32_t first = unit_owner(rb, total, ctas), last = unit_owner(re - 1, total, ctas);
+      if (atomicAdd(p.counters + r, 1u) == last - first) {  // every other contributor has published
+        p.counters[r] = 0u;                                    // ready for the next launch
+        s_info[1 + 4 * n] = r;
+        s_info[2 + 4 * n] = first;
+        s_info[3 + 4 * n] = last;
+        s_info[4 + 4 * n] = unit_start(first, total, ctas) < rb ? 1u : 0u;
+        ++n;
+      }
+    }
+    s_info[0] = n;
+    __threadfence();
+  }
+  __syncthreads();
+  const uint32_t n = s_info[0];
+  if (n == 0) return;
   const uint64_t cta_stride = 2ull * p.batch * 128;
-  for (uint32_t e = threadIdx.x; e < p.batch * 128; e += kStreamThreads) {
-    const uint32_t b = e >> 7, rit = e & 127, row = r * 128 + rit;
+  const uint32_t per_row = p.batch * 128;
+  for (uint32_t e = threadIdx.x; e < n * per_row; e += kStreamThreads) {
+    const uint32_t k = e / per_row, rem = e - k * per_row, b = rem >> 7, rit = rem & 127;
+    const uint32_t r = s_info[1 + 4 * k], first = s_info[2 + 4 * k], last = s_info[3 + 4 * k];
+    const uint32_t row = r * 128 + rit;
     if (row >= p.rows) continue;
     const float* src = p.partials + static_cast<uint64_t>(b) * 128 + rit;
     float sum = 0.0f;
-    sum += __ldcg(src + first * cta_stride + first_slot * p.batch * 128);
+    sum += __ldcg(src + first * cta_stride + s_info[4 + 4 * k] * p.batch * 128);
     uint32_t i = first + 1;
     for (; i + 4 <= last + 1; i += 4) {
       const float v0 = __ldcg(src + i * cta_stride), v1 = __ldcg(src + (i + 1) * cta_stride);
@@ -949,40 +1002,6 @@ __device__ __noinline__ void reduce_split_row(const GemvParams& p, uint32_t r, u
     if (p.y_dtype == HQB_F16) static_cast<__half*>(p.y)[o] = __float2half_rn(sum);
     else static_cast<float*>(p.y)[o] = sum;
   }
-}
-
-// End of tile row r for this CTA (units [u0, u1)).  A row wholly inside the range is
-// stored.  A split row is published as this CTA's part; the contributor that arrives
-// last (per-row counter, reset by that contributor) sums all parts.  Nothing waits.
-// CTA-uniform: every thread calls it at the same point.
-template <int NB>
-__device__ __forceinline__ void finish_row(const GemvParams& p, uint32_t r, uint64_t units_per_row, uint64_t u0,
-                                           uint64_t u1, uint64_t total, uint32_t ctas, uint32_t cta,
-                                           const float (&y)[NB][4], uint32_t rit0, uint32_t q, uint32_t* s_info) {
-  const uint64_t rb = static_cast<uint64_t>(r) * units_per_row, re = rb + units_per_row;
-  if (rb >= u0 && re <= u1) {
-    store_out<NB>(p, y, r * 128 + rit0, q);
-    return;
-  }
-  publish_partial<NB>(p, cta, rb <= u0 ? 0u : 1u, y, rit0, q);
-  __threadfence();
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    const uint32_t first = unit_owner(rb, total, ctas), last = unit_owner(re - 1, total, ctas);
-    const uint32_t old = atomicAdd(p.counters + r, 1u);
-    uint32_t info = 0;
-    if (old == last - first) {  // every other contributor has published
-      p.counters[r] = 0u;         // ready for the next launch
-      info = 1u | (unit_start(first, total, ctas) < rb ? 2u : 0u);
-      s_info[1] = first;
-      s_info[2] = last;
-    }
-    s_info[0] = info;
-    __threadfence();
-  }
-  __syncthreads();
-  const uint32_t info = s_info[0];
-  if (info & 1u) reduce_split_row<NB>(p, r, s_info[1], s_info[2], info >> 1);
 }
 
 // 2^k as a float for -126 <= k <= 127 (normal range), from the IEEE-754 bit layout.
@@ -1038,47 +1057,73 @@ __device__ __forceinline__ void build_xfrag_tiles(const GemvParams& p, uint8_t* 
   __syncthreads();
   const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t m = lane & 7, which = (lane >> 3) & 3, jj = m & 3;  // lane + 32i has the same m, which
-  for (uint32_t item = warp; item < ncol * p.batch; item += kStreamThreads / 32) {
-    const uint32_t ci = item / p.batch, b = item - ci * p.batch, c = cr.col(ci);
-    const XT* rx = reinterpret_cast<const XT*>(raw) + static_cast<uint64_t>(b) * span + c * 128;
-    float v[4], a = 0.0f;
+  // Two (column, batch row) items per warp at a time: their shuffle chains interleave.
+  constexpr int W = 2;
+  constexpr uint32_t kWarps = kStreamThreads / 32;
+  const uint32_t items = ncol * p.batch;
+  for (uint32_t base = warp; base < items; base += W * kWarps) {
+    float v[W][4], a[W];
+    uint32_t b[W], c[W];
+    bool ok[W];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      if constexpr (XL == 1) v[i] = __half2float(rx[lane + 32 * i]);
-      else v[i] = rx[lane + 32 * i];
-      a = fmaxf(a, fabsf(v[i]));
-    }
+    for (int w = 0; w < W; ++w) {
+      const uint32_t item = base + w * kWarps;
+      ok[w] = item < items;
+      const uint32_t it = ok[w] ? item : base;
+      const uint32_t ci = it / p.batch;
+      b[w] = it - ci * p.batch;
+      c[w] = cr.col(ci);
+      const XT* rx = reinterpret_cast<const XT*>(raw) + static_cast<uint64_t>(b[w]) * span + c[w] * 128;
+      a[w] = 0.0f;
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
-    // tile exponent: the largest |x| lands in [2^14, 2^15); |x| >= 2^-24 is a normal float
-    int e = 0;
-    if (a > 0.0f) e = max(-100, min(100, ((__float_as_int(a) >> 23) & 0xff) - 127 - 14));
-    const float down = exp2_int(-e - 2 * static_cast<int>(jj)), up = exp2_int(2 * static_cast<int>(jj));
-    uint8_t* slot = xres + c * p.xslot_bytes;
-    float part[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {  // column lane + 32i: q = i
-      const float xs = v[i] * down;
-      const __half hi = __float2half_rn(xs);
-      float eff = __half2float(hi);
-      const uint32_t idx = (b * 4 + i) * 32 + m * 4 + which;
-      reinterpret_cast<__half*>(slot)[idx] = hi;
-      if constexpr (XL == 2) {
-        const __half lo = __float2half_rn(xs - eff);
-        eff += __half2float(lo);
-        reinterpret_cast<__half*>(slot + p.batch * 256)[idx] = lo;
+      for (int i = 0; i < 4; ++i) {
+        if constexpr (XL == 1) v[w][i] = __half2float(rx[lane + 32 * i]);
+        else v[w][i] = rx[lane + 32 * i];
+        a[w] = fmaxf(a[w], fabsf(v[w][i]));
       }
-      part[i] = eff * up;
     }
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
+    for (int o = 16; o > 0; o >>= 1)
 #pragma unroll
-      for (int i = 0; i < 4; ++i) part[i] += __shfl_xor_sync(0xffffffffu, part[i], o);
+      for (int w = 0; w < W; ++w) a[w] = fmaxf(a[w], __shfl_xor_sync(0xffffffffu, a[w], o));
+    float part[W][4];
+    int e[W];
+#pragma unroll
+    for (int w = 0; w < W; ++w) {
+      // tile exponent: the largest |x| lands in [2^14, 2^15); |x| >= 2^-24 is a normal float
+      e[w] = 0;
+      if (a[w] > 0.0f) e[w] = max(-100, min(100, ((__float_as_int(a[w]) >> 23) & 0xff) - 127 - 14));
+      const float down = exp2_int(-e[w] - 2 * static_cast<int>(jj)), up = exp2_int(2 * static_cast<int>(jj));
+      uint8_t* slot = xres + c[w] * p.xslot_bytes;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {  // column lane + 32i: q = i
+        const float xs = v[w][i] * down;
+        const __half hi = __float2half_rn(xs);
+        float eff = __half2float(hi);
+        const uint32_t idx = (b[w] * 4 + i) * 32 + m * 4 + which;
+        if (ok[w]) reinterpret_cast<__half*>(slot)[idx] = hi;
+        if constexpr (XL == 2) {
+          const __half lo = __float2half_rn(xs - eff);
+          eff += __half2float(lo);
+          if (ok[w]) reinterpret_cast<__half*>(slot + p.batch * 256)[idx] = lo;
+        }
+        part[w][i] = eff * up;
+      }
     }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+      for (int w = 0; w < W; ++w)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) part[w][i] += __shfl_xor_sync(0xffffffffu, part[w][i], o);
     if (lane == 0) {
-      const float sum = (part[0] + part[1]) + (part[2] + part[3]);
-      *reinterpret_cast<float2*>(slot + p.batch * 256 * XL + b * 8) =
-          make_float2(exp2_int(24 + e), sum * exp2_int(e + 1));
+#pragma unroll
+      for (int w = 0; w < W; ++w) {
+        if (!ok[w]) continue;
+        const float sum = (part[w][0] + part[w][1]) + (part[w][2] + part[w][3]);
+        *reinterpret_cast<float2*>(xres + c[w] * p.xslot_bytes + p.batch * 256 * XL + b[w] * 8) =
+            make_float2(exp2_int(24 + e[w]), sum * exp2_int(e[w] + 1));
+      }
     }
   }
 }
@@ -1089,7 +1134,7 @@ __global__ void __launch_bounds__(kStreamThreads, (NB == 1 && XL == 1) ? 2 : 1)
   constexpr int R = TilesAhead<D>::value;
   constexpr uint32_t kFull = (1u << D) - 1u;
   extern __shared__ __align__(16) uint8_t xres[];  // [C x xslot activation fragments]
-  __shared__ uint32_t s_info[3];
+  __shared__ uint32_t s_info[9];
   const uint64_t total = p.total;
   const uint32_t ctas = static_cast<uint32_t>(total < gridDim.x ? total : gridDim.x), cta = blockIdx.x;
   griddep_launch_dependents();  // a following PDL kernel may be scheduled; it waits for this grid
@@ -1228,10 +1273,11 @@ __global__ void __launch_bounds__(kStreamThreads, (NB == 1 && XL == 1) ? 2 : 1)
     }
   };
   // After tile k: the row may end (its last tile, or the CTA's last tile).
+  SplitRows split{0u, 0u, 0u};
   auto advance = [&](uint32_t k) {
     xs += p.xslot_bytes;
     if (--left == 0 || k + 1 == ntiles) {
-      finish_row<NB>(p, row, units_per_row, u0, u1, total, ctas, cta, y, rit0, q, s_info);
+      end_row<NB>(p, row, units_per_row, u0, u1, cta, y, rit0, q, split);
 #pragma unroll
       for (int nb = 0; nb < NB; ++nb)
 #pragma unroll
@@ -1268,6 +1314,7 @@ __global__ void __launch_bounds__(kStreamThreads, (NB == 1 && XL == 1) ? 2 : 1)
     one_tile(j);
     advance(k);
   }
+  if (split.count != 0) finish_split_rows<NB>(p, split, units_per_row, total, ctas, s_info);
 }
 
 // Split tile rows: the parts of the contributing CTAs, summed in CTA order, plus
@@ -1507,6 +1554,7 @@ RingShape ring_shape(uint32_t slot_x, uint32_t cap, uint32_t resident) {
 constexpr uint32_t kXResidentMax = 64 * 1024;
 // Shared memory for in-kernel activation preparation: fragments plus staged raw rows.
 constexpr uint64_t kFusedXMax = 96 * 1024;
+constexpr uint64_t kFusedTilesMax = 24;
 
 uint32_t gemv_smem_cap() {
   uint32_t m = 0;
@@ -1705,7 +1753,11 @@ HQB_API int hqb_gemv_ex(const hqb_plane_matrix* m, uint32_t prefix, const uint8_
   const bool streaming_path = !simt && x_all_bytes <= kXResidentMax && !(flags & HQB_FLAG_RING);
   const uint64_t raw_offset = round_up(x_all_bytes, 16);
   const uint64_t raw_bytes = static_cast<uint64_t>(m->grid_cols) * 128 * batch * (xl == 1 ? 2 : 4);
-  const bool fuse_prep = !x_prepared && !mixed && streaming_path && raw_offset + raw_bytes <= kFusedXMax;
+  // Each CTA builds the fragments of the columns its tiles touch; when CTAs hold more
+  // than kFusedTilesMax tiles on average, one preparation launch shared by all is cheaper.
+  const uint64_t avg_tiles = static_cast<uint64_t>(m->grid_rows) * m->grid_cols / (static_cast<uint64_t>(sms) * 2);
+  const bool fuse_prep = !x_prepared && !mixed && streaming_path && raw_offset + raw_bytes <= kFusedXMax &&
+                         avg_tiles <= kFusedTilesMax;
   if (!x_prepared && !fuse_prep) {
     e = launch_prep(x, x_dtype, m->cols, batch, ws + L.xfrag, st);
     if (e != cudaSuccess) {

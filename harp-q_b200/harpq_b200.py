@@ -305,7 +305,9 @@ class PlaneMatrix:
         # staged raw rows fit its shared memory
         raw_offset = -(-(self.grid_cols * xslot) // 16) * 16
         raw_bytes = self.grid_cols * 128 * batch * (2 if xl == 1 else 4)
-        fused = streaming and not mixed and raw_offset + raw_bytes <= 96 * 1024
+        sms = torch.cuda.get_device_properties(self.device).multi_processor_count
+        avg_tiles = self.grid_rows * self.grid_cols // (sms * 2)
+        fused = streaming and not mixed and raw_offset + raw_bytes <= 96 * 1024 and avg_tiles <= 24
         n = 0 if (x_prepared or fused) else 1
         n += 1
         if not (streaming and not mixed):
