@@ -944,24 +944,30 @@ __device__ __forceinline__ void end_row(const GemvParams& p, uint32_t r, uint64_
   ++split.count;
 }
 
-// After the CTA's last tile: one fence and barrier, then one arrival per split row
-// (per-row counter; the contributor that arrives last resets it).  The last
-// contributor of a row sums the parts of all contributors in CTA order plus bias (the
-// arithmetic of fixup_kernel), reading them through L2.  Nothing waits on another CTA.
+// After the CTA's last tile: one barrier, then one arrival per split row on a per-row
+// counter (acquire-release atomics issued together by one thread; the barrier orders
+// every thread's published part before that thread's release).  The contributor that
+// arrives last resets the counter and sums the parts of all contributors in CTA order
+// plus bias (the arithmetic of fixup_kernel), reading them through L2.  Nothing waits
+// on another CTA.
 template <int NB>
 __device__ __forceinline__ void finish_split_rows(const GemvParams& p, const SplitRows& split,
                                                   uint64_t units_per_row, uint64_t total, uint32_t ctas,
                                                   uint32_t* s_info) {
-  __threadfence();
   __syncthreads();
   if (threadIdx.x == 0) {
+    const uint32_t r0 = split.row0, r1 = split.row1;
+    const uint32_t old0 = atom_add_acq_rel_gpu(p.counters + r0, 1u);
+    const uint32_t old1 = split.count > 1 ? atom_add_acq_rel_gpu(p.counters + r1, 1u) : 0u;
     uint32_t n = 0;
-    for (uint32_t i = 0; i < split.count; ++i) {
-      const uint32_t r = i == 0 ? split.row0 : split.row1;
+#pragma unroll
+    for (uint32_t i = 0; i < 2; ++i) {
+      if (i >= split.count) break;
+      const uint32_t r = i == 0 ? r0 : r1;
       const uint64_t rb = static_cast<uint64_t>(r) * units_per_row, re = rb + units_per_row;
       const uint32_t first = unit_owner(rb, total, ctas), last = unit_owner(re - 1, total, ctas);
-      if (atomicAdd(p.counters + r, 1u) == last - first) {  // every other contributor has published
-        p.counters[r] = 0u;                                    // ready for the next launch
+      if ((i == 0 ? old0 : old1) == last - first) {  // every other contributor has published
+        p.counters[r] = 0u;                           // ready for the next launch
         s_info[1 + 4 * n] = r;
         s_info[2 + 4 * n] = first;
         s_info[3 + 4 * n] = last;
@@ -970,7 +976,6 @@ __device__ __forceinline__ void finish_split_rows(const GemvParams& p, const Spl
       }
     }
     s_info[0] = n;
-    __threadfence();
   }
   __syncthreads();
   const uint32_t n = s_info[0];
@@ -984,17 +989,19 @@ __device__ __forceinline__ void finish_split_rows(const GemvParams& p, const Spl
     if (row >= p.rows) continue;
     const float* src = p.partials + static_cast<uint64_t>(b) * 128 + rit;
     float sum = 0.0f;
-    sum += __ldcg(src + first * cta_stride + s_info[4 + 4 * k] * p.batch * 128);
-    uint32_t i = first + 1;
-    for (; i + 4 <= last + 1; i += 4) {
-      const float v0 = __ldcg(src + i * cta_stride), v1 = __ldcg(src + (i + 1) * cta_stride);
-      const float v2 = __ldcg(src + (i + 2) * cta_stride), v3 = __ldcg(src + (i + 3) * cta_stride);
-      sum += v0;
-      sum += v1;
-      sum += v2;
-      sum += v3;
+    // contributors in groups of 8: the loads of a group are independent, the sum is in order
+    for (uint32_t i0 = first; i0 <= last; i0 += 8) {
+      float v[8];
+#pragma unroll
+      for (uint32_t j = 0; j < 8; ++j) {
+        const uint32_t i = i0 + j;
+        const uint64_t off = i * cta_stride + (i == first ? s_info[4 + 4 * k] * p.batch * 128 : 0u);
+        v[j] = i <= last ? __ldcg(src + off) : 0.0f;
+      }
+#pragma unroll
+      for (uint32_t j = 0; j < 8; ++j)
+        if (i0 + j <= last) sum += v[j];
     }
-    for (; i <= last; ++i) sum += __ldcg(src + i * cta_stride);
     if (p.bias != nullptr)
       sum += p.bias_dtype == HQB_F16 ? __half2float(static_cast<const __half*>(p.bias)[row])
                                      : static_cast<const float*>(p.bias)[row];
