@@ -305,7 +305,8 @@ def run_ours(args, rank, world, device):
         step(i % ncopies)
     torch.cuda.synchronize()
 
-    use_graph = world == 1 and not args.no_graph
+    # one CUDA graph per weight copy; at N > 1 it includes the NCCL all-gathers
+    use_graph = not args.no_graph
     graphs = []
     if use_graph:
         for c in range(ncopies):
@@ -415,6 +416,8 @@ def run_ours(args, rank, world, device):
     d2h = sum(y.numel() * 2 for y in host_y.values())
 
     clk.__exit__(None, None, None)
+    del graphs  # graphs holding NCCL work are released before the process group is destroyed
+    torch.cuda.synchronize()
     flags = ws.error_flags()
     result = {
         "metric": METRIC,
@@ -474,6 +477,94 @@ def _recorded_traffic_ratio():
     except OSError:
         pass
     return None
+
+
+# ---------------------------------------------------------------------------------------
+# supplementary single-GPU measurements (BASELINE configs 4 and 5, and the sharded
+# workload at one GPU); weights are random codes and scales: timing does not depend on
+# their values
+
+def _random_plane_matrix(rows, cols, gen, device):
+    import harpq_b200 as hqb
+
+    g = hqb.geometry(rows, cols)
+    codes, bits = [], []
+    for _ in range(4):
+        codes.append(torch.randint(0, 256, (g.padded_rows * g.padded_columns // 4,), dtype=torch.uint8,
+                                   device=device, generator=gen))
+        sc = (torch.rand(g.padded_rows // 128 * (g.padded_columns // 128) * 128, device=device, generator=gen)
+              * 0.01 + 1e-3).half()
+        bits.append(sc.view(torch.int16))
+    return hqb.PlaneMatrix.from_stages(rows, cols, codes, bits)
+
+
+def _graph_us(fn, launches, reps=5):
+    """Average µs per call of fn(i) over a CUDA graph of `launches` calls."""
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        for i in range(2):
+            fn(i)
+    torch.cuda.current_stream().wait_stream(side)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for i in range(launches):
+            fn(i)
+    for _ in range(2):
+        g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        g.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) * 1e3 / (reps * launches)
+
+
+def supplementary(device):
+    import harpq_b200 as hqb
+
+    gen = torch.Generator(device=device)
+    gen.manual_seed(11)
+    out = {}
+    # config 4: mixed depth, 11008x4096, per-tile depth uniform in {1..4} (seed 7), batch 1
+    copies = [_random_plane_matrix(11008, 4096, gen, device) for _ in range(4)]
+    gr, gc = copies[0].grid_rows, copies[0].grid_cols
+    depth = torch.from_numpy(np.random.default_rng(7).integers(1, 5, size=(gr, gc)).astype(np.uint8)).to(device)
+    plan = hqb.DepthPlan(depth, 4)
+    x = torch.randn(1, 4096, device=device, generator=gen).half()
+    y = torch.empty(1, 11008, device=device, dtype=torch.float16)
+    ws = hqb.Workspace(copies[0].workspace_bytes(16, hqb.F16), device)
+    mixed_bytes = int(depth.sum().item()) * 4352 + 2 * 4096 + 2 * 11008
+    us = _graph_us(lambda i: copies[i % 4].gemv(x, depth=plan, out=y, workspace=ws, flags=hqb.FLAG_PDL), 32)
+    uni = {p: _graph_us(lambda i: copies[i % 4].gemv(x, prefix=p, out=y, workspace=ws, flags=hqb.FLAG_PDL), 32)
+           for p in (2, 3)}
+    out["mixed_depth_11008x4096"] = {"us": round(us, 3), "gbs": round(mixed_bytes / (us * 1e-6) / 1e9, 1),
+                                     "mean_depth": round(mixed_bytes / (gr * gc * 4352), 3),
+                                     "uniform_p2_us": round(uni[2], 3), "uniform_p3_us": round(uni[3], 3)}
+    # config 5: small batch at prefix 4, tensor-core kernel vs the CUDA-core comparison kernel
+    sb = {}
+    for rows in (4096, 11008):
+        mats = copies if rows == 11008 else [_random_plane_matrix(4096, 4096, gen, device) for _ in range(4)]
+        for batch in (2, 4, 8, 16):
+            xb = torch.randn(batch, 4096, device=device, generator=gen).half()
+            yb = torch.empty(batch, rows, device=device, dtype=torch.float16)
+            nbytes = 4 * 17 * rows * 4096 // 64 + 2 * 4096 * batch + 2 * rows * batch
+            flops = 2.0 * batch * rows * 4096 * 4
+            t = _graph_us(lambda i: mats[i % 4].gemv(xb, prefix=4, out=yb, workspace=ws, flags=hqb.FLAG_PDL), 32)
+            e = {"tensor_us": round(t, 3), "tensor_gbs": round(nbytes / (t * 1e-6) / 1e9, 1),
+                 "tensor_tflops": round(flops / (t * 1e-6) / 1e12, 2)}
+            if batch <= 8:
+                t2 = _graph_us(lambda i: mats[i % 4].gemv(xb, prefix=4, out=yb, workspace=ws,
+                                                          flags=hqb.FLAG_SIMT), 32)
+                e.update({"simt_us": round(t2, 3), "simt_gbs": round(nbytes / (t2 * 1e-6) / 1e9, 1)})
+            sb[f"{rows}x4096_b{batch}"] = e
+        del mats
+    out["small_batch_p4"] = sb
+    del copies
+    torch.cuda.empty_cache()
+    return out
 
 
 # ---------------------------------------------------------------------------------------
@@ -564,6 +655,7 @@ def main(argv=None) -> int:
     ap.add_argument("--workload", default="auto", choices=["auto", *WORKLOADS])
     ap.add_argument("--no-graph", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extras", action="store_true", help="skip the supplementary single-GPU measurements")
     args = ap.parse_args(argv)
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -589,6 +681,13 @@ def main(argv=None) -> int:
     import harpq_b200  # noqa: F401  (fails loudly when the library is missing)
 
     result = run_ours(args, rank, world, device)
+    if rank == 0 and world == 1 and not args.no_extras:
+        result["supplementary"] = supplementary(device)
+        if args.workload == "llama7b_block_p2":
+            # the sharded workload at one GPU, the N=1 point of the multi-GPU series
+            sub = argparse.Namespace(**{**vars(args), "workload": "llama70b_mlp_p3", "steps": min(args.steps, 200)})
+            r70 = run_ours(sub, rank, world, device)
+            result["supplementary"]["llama70b_mlp_p3_n1"] = {k: r70[k] for k in ("value", "unit", "ms_per_step")}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cb = time_reference(args.workload, 3, 1, device, budget_s=20.0)
         result["cpu_baseline"] = {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")}
