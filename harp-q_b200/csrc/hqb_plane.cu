@@ -953,7 +953,7 @@ __device__ __forceinline__ void end_row(const GemvParams& p, uint32_t r, uint64_
 template <int NB>
 __device__ __forceinline__ void finish_split_rows(const GemvParams& p, const SplitRows& split,
                                                   uint64_t units_per_row, uint64_t total, uint32_t ctas,
-                                                  uint32_t* s_info) {
+                                                  uint32_t* s_info, uint32_t nthreads = kStreamThreads) {
   __syncthreads();
   if (threadIdx.x == 0) {
     const uint32_t r0 = split.row0, r1 = split.row1;
@@ -982,7 +982,7 @@ __device__ __forceinline__ void finish_split_rows(const GemvParams& p, const Spl
   if (n == 0) return;
   const uint64_t cta_stride = 2ull * p.batch * 128;
   const uint32_t per_row = p.batch * 128;
-  for (uint32_t e = threadIdx.x; e < n * per_row; e += kStreamThreads) {
+  for (uint32_t e = threadIdx.x; e < n * per_row; e += nthreads) {
     const uint32_t k = e / per_row, rem = e - k * per_row, b = rem >> 7, rit = rem & 127;
     const uint32_t r = s_info[1 + 4 * k], first = s_info[2 + 4 * k], last = s_info[3 + 4 * k];
     const uint32_t row = r * 128 + rit;
@@ -1324,6 +1324,317 @@ __global__ void __launch_bounds__(kStreamThreads, (NB == 1 && XL == 1) ? 2 : 1)
   if (split.count != 0) finish_split_rows<NB>(p, split, units_per_row, total, ctas, s_info);
 }
 
+// --------------------------------------------------------------------------------------
+// tcgen05 GEMV (batch <= 8, FP16 activations, uniform depth)
+//
+// The contraction runs on the 5th-generation tensor cores: per stage of a tile, 8 warps
+// decode the int2 codes into FP16 (the code+2 subnormal trick) and store them into tensor
+// memory as the A operand (TMEM lane = tile row); one thread issues 8 UMMAs
+// (M=128, N=16, K=16 each, kind::f16) whose B operand is the tile column's prepared
+// activations in shared memory and whose FP32 accumulators live in tensor memory; warps
+// 0..3 read the accumulators back and apply the per-row, per-stage scales.  A producer
+// warp streams each tile's stage records plus its activation block into a shared-memory
+// ring with 1-D bulk copies (no multicast).
+//
+// Activation block of one tile column (prep_x_tc_kernel), kTcColBytes:
+//   [u = 0..7][n-group 0..1][k-half 0..1][n % 8][8 halves]  UMMA B operand, canonical
+//     K-major layout: UMMA u covers lane-quad q = u/2 and word half s = u%2 of the
+//     plane record; its k = 2m + t is tile column 32q + 16s + 8t + m, scaled 4^-(m%4)
+//   [16 x {2^(24+e), 2^(e+1) * sum}]                     per batch row
+//
+// TMEM columns: A operand double buffer [0, 128) (64 columns = 128 FP16 per stage),
+// accumulators [128, 256): tile parity * 64 + stage * 16.
+
+constexpr uint32_t kTcBBytes = 4096;
+constexpr uint32_t kTcColBytes = kTcBBytes + 16 * 8;
+constexpr uint32_t kTcThreads = 320;  // warps 0-7 decode (0-3 also epilogue), 8 producer, 9 MMA issuer
+constexpr uint32_t kTcTmemCols = 256;
+constexpr uint32_t kTcRingBudget = 150 * 1024;
+
+__host__ __device__ inline uint32_t tc_slot_bytes(uint32_t d) {
+  return (d * kRecordBytes + kTcColBytes + 127u) / 128u * 128u;
+}
+
+// x [batch][cols] FP16 -> per tile column the UMMA B operand + {factor, correction}, the
+// same values as prep_x_kernel (tile exponent, rounding, summation order).  Batch rows
+// batch..15 are written as zeros.  Grid (C, 16), 128 threads.
+__global__ void __launch_bounds__(128) prep_x_tc_kernel(const __half* __restrict__ x, uint32_t cols, uint32_t batch,
+                                                        uint8_t* __restrict__ xtc) {
+  __shared__ float red[4];
+  const uint32_t c = blockIdx.x, b = blockIdx.y, k = threadIdx.x;
+  const uint32_t col = c * 128 + k;
+  float v = 0.0f;
+  if (b < batch && col < cols) v = __half2float(x[static_cast<uint64_t>(b) * cols + col]);
+  float a = fabsf(v);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
+  if ((k & 31) == 0) red[k >> 5] = a;
+  __syncthreads();
+  const float amax = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+  __syncthreads();
+  int e = 0;
+  if (amax > 0.0f) e = max(-100, min(100, ilogbf(amax) - 14));
+  const uint32_t m = k & 7, which = (k >> 3) & 3, q = k >> 5, jj = m & 3;
+  const float xs = ldexpf(v, -e - 2 * static_cast<int>(jj));
+  const __half hi = __float2half_rn(xs);
+  const float eff = __half2float(hi);
+  const uint32_t u = 2 * q + (which >> 1), kk = 2 * m + (which & 1);
+  uint8_t* slot = xtc + static_cast<uint64_t>(c) * kTcColBytes;
+  const uint32_t off = u * 512 + (b >> 3) * 256 + (kk >> 3) * 128 + (b & 7) * 16 + (kk & 7) * 2;
+  *reinterpret_cast<__half*>(slot + off) = hi;
+  float xt = ldexpf(eff, 2 * static_cast<int>(jj));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) xt += __shfl_xor_sync(0xffffffffu, xt, o);
+  if ((k & 31) == 0) red[k >> 5] = xt;
+  __syncthreads();
+  if (k == 0) {
+    const float sum = (red[0] + red[1]) + (red[2] + red[3]);
+    *reinterpret_cast<float2*>(slot + kTcBBytes + b * 8) = make_float2(ldexpf(1.0f, 24 + e), ldexpf(sum, e + 1));
+  }
+}
+
+// Bounded mbarrier wait that gives up at once after any earlier timeout of this CTA.
+__device__ __forceinline__ bool tc_wait(uint64_t* bar, uint32_t parity, const GemvParams& p, volatile uint32_t* abort) {
+  if (*abort) return false;
+  if (mbar_wait(bar, parity, p.error)) return true;
+  *abort = 1u;
+  return false;
+}
+
+template <int D>
+__global__ void __launch_bounds__(kTcThreads, 1) gemv_tc_kernel(const __grid_constant__ GemvParams p) {
+  extern __shared__ __align__(128) uint8_t sm[];
+  const uint32_t S = p.ring_slots, SB = p.slot_stride;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sm + S * SB);
+  uint64_t* empty = full + S;
+  uint64_t* a_full = empty + S;   // [2] A buffer written (8 warps)
+  uint64_t* a_empty = a_full + 2; // [2] A buffer consumed (MMA commit)
+  uint64_t* d_full = a_empty + 2; // [2] tile accumulators ready (MMA commit)
+  uint64_t* d_empty = d_full + 2; // [2] tile accumulators read (4 epilogue warps)
+  uint32_t* misc = reinterpret_cast<uint32_t*>(d_empty + 2);  // [0] TMEM base, [1] abort, [2] split count, [3..] s_info
+  volatile uint32_t* abort = misc + 1;
+  const uint64_t total = p.total;
+  const uint32_t ctas = static_cast<uint32_t>(total < gridDim.x ? total : gridDim.x), cta = blockIdx.x;
+  griddep_launch_dependents();
+  if (cta >= ctas) return;
+  const uint64_t u0 = unit_start(cta, total, ctas), u1 = unit_start(cta + 1, total, ctas);
+  const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t t0 = static_cast<uint32_t>(u0 / D), s0 = static_cast<uint32_t>(u0 % D);
+  const uint32_t t_end = static_cast<uint32_t>((u1 - 1) / D), s_end = static_cast<uint32_t>((u1 - 1) % D) + 1;
+  const uint32_t ntiles = t_end - t0 + 1;
+  constexpr uint32_t kFull = (1u << D) - 1u;
+  const uint32_t mask_first = kFull & ~((1u << s0) - 1u), mask_last = (1u << s_end) - 1u;
+  auto tile_mask = [&](uint32_t k) {
+    return (k == 0 ? mask_first : kFull) & (k == ntiles - 1 ? mask_last : kFull);
+  };
+  if (threadIdx.x == 0) {
+    for (uint32_t i = 0; i < S; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 4);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&a_full[i], 8);
+      mbar_init(&a_empty[i], 1);
+      mbar_init(&d_full[i], 1);
+      mbar_init(&d_empty[i], 4);
+    }
+    misc[1] = 0u;
+    misc[2] = 0u;
+    fence_barrier_init();
+  }
+  if (warp == 9) {
+    tmem_alloc(&misc[0], kTcTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = misc[0];
+  SplitRows split{0u, 0u, 0u};
+
+  if (warp == 8) {
+    // ---- producer: stage records of tile t0+k and its column's activation block
+    if (lane == 0) {
+      const uint64_t pol_w = policy_evict_first(), pol_x = policy_evict_last();
+      auto issue = [&](uint32_t k, bool weights, bool acts) {
+        const uint32_t slot = k % S, mask = tile_mask(k);
+        uint8_t* dst = sm + slot * SB;
+        const uint64_t tile = static_cast<uint64_t>(t0) + k;
+        if (weights) {
+          uint32_t bytes = kTcColBytes;
+#pragma unroll
+          for (int s = 0; s < D; ++s) bytes += (mask >> s & 1u) ? kRecordBytes : 0u;
+          mbar_expect_tx(&full[slot], bytes);
+#pragma unroll
+          for (int s = 0; s < D; ++s)
+            if (mask >> s & 1u) bulk_load(dst + s * kRecordBytes, p.planes[s] + tile * kRecordBytes, kRecordBytes,
+                                          &full[slot], pol_w);
+        }
+        if (acts) {
+          const uint32_t c = static_cast<uint32_t>(tile % p.C);
+          bulk_load(dst + D * kRecordBytes, p.xfrag + static_cast<uint64_t>(c) * kTcColBytes, kTcColBytes,
+                    &full[slot], pol_x);
+        }
+      };
+      const uint32_t first = ntiles < S ? ntiles : S;
+      for (uint32_t k = 0; k < first; ++k) issue(k, true, false);  // weights do not depend on earlier kernels
+      griddep_wait();
+      for (uint32_t k = 0; k < first; ++k) issue(k, false, true);
+      for (uint32_t k = first; k < ntiles; ++k) {
+        if (!tc_wait(&empty[k % S], ((k / S) - 1) & 1, p, abort)) break;
+        issue(k, true, true);
+      }
+    }
+  } else if (warp == 9) {
+    // ---- MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc = (1u << 4) | ((16u >> 3) << 17) | ((128u >> 4) << 24);  // F32 += F16 x F16, N 16, M 128
+      for (uint32_t k = 0; k < ntiles; ++k) {
+        const uint32_t slot = k % S, par = k & 1;
+        const uint32_t b_addr = smem_u32(sm + slot * SB + D * kRecordBytes);
+        bool ok = true;
+        for (uint32_t s = 0; s < D && ok; ++s) {
+          const uint32_t z = k * D + s, buf = z & 1;
+          ok = tc_wait(&a_full[buf], (z >> 1) & 1, p, abort);
+          if (ok && s == 0 && k >= 2) ok = tc_wait(&d_empty[par], ((k >> 1) - 1) & 1, p, abort);
+          if (!ok) break;
+          tc_fence_after();
+#pragma unroll
+          for (uint32_t u = 0; u < 8; ++u)
+            tc_mma_f16_ts(tmem + 128 + par * 64 + s * 16, tmem + buf * 64 + u * 8,
+                          umma_desc_kmajor(b_addr + u * 512, 128, 256), idesc, u > 0 ? 1u : 0u);
+          tc_commit(&a_empty[buf]);
+        }
+        if (!ok) break;
+        tc_commit(&d_full[par]);
+      }
+    }
+  } else {
+    // ---- decode warps 0..7: lane quadrant warp % 4 (tile rows), column half warp / 4
+    griddep_wait();  // outputs and partials are written only after earlier kernels complete
+    const uint32_t quad = warp & 3, colhalf = warp >> 2;
+    const uint32_t rit = quad * 32 + lane;  // tile row of this thread
+    const uint32_t rb = rit >> 4, gg = rit & 7, half = (rit >> 3) & 1;
+    // this row's four words of its column half: lane quads q = 2*colhalf, +1, words s = 0, 1
+    const uint32_t word_off = rb * kRowBlockBytes + (4 * gg + 2 * colhalf) * 16 + half * 4;
+    const uint32_t scale_off = rb * kRowBlockBytes + 512 + 4 * gg + 2 * half;
+    const uint32_t lane_taddr = tmem + ((quad * 32u) << 16);
+    const uint64_t units_per_row = static_cast<uint64_t>(p.C) * D;
+    float y[8];
+#pragma unroll
+    for (int b = 0; b < 8; ++b) y[b] = 0.0f;
+    uint32_t row = t0 / p.C, left = p.C - t0 % p.C;
+
+    auto epilogue = [&](uint32_t kk) -> bool {
+      const uint32_t par = kk & 1, slot = kk % S, mask = tile_mask(kk);
+      if (!tc_wait(&d_full[par], (kk >> 1) & 1, p, abort)) return false;
+      tc_fence_after();
+      const uint8_t* rec = sm + slot * SB;
+      const float2* fg = reinterpret_cast<const float2*>(rec + D * kRecordBytes + kTcBBytes);
+#pragma unroll
+      for (int s = 0; s < D; ++s) {
+        uint32_t acc[8];
+        tc_ld_x8(lane_taddr + 128 + par * 64 + s * 16, acc);
+        tc_wait_ld();
+        const float sigma = (mask >> s & 1u)
+                                ? half_bits_to_float(*reinterpret_cast<const uint16_t*>(rec + s * kRecordBytes + scale_off))
+                                : 0.0f;
+#pragma unroll
+        for (int b = 0; b < 8; ++b) {
+          if (static_cast<uint32_t>(b) < p.batch) {
+            const float2 f = fg[b];
+            y[b] = fmaf(sigma, fmaf(__uint_as_float(acc[b]), f.x, -f.y), y[b]);
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&d_empty[par]);
+        mbar_arrive(&empty[slot]);
+      }
+      // end of a tile row for this CTA: store or publish the row's outputs
+      if (--left == 0 || kk + 1 == ntiles) {
+        const uint64_t rb_u = static_cast<uint64_t>(row) * units_per_row, re_u = rb_u + units_per_row;
+        const uint32_t out_row = row * 128 + rit;
+        if (rb_u >= u0 && re_u <= u1) {
+          if (out_row < p.rows) {
+            float bias = 0.0f;
+            if (p.bias != nullptr)
+              bias = p.bias_dtype == HQB_F16 ? __half2float(static_cast<const __half*>(p.bias)[out_row])
+                                             : static_cast<const float*>(p.bias)[out_row];
+#pragma unroll
+            for (int b = 0; b < 8; ++b) {
+              if (static_cast<uint32_t>(b) >= p.batch) break;
+              const uint64_t o = static_cast<uint64_t>(b) * p.rows + out_row;
+              if (p.y_dtype == HQB_F16) static_cast<__half*>(p.y)[o] = __float2half_rn(y[b] + bias);
+              else static_cast<float*>(p.y)[o] = y[b] + bias;
+            }
+          }
+        } else {
+          float* part = p.partials + static_cast<uint64_t>(cta * 2 + (rb_u <= u0 ? 0u : 1u)) * p.batch * 128;
+#pragma unroll
+          for (int b = 0; b < 8; ++b)
+            if (static_cast<uint32_t>(b) < p.batch) part[b * 128 + rit] = y[b];
+          if (split.count == 0) split.row0 = row;
+          else split.row1 = row;
+          ++split.count;
+        }
+#pragma unroll
+        for (int b = 0; b < 8; ++b) y[b] = 0.0f;
+        ++row;
+        left = p.C;
+      }
+      return true;
+    };
+
+    bool ok = true;
+    for (uint32_t k = 0; k < ntiles && ok; ++k) {
+      const uint32_t slot = k % S;
+      ok = tc_wait(&full[slot], (k / S) & 1, p, abort);
+      const uint8_t* rec = sm + slot * SB;
+      for (uint32_t s = 0; s < D && ok; ++s) {
+        const uint32_t z = k * D + s, buf = z & 1;
+        if (z >= 2) ok = tc_wait(&a_empty[buf], ((z >> 1) - 1) & 1, p, abort);
+        if (!ok) break;
+        const uint8_t* r = rec + s * kRecordBytes + word_off;
+        const uint32_t w[4] = {lds32(r), lds32(r + 8), lds32(r + 16), lds32(r + 24)};
+        uint32_t a[32];
+#pragma unroll
+        for (int wi = 0; wi < 4; ++wi) {
+          const uint32_t h = __umulhi(w[wi], p.shift_mul);
+#pragma unroll
+          for (int m = 0; m < 8; ++m) a[wi * 8 + m] = int2_pair(w[wi], h, m);
+        }
+        tc_st_x32(lane_taddr + buf * 64 + colhalf * 32, a);
+        tc_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&a_full[buf]);
+      }
+      if (ok && colhalf == 0 && k >= 1) ok = epilogue(k - 1);
+    }
+    if (ok && colhalf == 0 && ntiles >= 1) ok = epilogue(ntiles - 1);
+    if (threadIdx.x == 0) {
+      misc[2] = split.count;
+      misc[12] = split.row0;
+      misc[13] = split.row1;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  // split tile rows: thread 0 holds this CTA's list (a CTA-uniform decision)
+  const uint32_t nsplit = misc[2];
+  if (nsplit != 0 && *abort == 0u) {
+    SplitRows sp{misc[12], misc[13], nsplit};
+    finish_split_rows<1>(p, sp, static_cast<uint64_t>(p.C) * D, total, ctas, misc + 3, kTcThreads);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 9) tmem_dealloc(tmem, kTcTmemCols);
+}
+
 // Split tile rows: the parts of the contributing CTAs, summed in CTA order, plus
 // bias.  Launched as a programmatic dependent of the GEMV; griddepcontrol.wait makes
 // the GEMV's stores visible.  One block per tile row; whole rows exit at once.
@@ -1483,11 +1794,11 @@ int device_sm_count(int device) {
 namespace {
 
 struct WsLayout {
-  uint64_t counters, partials, xfrag, total;
+  uint64_t counters, partials, xfrag, xtc, total;
 };
 
 // [error word][split-row counters: R uint32][split-row partials: G x 2 x batch x 128
-// FP32][prepared activations].  The error word and the counters must start at zero
+// FP32][prepared activations: mma fragments][prepared activations: tcgen05 B blocks].  The error word and the counters must start at zero
 // (hqb_workspace_init); the counters return to zero at the end of every launch.
 WsLayout ws_layout(uint32_t R, uint32_t C, uint32_t batch, uint32_t xl, int sms) {
   WsLayout L{};
@@ -1495,7 +1806,8 @@ WsLayout ws_layout(uint32_t R, uint32_t C, uint32_t batch, uint32_t xl, int sms)
   L.partials = L.counters + round_up(static_cast<uint64_t>(R) * 4, 256);
   const uint64_t gmax = static_cast<uint64_t>(sms) * kMaxCtasPerSm;
   L.xfrag = L.partials + round_up(gmax * 2 * batch * 128 * 4, 256);
-  L.total = L.xfrag + round_up(static_cast<uint64_t>(C) * xslot_bytes_for(batch, xl), 256);
+  L.xtc = L.xfrag + round_up(static_cast<uint64_t>(C) * xslot_bytes_for(batch, xl), 256);
+  L.total = L.xtc + round_up(static_cast<uint64_t>(C) * kTcColBytes, 256);
   return L;
 }
 
@@ -1602,6 +1914,29 @@ int ctas_per_sm(GemvKernel k, uint32_t smem, int device, uint32_t threads) {
   n = std::min<int>(n, kMaxCtasPerSm);
   if (used < 64) cache[used++] = Entry{k, smem, device, n};
   return n;
+}
+
+template <int D>
+cudaError_t launch_tc(const GemvParams& p, uint32_t grid, uint32_t smem, bool pdl, cudaStream_t st) {
+  static std::once_flag once;
+  static cudaError_t attr_status = cudaSuccess;
+  std::call_once(once, [] {
+    attr_status = cudaFuncSetAttribute(gemv_tc_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+  });
+  if (attr_status != cudaSuccess) return attr_status;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kTcThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  if (pdl) {
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+  }
+  return cudaLaunchKernelEx(&cfg, gemv_tc_kernel<D>, p);
 }
 
 cudaError_t launch_prep(const void* x, int x_dtype, uint64_t cols, uint32_t batch, void* xfrag, cudaStream_t st) {
@@ -1752,6 +2087,52 @@ HQB_API int hqb_gemv_ex(const hqb_plane_matrix* m, uint32_t prefix, const uint8_
     return cudaGetLastError();
   }
   uint8_t* ws = static_cast<uint8_t*>(workspace);
+  // tcgen05 comparison path (on request): uniform depth, raw FP16 activations, batch <= 8
+  if ((flags & HQB_FLAG_TCGEN05) && !mixed && !simt && !x_prepared && x_dtype == HQB_F16 && batch <= 8 &&
+      !(flags & HQB_FLAG_RING)) {
+    const uint32_t C = m->grid_cols;
+    prep_x_tc_kernel<<<dim3(C, 16), 128, 0, st>>>(static_cast<const __half*>(x), static_cast<uint32_t>(m->cols), batch,
+                                                  ws + L.xtc);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    GemvParams p{};
+    for (uint32_t s = 0; s < HQB_MAX_STAGES; ++s) p.planes[s] = static_cast<const uint8_t*>(m->planes[s]);
+    p.xfrag = ws + L.xtc;
+    p.bias = bias;
+    p.y = y;
+    p.error = reinterpret_cast<int*>(ws);
+    p.partials = reinterpret_cast<float*>(ws + L.partials);
+    p.counters = reinterpret_cast<uint32_t*>(ws + L.counters);
+    p.rows = static_cast<uint32_t>(m->rows);
+    p.R = m->grid_rows;
+    p.C = C;
+    p.prefix = prefix;
+    p.stage_count = m->stage_count;
+    p.batch = batch;
+    p.bias_dtype = bias_dtype;
+    p.y_dtype = y_dtype;
+    p.cols = static_cast<uint32_t>(m->cols);
+    p.shift_mul = 1u << 24;
+    p.total = static_cast<uint64_t>(m->grid_rows) * C * prefix;
+    const uint32_t sb = tc_slot_bytes(prefix);
+    const uint32_t slots = std::max<uint32_t>(3, std::min<uint32_t>(16, kTcRingBudget / sb));
+    p.ring_slots = slots;
+    p.slot_stride = sb;
+    const uint32_t smem = slots * sb + (2 * slots + 8) * 8 + 16 * 4;
+    const uint32_t grid = static_cast<uint32_t>(std::min<uint64_t>(static_cast<uint64_t>(sms), p.total));
+    const bool pdl = (flags & HQB_FLAG_PDL) != 0;
+    switch (prefix) {
+      case 1: e = launch_tc<1>(p, grid, smem, pdl, st); break;
+      case 2: e = launch_tc<2>(p, grid, smem, pdl, st); break;
+      case 3: e = launch_tc<3>(p, grid, smem, pdl, st); break;
+      default: e = launch_tc<4>(p, grid, smem, pdl, st); break;
+    }
+    if (e != cudaSuccess) {
+      cudaGetLastError();
+      return e;
+    }
+    return cudaGetLastError();
+  }
   const uint8_t* xfrag = static_cast<const uint8_t*>(x);
   // The uniform streaming kernel prepares raw activations itself when they fit beside
   // the fragments in shared memory (no separate preparation launch).

@@ -22,7 +22,7 @@ PKG = Path(__file__).resolve().parent
 LIB_PATH = PKG / "lib" / "libharpq_b200.so"
 
 F32, F16 = 0, 1
-FLAG_PDL, FLAG_SIMT, FLAG_RING = 1, 2, 4
+FLAG_PDL, FLAG_SIMT, FLAG_RING, FLAG_TCGEN05 = 1, 2, 4, 8
 TILE = 128
 RECORD_BYTES = 4352
 MAX_STAGES = 4
@@ -298,6 +298,9 @@ class PlaneMatrix:
         kernel runs (it reduces split tile rows itself), the split-row fix-up."""
         if not mixed and prefix == 0:
             return 1  # bias / zero fill only
+        if (flags & FLAG_TCGEN05) and not mixed and not x_prepared and x_dtype == F16 and batch <= 8 \
+                and not (flags & (FLAG_SIMT | FLAG_RING)):
+            return 2  # activation blocks, then the tcgen05 kernel
         xl = 2 if x_dtype == F32 else 1
         xslot = -(-(batch * (256 * xl + 8)) // 16) * 16
         streaming = not (flags & FLAG_SIMT) and self.grid_cols * xslot <= 64 * 1024 and not (flags & FLAG_RING)

@@ -45,6 +45,9 @@ extern "C" {
 #define HQB_FLAG_PDL 1u  /* launch with programmatic dependent launch (see hqb_gemv_ex) */
 #define HQB_FLAG_SIMT 2u /* CUDA-core decode+FFMA consumer instead of tensor-core mma */
 #define HQB_FLAG_RING 4u /* force the bulk-copy ring pipeline (comparison/diagnostics) */
+#define HQB_FLAG_TCGEN05 8u /* tcgen05 (UMMA, TMEM accumulators) kernel: FP16 x, batch <= 8,
+                                 uniform prefix; a comparison path, slower than the default
+                                 mma.sync kernels at these shapes */
 
 /* Fast-path tiling: 128x128 tiles, one scale group per tile row (group 128). */
 #define HQB_TILE 128

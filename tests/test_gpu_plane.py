@@ -227,9 +227,12 @@ def test_prepared_activations_shared_across_matrices():
         ya = pm.gemv(x, prefix=2, y_dtype=torch.float32, x_prepared=xf)
         yb = pm.gemv(x, prefix=2, y_dtype=torch.float32)
         assert torch.equal(ya, yb)
+        # the tcgen05 comparison kernel: equal within the FP32 contract (another summation order)
+        yc = pm.gemv(x, prefix=2, y_dtype=torch.float32, flags=hqb.FLAG_TCGEN05)
+        assert_close(yc.cpu().numpy(), yb.cpu().numpy(), 2e-4, 2e-4, "tcgen05 vs mma.sync kernel")
     # PDL launch flag gives the same result
     y1 = a.gemv(x, prefix=3, y_dtype=torch.float32, x_prepared=xf, flags=hqb.FLAG_PDL)
-    y2 = a.gemv(x, prefix=3, y_dtype=torch.float32)
+    y2 = a.gemv(x, prefix=3, y_dtype=torch.float32, x_prepared=xf)
     torch.cuda.synchronize()
     assert torch.equal(y1, y2)
 
@@ -315,3 +318,31 @@ def test_in_kernel_activation_prep_matches_prepared(cols, xdt, misalign):
             ya = pm.gemv(x, prefix=p, y_dtype=torch.float32, x_prepared=xf)
             yb = pm.gemv(x, prefix=p, y_dtype=torch.float32)
             assert torch.equal(ya, yb), (batch, p)
+
+
+@pytest.mark.parametrize("batch", [1, 3, 8])
+def test_tcgen05_kernel_ring_wrap_and_pdl(batch):
+    """The tcgen05 comparison kernel (HQB_FLAG_TCGEN05: raw FP16 activations, batch <= 8)
+    on a layer whose CTAs hold more tiles than the shared-memory ring has slots at
+    prefixes 2-4: against the FP64 materialize-then-matvec result, against the default
+    mma.sync kernel, and bit-identical between plain and programmatic-dependent launches."""
+    import harpq_b200 as hqb
+
+    rng = np.random.default_rng(4242 + batch)
+    m = random_matrix(rng, 4096, 8192)
+    pm = plane_matrix(m)
+    x = (rng.standard_normal((batch, m.cols)) * 2.0).astype(np.float16).astype(np.float32)
+    xt = torch.from_numpy(x).cuda().half()
+    ws = pm.workspace(batch)
+    for p in (1, 2, 4):
+        tc = hqb.FLAG_TCGEN05
+        y = pm.gemv(xt, prefix=p, y_dtype=torch.float32, workspace=ws, flags=tc).cpu().numpy()
+        e64 = _fp64_reference(m, x, p)
+        assert rel_l2(y, e64) <= 1e-3
+        assert_close(y, e64, 2e-4, 2e-4, f"tcgen05 p{p}")
+        y_mma = pm.gemv(xt, prefix=p, y_dtype=torch.float32, workspace=ws).cpu().numpy()
+        assert_close(y, y_mma, 2e-4, 2e-4, f"tcgen05 vs mma.sync p{p}")
+        y_pdl = pm.gemv(xt, prefix=p, y_dtype=torch.float32, workspace=ws, flags=tc | hqb.FLAG_PDL)
+        torch.cuda.synchronize()
+        assert np.array_equal(y_pdl.cpu().numpy(), y), f"PDL p{p}"
+    assert ws.error_flags() == 0
