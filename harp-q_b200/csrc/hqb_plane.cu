@@ -77,6 +77,12 @@ struct GemvParams {
   uint32_t x_resident;   // all activation fragments staged once per CTA (else one per slot)
   uint32_t slot_x_bytes; // activation bytes carried by each slot (0 when resident)
   uint32_t cols;         // original columns (raw activation rows)
+  // fused all-gather (g_world > 1): outputs go to every rank's gathered buffer
+  uint32_t g_world, g_rank;
+  uint64_t g_slot_rows;
+  void* g_peer_y[HQB_MAX_PEERS];
+  uint32_t* g_peer_flags[HQB_MAX_PEERS];
+  uint32_t* g_done;      // CTAs of this launch that finished (local, returns to zero)
   uint32_t x_vec;        // raw activation rows can be read as aligned 16-byte chunks
   uint32_t raw_offset;   // shared-memory offset of the raw activation staging area
   int bias_dtype;
@@ -367,6 +373,22 @@ __device__ void gemv_producer(const GemvParams& p, const Ring& ring, uint64_t u0
   }
 }
 
+// Output element (batch b, row): local y, or with the fused gather every rank's gathered
+// buffer [batch][world * slot_rows] at column rank * slot_rows + row (P2P stores).
+__device__ __forceinline__ void put_y(const GemvParams& p, uint32_t b, uint32_t row, float v) {
+  if (p.g_world > 1) {
+    const uint64_t o = static_cast<uint64_t>(b) * p.g_world * p.g_slot_rows + p.g_rank * p.g_slot_rows + row;
+    for (uint32_t r = 0; r < p.g_world; ++r) {
+      if (p.y_dtype == HQB_F16) static_cast<__half*>(p.g_peer_y[r])[o] = __float2half_rn(v);
+      else static_cast<float*>(p.g_peer_y[r])[o] = v;
+    }
+    return;
+  }
+  const uint64_t o = static_cast<uint64_t>(b) * p.rows + row;
+  if (p.y_dtype == HQB_F16) static_cast<__half*>(p.y)[o] = __float2half_rn(v);
+  else static_cast<float*>(p.y)[o] = v;
+}
+
 template <int NB>
 __device__ __forceinline__ void store_out(const GemvParams& p, const float (&v)[NB][4], uint32_t row0,
                                           uint32_t q) {
@@ -386,9 +408,7 @@ __device__ __forceinline__ void store_out(const GemvParams& p, const float (&v)[
           out += p.bias_dtype == HQB_F16 ? __half2float(static_cast<const __half*>(p.bias)[row])
                                          : static_cast<const float*>(p.bias)[row];
         }
-        const uint64_t o = static_cast<uint64_t>(b) * p.rows + row;
-        if (p.y_dtype == HQB_F16) static_cast<__half*>(p.y)[o] = __float2half_rn(out);
-        else static_cast<float*>(p.y)[o] = out;
+        put_y(p, b, row, out);
       }
     }
   }
@@ -1005,9 +1025,21 @@ __device__ __forceinline__ void finish_split_rows(const GemvParams& p, const Spl
     if (p.bias != nullptr)
       sum += p.bias_dtype == HQB_F16 ? __half2float(static_cast<const __half*>(p.bias)[row])
                                      : static_cast<const float*>(p.bias)[row];
-    const uint64_t o = static_cast<uint64_t>(b) * p.rows + row;
-    if (p.y_dtype == HQB_F16) static_cast<__half*>(p.y)[o] = __float2half_rn(sum);
-    else static_cast<float*>(p.y)[o] = sum;
+    put_y(p, b, row, sum);
+  }
+}
+
+// Fused all-gather completion: after every CTA of the launch has stored its outputs (a
+// system-scope fence orders the CTA's peer stores first), the last CTA adds 1 to this
+// rank's counter in every rank's flag array with a system-scope release.
+__device__ __forceinline__ void gather_signal(const GemvParams& p, uint32_t ctas) {
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    if (atom_add_acq_rel_gpu(p.g_done, 1u) == ctas - 1) {
+      *p.g_done = 0u;  // ready for the next launch
+      for (uint32_t r = 0; r < p.g_world; ++r) red_add_release_sys(p.g_peer_flags[r] + p.g_rank, 1u);
+    }
   }
 }
 
@@ -1322,6 +1354,7 @@ __global__ void __launch_bounds__(kStreamThreads, (NB == 1 && XL == 1) ? 2 : 1)
     advance(k);
   }
   if (split.count != 0) finish_split_rows<NB>(p, split, units_per_row, total, ctas, s_info);
+  if (p.g_world > 1) gather_signal(p, ctas);
 }
 
 // --------------------------------------------------------------------------------------
@@ -1635,6 +1668,24 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemv_tc_kernel(const __grid_con
   if (warp == 9) tmem_dealloc(tmem, kTcTmemCols);
 }
 
+// Waits (one thread, bounded) until every rank's counter in `flags` reached *epoch + 1,
+// then advances the epoch.
+__global__ void gather_wait_kernel(const uint32_t* flags, uint32_t world, uint32_t* epoch, int* device_flags) {
+  if (threadIdx.x != 0) return;
+  const uint32_t target = *epoch + 1u;
+  const unsigned long long start = global_timer_ns();
+  for (uint32_t r = 0; r < world; ++r) {
+    while (static_cast<int32_t>(ld_acquire_sys(flags + r) - target) < 0) {
+      if (global_timer_ns() - start > kWaitLimitNs) {
+        if (device_flags != nullptr) atomicOr(device_flags, HQB_DEVERR_TIMEOUT);
+        *epoch = target;
+        return;
+      }
+    }
+  }
+  *epoch = target;
+}
+
 // Split tile rows: the parts of the contributing CTAs, summed in CTA order, plus
 // bias.  Launched as a programmatic dependent of the GEMV; griddepcontrol.wait makes
 // the GEMV's stores visible.  One block per tile row; whole rows exit at once.
@@ -1803,7 +1854,7 @@ struct WsLayout {
 WsLayout ws_layout(uint32_t R, uint32_t C, uint32_t batch, uint32_t xl, int sms) {
   WsLayout L{};
   L.counters = 256;
-  L.partials = L.counters + round_up(static_cast<uint64_t>(R) * 4, 256);
+  L.partials = L.counters + round_up((static_cast<uint64_t>(R) + 1) * 4, 256);  // + launch-done counter
   const uint64_t gmax = static_cast<uint64_t>(sms) * kMaxCtasPerSm;
   L.xfrag = L.partials + round_up(gmax * 2 * batch * 128 * 4, 256);
   L.xtc = L.xfrag + round_up(static_cast<uint64_t>(C) * xslot_bytes_for(batch, xl), 256);
@@ -2053,11 +2104,25 @@ HQB_API int hqb_depth_plan(const uint8_t* depth, uint32_t grid_rows, uint32_t gr
   return cudaGetLastError();
 }
 
-HQB_API int hqb_gemv_ex(const hqb_plane_matrix* m, uint32_t prefix, const uint8_t* depth, const uint32_t* depth_plan,
-                        const void* x, int x_dtype, uint32_t batch, int x_prepared, const void* bias, int bias_dtype,
-                        void* y, int y_dtype, void* workspace, uint64_t workspace_bytes, uint32_t flags,
-                        void* stream) {
-  if (!plane_matrix_ok(m) || x == nullptr || y == nullptr || workspace == nullptr) return HQB_ERR_INVALID;
+}  // extern "C"
+
+namespace {
+
+// hqb_gemv_ex, optionally with the fused all-gather of the outputs (gather != nullptr).
+int gemv_impl(const hqb_plane_matrix* m, uint32_t prefix, const uint8_t* depth, const uint32_t* depth_plan,
+              const void* x, int x_dtype, uint32_t batch, int x_prepared, const void* bias, int bias_dtype, void* y,
+              int y_dtype, void* workspace, uint64_t workspace_bytes, uint32_t flags, void* stream,
+              const hqb_gather* gather) {
+  if (!plane_matrix_ok(m) || x == nullptr || (y == nullptr && gather == nullptr) || workspace == nullptr)
+    return HQB_ERR_INVALID;
+  if (gather != nullptr) {
+    if (gather->world < 2 || gather->world > HQB_MAX_PEERS || gather->rank >= gather->world ||
+        gather->slot_rows < m->rows || depth != nullptr || prefix == 0)
+      return HQB_ERR_INVALID;
+    for (uint32_t r = 0; r < gather->world; ++r)
+      if (gather->peer_y[r] == nullptr || gather->peer_flags[r] == nullptr) return HQB_ERR_INVALID;
+    if (flags & (HQB_FLAG_SIMT | HQB_FLAG_RING | HQB_FLAG_TCGEN05)) return HQB_ERR_UNSUPPORTED;
+  }
   if (batch == 0 || batch > HQB_MAX_BATCH) return HQB_ERR_INVALID;
   if ((x_dtype != HQB_F16 && x_dtype != HQB_F32) || (y_dtype != HQB_F16 && y_dtype != HQB_F32)) return HQB_ERR_INVALID;
   if (bias != nullptr && bias_dtype != HQB_F16 && bias_dtype != HQB_F32) return HQB_ERR_INVALID;
@@ -2088,8 +2153,8 @@ HQB_API int hqb_gemv_ex(const hqb_plane_matrix* m, uint32_t prefix, const uint8_
   }
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   // tcgen05 comparison path (on request): uniform depth, raw FP16 activations, batch <= 8
-  if ((flags & HQB_FLAG_TCGEN05) && !mixed && !simt && !x_prepared && x_dtype == HQB_F16 && batch <= 8 &&
-      !(flags & HQB_FLAG_RING)) {
+  if ((flags & HQB_FLAG_TCGEN05) && gather == nullptr && !mixed && !simt && !x_prepared && x_dtype == HQB_F16 &&
+      batch <= 8 && !(flags & HQB_FLAG_RING)) {
     const uint32_t C = m->grid_cols;
     prep_x_tc_kernel<<<dim3(C, 16), 128, 0, st>>>(static_cast<const __half*>(x), static_cast<uint32_t>(m->cols), batch,
                                                   ws + L.xtc);
@@ -2174,6 +2239,17 @@ HQB_API int hqb_gemv_ex(const hqb_plane_matrix* m, uint32_t prefix, const uint8_
   p.bias_dtype = bias_dtype;
   p.y_dtype = y_dtype;
   p.cols = static_cast<uint32_t>(m->cols);
+  if (gather != nullptr) {
+    if (!streaming_path) return HQB_ERR_UNSUPPORTED;  // only the uniform streaming kernel gathers
+    p.g_world = gather->world;
+    p.g_rank = gather->rank;
+    p.g_slot_rows = gather->slot_rows;
+    for (uint32_t r = 0; r < gather->world; ++r) {
+      p.g_peer_y[r] = gather->peer_y[r];
+      p.g_peer_flags[r] = gather->peer_flags[r];
+    }
+    p.g_done = reinterpret_cast<uint32_t*>(ws + L.counters) + m->grid_rows;
+  }
   if (fuse_prep) {
     p.x_raw = x;
     p.raw_offset = static_cast<uint32_t>(raw_offset);
@@ -2237,6 +2313,68 @@ HQB_API int hqb_gemv_ex(const hqb_plane_matrix* m, uint32_t prefix, const uint8_
     }
   }
   return cudaGetLastError();
+}
+
+}  // namespace
+
+extern "C" {
+
+HQB_API int hqb_gemv_ex(const hqb_plane_matrix* m, uint32_t prefix, const uint8_t* depth, const uint32_t* depth_plan,
+                        const void* x, int x_dtype, uint32_t batch, int x_prepared, const void* bias, int bias_dtype,
+                        void* y, int y_dtype, void* workspace, uint64_t workspace_bytes, uint32_t flags,
+                        void* stream) {
+  return gemv_impl(m, prefix, depth, depth_plan, x, x_dtype, batch, x_prepared, bias, bias_dtype, y, y_dtype,
+                   workspace, workspace_bytes, flags, stream, nullptr);
+}
+
+HQB_API int hqb_gemv_gather(const hqb_plane_matrix* m, uint32_t prefix, const void* x, int x_dtype, uint32_t batch,
+                            const void* bias, int bias_dtype, int y_dtype, const hqb_gather* gather,
+                            void* workspace, uint64_t workspace_bytes, uint32_t flags, void* stream) {
+  if (gather == nullptr) return HQB_ERR_INVALID;
+  return gemv_impl(m, prefix, nullptr, nullptr, x, x_dtype, batch, 0, bias, bias_dtype, nullptr, y_dtype, workspace,
+                   workspace_bytes, flags, stream, gather);
+}
+
+HQB_API int hqb_gather_wait(const uint32_t* flags, uint32_t world, uint32_t* epoch, int* device_flags,
+                            void* stream) {
+  if (flags == nullptr || epoch == nullptr || world == 0 || world > HQB_MAX_PEERS) return HQB_ERR_INVALID;
+  const cudaError_t prior = take_prior_error();
+  if (prior != cudaSuccess) return prior;
+  gather_wait_kernel<<<1, 32, 0, as_stream(stream)>>>(flags, world, epoch, device_flags);
+  return cudaGetLastError();
+}
+
+HQB_API int hqb_peer_alloc(uint64_t bytes, void** ptr, void* ipc_handle) {
+  if (bytes == 0 || ptr == nullptr || ipc_handle == nullptr) return HQB_ERR_INVALID;
+  static_assert(sizeof(cudaIpcMemHandle_t) == HQB_IPC_HANDLE_BYTES, "IPC handle size");
+  void* p = nullptr;
+  cudaError_t e = cudaMalloc(&p, bytes);
+  if (e != cudaSuccess) return e;
+  e = cudaMemset(p, 0, bytes);
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(static_cast<cudaIpcMemHandle_t*>(ipc_handle), p);
+  if (e != cudaSuccess) {
+    cudaFree(p);
+    return e;
+  }
+  *ptr = p;
+  return cudaSuccess;
+}
+
+HQB_API int hqb_peer_open(const void* ipc_handle, void** ptr) {
+  if (ipc_handle == nullptr || ptr == nullptr) return HQB_ERR_INVALID;
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, ipc_handle, sizeof(h));
+  return cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess);
+}
+
+HQB_API int hqb_peer_close(void* ptr) {
+  if (ptr == nullptr) return HQB_ERR_INVALID;
+  return cudaIpcCloseMemHandle(ptr);
+}
+
+HQB_API int hqb_peer_free(void* ptr) {
+  if (ptr == nullptr) return HQB_ERR_INVALID;
+  return cudaFree(ptr);
 }
 
 HQB_API int hqb_gemv(const hqb_plane_matrix* m, uint32_t prefix, const void* x, int x_dtype, uint32_t batch,

@@ -52,6 +52,14 @@ class PlaneMatrixC(ctypes.Structure):
                 ("reserved", u32), ("planes", vp * MAX_STAGES)]
 
 
+MAX_PEERS = 8
+
+
+class GatherC(ctypes.Structure):
+    _fields_ = [("world", u32), ("rank", u32), ("slot_rows", u64), ("peer_y", vp * MAX_PEERS),
+                ("peer_flags", vp * MAX_PEERS)]
+
+
 EXPORTS = {
     "hqb_version": (i32, []),
     "hqb_status_string": (ctypes.c_char_p, [i32]),
@@ -69,6 +77,13 @@ EXPORTS = {
     "hqb_gemv_ex": (i32, [ctypes.POINTER(PlaneMatrixC), u32, vp, vp, vp, i32, u32, i32, vp, i32, vp, i32, vp, u64,
                           u32, vp]),
     "hqb_gemv_noalloc": (i32, [ctypes.POINTER(PlaneMatrixC), u32, vp, i32, u32, vp, i32, vp, i32, vp]),
+    "hqb_peer_alloc": (i32, [u64, ctypes.POINTER(vp), vp]),
+    "hqb_peer_open": (i32, [vp, ctypes.POINTER(vp)]),
+    "hqb_peer_close": (i32, [vp]),
+    "hqb_peer_free": (i32, [vp]),
+    "hqb_gemv_gather": (i32, [ctypes.POINTER(PlaneMatrixC), u32, vp, i32, u32, vp, i32, i32, ctypes.POINTER(GatherC),
+                              vp, u64, u32, vp]),
+    "hqb_gather_wait": (i32, [vp, u32, vp, vp, vp]),
     "hqb_decode_planes": (i32, [ctypes.POINTER(PlaneMatrixC), u32, vp, vp, u64, vp]),
     "hqb_raw_gemv": (i32, [ctypes.POINTER(Geometry), ctypes.POINTER(RawStage), u32, u32, vp, u64, vp, u64, vp, u64,
                            vp]),
@@ -317,6 +332,23 @@ class PlaneMatrix:
             n += 1
         return n
 
+    def gemv_gather(self, x: torch.Tensor, gather: "Gather", prefix: int | None = None,
+                    bias: torch.Tensor | None = None, workspace: Workspace | None = None, flags: int = 0,
+                    stream=None) -> None:
+        """This rank's row shard of the layer, its outputs written into every rank's
+        gathered buffer (gather.out after gather.wait())."""
+        if x.dim() == 1:
+            x = x.unsqueeze(0)
+        x = x.contiguous()
+        batch = x.shape[0]
+        xd = _dtype_code(x)
+        ws = workspace or self.workspace(batch, xd)
+        prefix = self.stage_count if prefix is None else prefix
+        check(lib().hqb_gemv_gather(ctypes.byref(self.c_struct()), prefix, _ptr(x), xd, batch, _ptr(bias),
+                                    F32 if bias is None else _dtype_code(bias),
+                                    F16 if gather.y_dtype == torch.float16 else F32, ctypes.byref(gather.c),
+                                    ws.ptr(), ws.nbytes, flags, _stream(stream)), "hqb_gemv_gather")
+
     def decode(self, prefix: int | None = None, depth: torch.Tensor | None = None, stream=None) -> torch.Tensor:
         out = torch.empty(self.rows, self.cols, dtype=torch.float32, device=self.device)
         prefix = self.stage_count if prefix is None else prefix
@@ -408,3 +440,89 @@ def slice_stage_rows(codes, bits, cols: int, r0: int, nrows: int):
     t0 = r0 // TILE
     b = [x[t0 * per_tile_row:(t0 + nt) * per_tile_row] for x in bits]
     return c, b
+
+
+# ---------------------------------------------------------------------------------------
+# output-row shards across the GPUs of one node: fused all-gather over peer memory
+
+class _DeviceView:
+    """Raw device memory seen as a torch tensor (CUDA array interface, no copy)."""
+
+    def __init__(self, ptr: int, shape, typestr: str):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr, "data": (ptr, False),
+                                         "version": 3, "strides": None}
+
+
+class PeerBuffer:
+    """A device buffer of `nbytes` (zero-initialised) that every rank of a torch.distributed
+    group maps: rank r's copy is peers[r] (peers[rank] is the local one).  Collective:
+    every rank constructs it in the same order."""
+
+    def __init__(self, nbytes: int, group=None):
+        import torch.distributed as dist
+
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        local = vp()
+        handle = ctypes.create_string_buffer(64)
+        check(lib().hqb_peer_alloc(nbytes, ctypes.byref(local), handle), "hqb_peer_alloc")
+        handles = [None] * self.world
+        dist.all_gather_object(handles, bytes(handle.raw), group=group)
+        self.local = local.value
+        self.peers = []
+        self._opened = []
+        for r, h in enumerate(handles):
+            if r == self.rank:
+                self.peers.append(self.local)
+                continue
+            ptr = vp()
+            check(lib().hqb_peer_open(ctypes.create_string_buffer(h, 64), ctypes.byref(ptr)), "hqb_peer_open")
+            self.peers.append(ptr.value)
+            self._opened.append(ptr.value)
+        self.nbytes = nbytes
+
+    def close(self):
+        for ptr in self._opened:
+            lib().hqb_peer_close(ptr)
+        self._opened = []
+        if self.local:
+            lib().hqb_peer_free(self.local)
+            self.local = None
+
+
+class Gather:
+    """Gathered output of a row-sharded layer: [batch][world * slot_rows] of y_dtype on every
+    rank, filled by PlaneMatrix.gemv_gather on all ranks; wait() orders later work in the
+    stream after every rank's slice has arrived."""
+
+    def __init__(self, slot_rows: int, batch: int = 1, y_dtype=torch.float16, group=None):
+        self.slot_rows, self.batch = slot_rows, batch
+        self.y_dtype = y_dtype
+        esize = 2 if y_dtype == torch.float16 else 4
+        self.ybuf = PeerBuffer(batch * slot_rows * _world(group) * esize, group)
+        self.flags = PeerBuffer(4 * MAX_PEERS, group)
+        self.epoch = torch.zeros(1, dtype=torch.int32, device="cuda")
+        self.device_flags = torch.zeros(1, dtype=torch.int32, device="cuda")
+        self.world, self.rank = self.ybuf.world, self.ybuf.rank
+        c = GatherC()
+        c.world, c.rank, c.slot_rows = self.world, self.rank, slot_rows
+        for r in range(self.world):
+            c.peer_y[r] = self.ybuf.peers[r]
+            c.peer_flags[r] = self.flags.peers[r]
+        self.c = c
+        self.out = torch.as_tensor(_DeviceView(self.ybuf.local, (batch, self.world * slot_rows),
+                                               "<f2" if esize == 2 else "<f4"), device="cuda")
+
+    def wait(self, stream=None):
+        check(lib().hqb_gather_wait(self.flags.local, self.world, _ptr(self.epoch), _ptr(self.device_flags),
+                                    _stream(stream)), "hqb_gather_wait")
+
+    def close(self):
+        self.ybuf.close()
+        self.flags.close()
+
+
+def _world(group=None) -> int:
+    import torch.distributed as dist
+
+    return dist.get_world_size(group)

@@ -225,6 +225,52 @@ HQB_API int hqb_gemv_noalloc(const hqb_plane_matrix* m, uint32_t prefix, const v
                              int x_dtype, uint32_t batch, const void* bias, int bias_dtype,
                              void* y, int y_dtype, void* stream);
 
+/* ---- output-row shards across GPUs: fused all-gather over peer memory --------------- */
+
+#define HQB_MAX_PEERS 8
+#define HQB_IPC_HANDLE_BYTES 64
+
+/* Device buffer that peers of this node can map (cudaMalloc + IPC handle).  The handle
+ * (HQB_IPC_HANDLE_BYTES) goes to the peers by any host channel. */
+HQB_API int hqb_peer_alloc(uint64_t bytes, void** ptr, void* ipc_handle);
+/* Maps a peer's buffer from its handle (P2P over NVLink) / unmaps it. */
+HQB_API int hqb_peer_open(const void* ipc_handle, void** ptr);
+HQB_API int hqb_peer_close(void* ptr);
+HQB_API int hqb_peer_free(void* ptr);
+
+/* One rank's view of a gathered output.  Every rank owns a row shard of the layer; its
+ * GEMV writes its outputs straight into every rank's gathered buffer (its own included)
+ * at columns [rank * slot_rows, rank * slot_rows + rows) of each batch row, so the
+ * gathered buffer is [batch][world * slot_rows] of y_dtype on every rank.  After the
+ * last CTA's stores, the kernel adds 1 to counter `rank` of every rank's flag array
+ * (world uint32, zero-initialised, peer-mapped).  peer_y[r] / peer_flags[r] are rank r's
+ * buffers as mapped here (r == rank: the local ones).  No reference counterpart: the
+ * reference GEMV runs on one device (native/src/progressive_gemv.cu:420-439). */
+typedef struct hqb_gather {
+  uint32_t world;
+  uint32_t rank;
+  uint64_t slot_rows;
+  void* peer_y[HQB_MAX_PEERS];
+  uint32_t* peer_flags[HQB_MAX_PEERS];
+} hqb_gather;
+
+/* hqb_gemv whose outputs go to every rank's gathered buffer (uniform prefix; the plane
+ * matrix is this rank's row shard, rows <= slot_rows).  HQB_ERR_UNSUPPORTED when the
+ * shape or batch needs a kernel without the fused gather (activations wider than the
+ * resident limit, HQB_FLAG_SIMT/RING/TCGEN05). */
+HQB_API int hqb_gemv_gather(const hqb_plane_matrix* m, uint32_t prefix, const void* x, int x_dtype,
+                            uint32_t batch, const void* bias, int bias_dtype, int y_dtype,
+                            const hqb_gather* gather, void* workspace, uint64_t workspace_bytes,
+                            uint32_t flags, void* stream);
+
+/* Waits on the device until every rank has signalled the gathered buffer whose local flag
+ * array is `flags` once more than the previous wait: one thread spins (bounded, 2 s) on
+ * flags[0..world) >= *epoch + 1, then stores the new epoch.  A timeout sets
+ * HQB_DEVERR_TIMEOUT in *device_flags.  Launch it before anything reads the gathered
+ * buffer. */
+HQB_API int hqb_gather_wait(const uint32_t* flags, uint32_t world, uint32_t* epoch, int* device_flags,
+                            void* stream);
+
 /* Dense FP32 weights [rows][cols] decoded from planes, Σ_{s<d} code·scale summed in
  * stage order from 0.0f — bit-identical to DequantizePrefix
  * (native/src/stage_codec.cpp:254-272).  depth NULL: uniform prefix. */
