@@ -253,6 +253,7 @@ def build_workload(name, rank, world, device, rotation_target):
     step_bytes = sum(g["bytes"] for g in built)
     plane_bytes_step = sum(sum(p.numel() for p in g["copies"][0].planes[:prefix]) for g in built)
     ncopies = max(2, -(-rotation_target // max(1, plane_bytes_step)))
+    ncopies += ncopies % 2  # consecutive steps alternate the two gathered-output buffers
     for g in built:
         base = g["copies"][0]
         for _ in range(ncopies - 1):
@@ -275,11 +276,17 @@ def run_ours(args, rank, world, device):
     x_dev = {s: torch.randn(1, k, generator=gen, device=device).half() for s, k in srcs.items()}
     y_loc = {g["name"]: torch.empty(1, g["nrows"], dtype=torch.float16, device=device) for g in groups}
     y_full = {g["name"]: torch.empty(world, g["slot_rows"], dtype=torch.float16, device=device) for g in groups}
+    # N > 1: NCCL all_gather_into_tensor of each group's output slices; --fused-gather uses
+    # the fused all-gather instead (outputs stored into every rank's buffer over NVLink by
+    # the GEMV itself, then a bounded flag wait), two buffers per group alternating by step
+    fused = world > 1 and args.fused_gather
+    gathers = {g["name"]: [hqb.Gather(g["slot_rows"], 1, torch.float16) for _ in range(2)] for g in groups} \
+        if fused else {}
     ws_bytes = max(g["copies"][0].workspace_bytes(1, hqb.F16) for g in groups)
     ws = hqb.Workspace(ws_bytes, device)
     # per step: the launches of each group's GEMV by the library's own dispatch rule (the
     # uniform kernel prepares its raw activations itself where they fit)
-    launches_per_step = sum(g["copies"][0].gemv_launches(1, hqb.F16, prefix) for g in groups)
+    launches_per_step = sum(g["copies"][0].gemv_launches(1, hqb.F16, prefix) + (1 if fused else 0) for g in groups)
 
     def gather(g):
         if world == 1:
@@ -293,8 +300,17 @@ def run_ours(args, rank, world, device):
         xs = x_dev if x_src is None else x_src
         for g in groups:
             pm = g["copies"][copy]
-            pm.gemv(xs[g["src"]], prefix=prefix, out=y_loc[g["name"]], workspace=ws, flags=hqb.FLAG_PDL)
-            gather(g)
+            if fused:
+                G = gathers[g["name"]][copy % 2]
+                pm.gemv_gather(xs[g["src"]], G, prefix=prefix, workspace=ws, flags=hqb.FLAG_PDL)
+            else:
+                pm.gemv(xs[g["src"]], prefix=prefix, out=y_loc[g["name"]], workspace=ws, flags=hqb.FLAG_PDL)
+                gather(g)
+        # the workload's layers take given inputs, so each gathered output is waited for
+        # once per step, before anything reads it (here: the end of the step)
+        for g in groups:
+            if fused:
+                gathers[g["name"]][copy % 2].wait()
 
     # clocks are sampled from warm-up to the end of the e2e leg; the summary keeps the
     # samples that fall inside the timed region
@@ -386,8 +402,12 @@ def run_ours(args, rank, world, device):
 
     # ---- e2e through the public API: pinned host x -> device, GEMVs, device -> host y
     host_x = {s: x_dev[s].cpu().pin_memory() for s in srcs}
-    host_y = {g["name"]: torch.empty_like(y_full[g["name"]] if world > 1 else y_loc[g["name"]], device="cpu").pin_memory()
-              for g in groups}
+    def gathered(g, copy):
+        if fused:
+            return gathers[g["name"]][copy % 2].out
+        return y_full[g["name"]] if world > 1 else y_loc[g["name"]]
+
+    host_y = {g["name"]: torch.empty_like(gathered(g, 0), device="cpu").pin_memory() for g in groups}
     x_stage = {s: torch.empty_like(x_dev[s]) for s in srcs}
 
     def e2e_step(copy):
@@ -395,7 +415,7 @@ def run_ours(args, rank, world, device):
             x_stage[s].copy_(host_x[s], non_blocking=True)
         step(copy, x_src=x_stage)
         for g in groups:
-            host_y[g["name"]].copy_(y_full[g["name"]] if world > 1 else y_loc[g["name"]], non_blocking=True)
+            host_y[g["name"]].copy_(gathered(g, copy), non_blocking=True)
 
     for i in range(3):
         e2e_step(i % ncopies)
@@ -418,6 +438,15 @@ def run_ours(args, rank, world, device):
     clk.__exit__(None, None, None)
     del graphs  # graphs holding NCCL work are released before the process group is destroyed
     torch.cuda.synchronize()
+    gather_flags = 0
+    for pair in gathers.values():
+        for G in pair:
+            gather_flags |= int(G.device_flags.item())
+    if world > 1:
+        torch.distributed.barrier()  # every rank is done with the peers' buffers
+    for pair in gathers.values():
+        for G in pair:
+            G.close()
     flags = ws.error_flags()
     result = {
         "metric": METRIC,
@@ -438,7 +467,8 @@ def run_ours(args, rank, world, device):
                    "layers": [[m["name"], m["rows"], g["cols"]] for g in groups for m in g["members"]],
                    "launches": [[g["name"], g["nrows"], g["cols"]] for g in groups],
                    "grouping": "layers sharing an input run as one row-stacked launch",
-                   "parallelism": f"row-shard{world}+allgather" if world > 1 else "single",
+                   "parallelism": (f"row-shard{world}+" + ("fused-p2p-allgather" if fused else "nccl-allgather"))
+                                  if world > 1 else "single",
                    "l2": f"{ncopies} rotating weight copies, {ncopies * step_bytes / 2**20:.0f} MiB > 3x L2",
                    "graph": use_graph},
         "roofline": None,
@@ -447,7 +477,7 @@ def run_ours(args, rank, world, device):
                 "us_per_step": round(e2e_ms * 1e3, 2), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
         "gpu_launches": launches_per_step * args.steps,
         "clocks": clk.summary(t_timed0, t_timed1),
-        "device_error_flags": flags,
+        "device_error_flags": flags | gather_flags,
     }
     peaks = {}
     try:
@@ -656,6 +686,8 @@ def main(argv=None) -> int:
     ap.add_argument("--no-graph", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extras", action="store_true", help="skip the supplementary single-GPU measurements")
+    ap.add_argument("--fused-gather", action="store_true",
+                    help="N > 1: gather outputs with the fused P2P gather instead of NCCL all_gather_into_tensor")
     args = ap.parse_args(argv)
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
