@@ -1167,7 +1167,7 @@ __device__ __forceinline__ void build_xfrag_tiles(const GemvParams& p, uint8_t* 
   }
 }
 
-template <int NB, int XL, int D>
+template <int NB, int XL, int D, bool B1 = false>
 __global__ void __launch_bounds__(kStreamThreads, (NB == 1 && XL == 1) ? 2 : 1)
     gemv_uniform_kernel(const __grid_constant__ GemvParams p) {
   constexpr int R = TilesAhead<D>::value;
@@ -1262,7 +1262,7 @@ __global__ void __launch_bounds__(kStreamThreads, (NB == 1 && XL == 1) ? 2 : 1)
 
   // Tensor-core part of one tile from ring slot j: D independent MMA chains (two for
   // D == 1); the first MMA of each chain starts from zero.
-  constexpr int CH = D == 1 ? 2 : D;
+  constexpr int CH = D == 1 ? 2 : D;  // depth 1 alternates two chains
   auto mma_tile = [&](int j, const XFrag<NB, XL>& xf, float (&acc)[CH][NB][4]) {
     uint32_t hi[D][4];
 #pragma unroll
@@ -1291,12 +1291,18 @@ __global__ void __launch_bounds__(kStreamThreads, (NB == 1 && XL == 1) ? 2 : 1)
     }
   };
   // Scale epilogue of one tile into y.
+  // With B1 (batch 1) only accumulator column 0 is ever stored: the others are skipped.
   auto epi_tile = [&](int j, const XFrag<NB, XL>& xf, float (&acc)[CH][NB][4]) {
     if (D == 1) {
 #pragma unroll
-      for (int nb = 0; nb < NB; ++nb)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) acc[0][nb][e] += acc[CH - 1][nb][e];
+      for (int nb = 0; nb < NB; ++nb) {
+        acc[0][nb][0] += acc[CH - 1][nb][0];
+        acc[0][nb][2] += acc[CH - 1][nb][2];
+        if (!B1) {
+          acc[0][nb][1] += acc[CH - 1][nb][1];
+          acc[0][nb][3] += acc[CH - 1][nb][3];
+        }
+      }
     }
 #pragma unroll
     for (int s = 0; s < D; ++s) {
@@ -1305,9 +1311,11 @@ __global__ void __launch_bounds__(kStreamThreads, (NB == 1 && XL == 1) ? 2 : 1)
 #pragma unroll
       for (int nb = 0; nb < NB; ++nb) {
         y[nb][0] = fmaf(s_lo, fmaf(acc[s][nb][0], xf.f[nb][0], -xf.gsum[nb][0]), y[nb][0]);
-        y[nb][1] = fmaf(s_lo, fmaf(acc[s][nb][1], xf.f[nb][1], -xf.gsum[nb][1]), y[nb][1]);
         y[nb][2] = fmaf(s_hi, fmaf(acc[s][nb][2], xf.f[nb][0], -xf.gsum[nb][0]), y[nb][2]);
-        y[nb][3] = fmaf(s_hi, fmaf(acc[s][nb][3], xf.f[nb][1], -xf.gsum[nb][1]), y[nb][3]);
+        if (!B1) {
+          y[nb][1] = fmaf(s_lo, fmaf(acc[s][nb][1], xf.f[nb][1], -xf.gsum[nb][1]), y[nb][1]);
+          y[nb][3] = fmaf(s_hi, fmaf(acc[s][nb][3], xf.f[nb][1], -xf.gsum[nb][1]), y[nb][3]);
+        }
       }
     }
   };
@@ -1879,17 +1887,18 @@ bool stage_planes_ok(const hqb_plane_matrix* m, uint32_t needed) {
 
 using GemvKernel = void (*)(GemvParams);
 
-template <int NB, int XL>
+template <int NB, int XL, bool B1 = false>
 GemvKernel pick_uniform_depth(uint32_t d) {
   switch (d) {
-    case 1: return gemv_uniform_kernel<NB, XL, 1>;
-    case 2: return gemv_uniform_kernel<NB, XL, 2>;
-    case 3: return gemv_uniform_kernel<NB, XL, 3>;
-    default: return gemv_uniform_kernel<NB, XL, 4>;
+    case 1: return gemv_uniform_kernel<NB, XL, 1, B1>;
+    case 2: return gemv_uniform_kernel<NB, XL, 2, B1>;
+    case 3: return gemv_uniform_kernel<NB, XL, 3, B1>;
+    default: return gemv_uniform_kernel<NB, XL, 4, B1>;
   }
 }
 
-GemvKernel pick_uniform_kernel(uint32_t nb, uint32_t xl, uint32_t d) {
+GemvKernel pick_uniform_kernel(uint32_t nb, uint32_t xl, uint32_t d, uint32_t batch) {
+  if (nb == 1 && xl == 1 && batch == 1) return pick_uniform_depth<1, 1, true>(d);
   if (nb == 1) return xl == 1 ? pick_uniform_depth<1, 1>(d) : pick_uniform_depth<1, 2>(d);
   return xl == 1 ? pick_uniform_depth<2, 1>(d) : pick_uniform_depth<2, 2>(d);
 }
@@ -2261,7 +2270,7 @@ int gemv_impl(const hqb_plane_matrix* m, uint32_t prefix, const uint8_t* depth, 
                          !(flags & HQB_FLAG_RING);
   const GemvKernel k = !streaming ? pick_kernel(batch > 8 ? 2 : 1, xl, simt)
                        : mixed    ? pick_stream_kernel(batch > 8 ? 2 : 1, xl)
-                                  : pick_uniform_kernel(batch > 8 ? 2 : 1, xl, prefix);
+                                  : pick_uniform_kernel(batch > 8 ? 2 : 1, xl, prefix, batch);
   const uint64_t x_all = static_cast<uint64_t>(m->grid_cols) * p.xslot_bytes;
   p.x_resident = x_all <= kXResidentMax ? 1u : 0u;
   p.slot_x_bytes = p.x_resident ? 0u : p.xslot_bytes;
