@@ -84,7 +84,7 @@ struct GemvParams {
   uint32_t* g_peer_flags[HQB_MAX_PEERS];
   uint32_t* g_done;      // CTAs of this launch that finished (local, returns to zero)
   uint32_t x_vec;        // raw activation rows can be read as aligned 16-byte chunks
-  uint32_t raw_offset;   // shared-memory offset of the raw activation staging area
+  uint32_t xw_bytes;     // row-block kernel: fragment bytes of each warp's shared-memory area
   int bias_dtype;
   int y_dtype;
 };
@@ -142,50 +142,118 @@ __global__ void __launch_bounds__(256) repack_kernel(const uint8_t* __restrict__
 // --------------------------------------------------------------------------------------
 // activation preparation
 
+// 2^k as a float for -126 <= k <= 127 (normal range), from the IEEE-754 bit layout.
+__device__ __forceinline__ float exp2_int(int k) { return __int_as_float((k + 127) << 23); }
+
+// Four consecutive activations [col0, col0 + 4) of one row as FP32, zero past `cols`.
+// vec: the row start is 16-byte aligned and cols is a multiple of 16 bytes of elements,
+// so the four lie wholly inside or wholly outside the row and load as one vector.
+template <typename XT>
+__device__ __forceinline__ void load_x4(const XT* row, uint32_t col0, uint32_t cols, bool vec, float (&v)[4]) {
+  if (vec) {
+    if (col0 >= cols) {
+      v[0] = v[1] = v[2] = v[3] = 0.0f;
+    } else if constexpr (sizeof(XT) == 2) {
+      const uint2 u = __ldcg(reinterpret_cast<const uint2*>(row + col0));
+      const float2 f0 = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
+      const float2 f1 = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
+      v[0] = f0.x;
+      v[1] = f0.y;
+      v[2] = f1.x;
+      v[3] = f1.y;
+    } else {
+      const float4 f = __ldcg(reinterpret_cast<const float4*>(row + col0));
+      v[0] = f.x;
+      v[1] = f.y;
+      v[2] = f.z;
+      v[3] = f.w;
+    }
+    return;
+  }
+#pragma unroll
+  for (int t = 0; t < 4; ++t) {
+    float f = 0.0f;
+    if (col0 + t < cols) {
+      if constexpr (sizeof(XT) == 2) f = __half2float(row[col0 + t]);
+      else f = row[col0 + t];
+    }
+    v[t] = f;
+  }
+}
+
+// Preparation of W (tile column, batch row) items, one warp per item; lane L holds
+// columns 4L..4L+3 of the item's tile (v, zero past the last column).  Per item:
+//   e    tile exponent: the largest |x| of the tile lands in [2^14, 2^15) after 2^-e;
+//   the B fragments: FP16 x·2^-e·4^-(c%4) of column c at half (4b + c/32)·32 + (c%8)·4
+//        + (c%32)/8 of the slot (XL 2: the FP16 remainder batch·256 bytes further on);
+//   {2^(24+e), 2^(e+1)·Σ_c x̃_c·4^(c%4)} at byte batch·256·XL + 8b, x̃ the stored value.
+// The sum adds each lane's four terms pairwise, then across lanes in butterfly order.
+// Every preparation path (prep_x_kernel and both in-kernel paths) goes through this
+// function, so their fragments are bit-identical.
+template <int XL, int W>
+__device__ __forceinline__ void prep_items(const float (&v)[W][4], const bool (&ok)[W], uint8_t* const (&slot)[W],
+                                           const uint32_t (&b)[W], uint32_t batch, uint32_t lane) {
+  float a[W];
+#pragma unroll
+  for (int w = 0; w < W; ++w)
+    a[w] = fmaxf(fmaxf(fabsf(v[w][0]), fabsf(v[w][1])), fmaxf(fabsf(v[w][2]), fabsf(v[w][3])));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+    for (int w = 0; w < W; ++w) a[w] = fmaxf(a[w], __shfl_xor_sync(0xffffffffu, a[w], o));
+  // column 4L + t: quad L/8, position m = 4(L%2) + t, column group (L%8)/2
+  const uint32_t pos = 32 * (lane >> 3) + 16 * (lane & 1) + ((lane & 7) >> 1);
+  int e[W];
+  float s[W];
+#pragma unroll
+  for (int w = 0; w < W; ++w) {
+    // |x| >= 2^-24 is a normal float, so the biased exponent field gives floor(log2)
+    e[w] = a[w] > 0.0f ? max(-100, min(100, ((__float_as_int(a[w]) >> 23) & 0xff) - 127 - 14)) : 0;
+    __half* dst = reinterpret_cast<__half*>(slot[w]) + b[w] * 128 + pos;
+    float part[4];
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      const float xs = v[w][t] * exp2_int(-e[w] - 2 * t);
+      const __half hi = __float2half_rn(xs);
+      float eff = __half2float(hi);
+      if (ok[w]) dst[4 * t] = hi;
+      if constexpr (XL == 2) {
+        const __half lo = __float2half_rn(xs - eff);
+        eff += __half2float(lo);
+        if (ok[w]) dst[batch * 128 + 4 * t] = lo;
+      }
+      part[t] = eff * exp2_int(2 * t);
+    }
+    s[w] = (part[0] + part[1]) + (part[2] + part[3]);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+    for (int w = 0; w < W; ++w) s[w] += __shfl_xor_sync(0xffffffffu, s[w], o);
+  if (lane == 0) {
+#pragma unroll
+    for (int w = 0; w < W; ++w)
+      if (ok[w])
+        *reinterpret_cast<float2*>(slot[w] + batch * 256 * XL + b[w] * 8) =
+            make_float2(exp2_int(24 + e[w]), s[w] * exp2_int(e[w] + 1));
+  }
+}
+
+// x [batch][cols] -> one fragment slot per 128-column tile; one warp per (tile column,
+// batch row) item, four items per block.
 template <int XL, typename XT>
-__global__ void __launch_bounds__(128) prep_x_kernel(const XT* __restrict__ x, uint32_t cols,
-                                                     uint32_t batch, uint8_t* __restrict__ xfrag,
-                                                     uint32_t xslot) {
-  __shared__ float red[4];
-  const uint32_t c = blockIdx.x, b = blockIdx.y, k = threadIdx.x;
-  const uint32_t col = c * 128 + k;
-  float v = 0.0f;
-  if (col < cols) {
-    if constexpr (sizeof(XT) == 2) v = __half2float(x[static_cast<uint64_t>(b) * cols + col]);
-    else v = x[static_cast<uint64_t>(b) * cols + col];
-  }
-  // tile exponent e: the largest |x| of the tile lands in [2^14, 2^15) after 2^-e
-  float a = fabsf(v);
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
-  if ((k & 31) == 0) red[k >> 5] = a;
-  __syncthreads();
-  const float amax = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
-  __syncthreads();
-  int e = 0;
-  if (amax > 0.0f) e = max(-100, min(100, ilogbf(amax) - 14));
-  const uint32_t m = k & 7, which = (k >> 3) & 3, q = k >> 5, jj = m & 3;
-  const float xs = ldexpf(v, -e - 2 * static_cast<int>(jj));
-  const __half hi = __float2half_rn(xs);
-  float eff = __half2float(hi);
-  uint8_t* slot = xfrag + static_cast<uint64_t>(c) * xslot;
-  const uint32_t idx = (b * 4 + q) * 32 + m * 4 + which;
-  reinterpret_cast<__half*>(slot)[idx] = hi;
-  if constexpr (XL == 2) {
-    const __half lo = __float2half_rn(xs - eff);
-    eff += __half2float(lo);
-    reinterpret_cast<__half*>(slot + batch * 256)[idx] = lo;
-  }
-  float xt = ldexpf(eff, 2 * static_cast<int>(jj));
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) xt += __shfl_xor_sync(0xffffffffu, xt, o);
-  if ((k & 31) == 0) red[k >> 5] = xt;
-  __syncthreads();
-  if (k == 0) {
-    const float sum = (red[0] + red[1]) + (red[2] + red[3]);
-    *reinterpret_cast<float2*>(slot + batch * 256 * XL + b * 8) =
-        make_float2(ldexpf(1.0f, 24 + e), ldexpf(sum, e + 1));
-  }
+__global__ void __launch_bounds__(128) prep_x_kernel(const XT* __restrict__ x, uint32_t cols, uint32_t batch,
+                                                     uint32_t C, uint8_t* __restrict__ xfrag, uint32_t xslot,
+                                                     uint32_t vec) {
+  const uint32_t item = blockIdx.x * 4 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (item >= C * batch) return;  // the whole warp leaves together
+  const uint32_t c = item / batch;
+  float v[1][4];
+  const bool ok[1] = {true};
+  uint8_t* const slot[1] = {xfrag + static_cast<uint64_t>(c) * xslot};
+  const uint32_t b[1] = {item - c * batch};
+  load_x4<XT>(x + static_cast<uint64_t>(b[0]) * cols, c * 128 + 4 * lane, cols, vec != 0, v[0]);
+  prep_items<XL, 1>(v, ok, slot, b, batch, lane);
 }
 
 // --------------------------------------------------------------------------------------
@@ -939,29 +1007,177 @@ __device__ __forceinline__ void load_xfrag(XFrag<NB, XL>& xf, const XLane<NB, XL
   }
 }
 
+// Accumulator chains per tile: one per stage; depth 1 alternates two chains.
+template <int D>
+struct TileChains {
+  static constexpr int value = D == 1 ? 2 : D;
+};
+
+// Tensor-core part of one tile (its D stage records w): D independent MMA chains (two
+// for D == 1); the first MMA of each chain starts from zero.
+template <int NB, int XL, int D>
+__device__ __forceinline__ void tile_mma(const uint4 (&w)[D], const XFrag<NB, XL>& xf, uint32_t shift_mul,
+                                         float (&acc)[TileChains<D>::value][NB][4]) {
+  uint32_t hi[D][4];
+#pragma unroll
+  for (int s = 0; s < D; ++s) {
+    hi[s][0] = __umulhi(w[s].x, shift_mul);
+    hi[s][1] = __umulhi(w[s].y, shift_mul);
+    hi[s][2] = __umulhi(w[s].z, shift_mul);
+    hi[s][3] = __umulhi(w[s].w, shift_mul);
+  }
+#pragma unroll
+  for (int m = 0; m < 8; ++m) {
+#pragma unroll
+    for (int s = 0; s < D; ++s) {
+      const int c = D == 1 ? (m & 1) : s;
+      const bool first = D == 1 ? m < 2 : m == 0;
+      const uint32_t a0 = int2_pair(w[s].x, hi[s][0], m), a1 = int2_pair(w[s].y, hi[s][1], m);
+      const uint32_t a2 = int2_pair(w[s].z, hi[s][2], m), a3 = int2_pair(w[s].w, hi[s][3], m);
+#pragma unroll
+      for (int nb = 0; nb < NB; ++nb)
+#pragma unroll
+        for (int l = 0; l < XL; ++l) {
+          if (first && l == 0) mma_f16_zero(acc[c][nb], a0, a1, a2, a3, xf.bf[nb][l][m][0], xf.bf[nb][l][m][1]);
+          else mma_f16(acc[c][nb], a0, a1, a2, a3, xf.bf[nb][l][m][0], xf.bf[nb][l][m][1]);
+        }
+    }
+  }
+}
+
+// Scale epilogue of one tile into y: y += σ·(acc·2^(24+e) − 2^(e+1)·Σx̃) per stage.
+// With B1 (batch 1) only accumulator column 0 is ever stored: the others are skipped.
+template <int NB, int XL, int D, bool B1>
+__device__ __forceinline__ void tile_epilogue(const uint32_t (&sc)[D], const XFrag<NB, XL>& xf,
+                                              float (&acc)[TileChains<D>::value][NB][4], float (&y)[NB][4]) {
+  constexpr int CH = TileChains<D>::value;
+  if (D == 1) {
+#pragma unroll
+    for (int nb = 0; nb < NB; ++nb) {
+      acc[0][nb][0] += acc[CH - 1][nb][0];
+      acc[0][nb][2] += acc[CH - 1][nb][2];
+      if (!B1) {
+        acc[0][nb][1] += acc[CH - 1][nb][1];
+        acc[0][nb][3] += acc[CH - 1][nb][3];
+      }
+    }
+  }
+#pragma unroll
+  for (int s = 0; s < D; ++s) {
+    const __half2 s2 = *reinterpret_cast<const __half2*>(&sc[s]);
+    const float s_lo = __low2float(s2), s_hi = __high2float(s2);
+#pragma unroll
+    for (int nb = 0; nb < NB; ++nb) {
+      y[nb][0] = fmaf(s_lo, fmaf(acc[s][nb][0], xf.f[nb][0], -xf.gsum[nb][0]), y[nb][0]);
+      y[nb][2] = fmaf(s_hi, fmaf(acc[s][nb][2], xf.f[nb][0], -xf.gsum[nb][0]), y[nb][2]);
+      if (!B1) {
+        y[nb][1] = fmaf(s_lo, fmaf(acc[s][nb][1], xf.f[nb][1], -xf.gsum[nb][1]), y[nb][1]);
+        y[nb][3] = fmaf(s_hi, fmaf(acc[s][nb][3], xf.f[nb][1], -xf.gsum[nb][1]), y[nb][3]);
+      }
+    }
+  }
+}
+
 // A CTA's part of the split tile rows it touches: at most its first and its last row.
 struct SplitRows {
   uint32_t row0, row1;
   uint32_t count;
 };
 
-// End of tile row r for this CTA (units [u0, u1)).  A row wholly inside the range is
-// stored.  A split row is published as this CTA's part (slot 0 for the CTA's first
-// row, 1 for its last) and remembered; finish_split_rows completes it.  No fence and
-// no barrier here, so the stream of tiles goes on.
+// Split tile rows of the uniform stream-K kernel.  A CTA's part of a tile row that goes
+// on in later CTAs is published as 64-bit words {FP32 bits, kPartFlag} in the CTA's one
+// slot [cta][batch][128] of the partials region: one single-copy-atomic store per value,
+// so no fence is needed.  The row's last contributor (the CTA in whose range it ends)
+// waits (bounded) for the words of the earlier contributors, adds them in CTA order and
+// its own part last, stores the rows and clears the words to zero.  Earlier CTAs never
+// wait for later ones, so the scheme needs no co-residency beyond CTA-index order.  The
+// partials region is all zero between launches (every consumer clears what it reads).
+constexpr uint32_t kPartFlag = 0x7fc0a5a5u;  // an FP32 NaN pattern no arithmetic produces
+
+__device__ __forceinline__ unsigned long long ld_relaxed_gpu_u64(const unsigned long long* a) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(a) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_relaxed_gpu_u64(unsigned long long* a, unsigned long long v) {
+  asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(a), "l"(v) : "memory");
+}
+
 template <int NB>
-__device__ __forceinline__ void end_row(const GemvParams& p, uint32_t r, uint64_t units_per_row, uint64_t u0,
-                                        uint64_t u1, uint32_t cta, const float (&y)[NB][4], uint32_t rit0, uint32_t q,
-                                        SplitRows& split) {
-  const uint64_t rb = static_cast<uint64_t>(r) * units_per_row, re = rb + units_per_row;
-  if (rb >= u0 && re <= u1) {
-    store_out<NB>(p, y, r * 128 + rit0, q);
-    return;
+__device__ __forceinline__ void publish_flagged(const GemvParams& p, uint32_t cta, const float (&y)[NB][4],
+                                                uint32_t rit0, uint32_t q) {
+  unsigned long long* part = reinterpret_cast<unsigned long long*>(p.partials) + static_cast<uint64_t>(cta) * p.batch * 128;
+  const unsigned long long flag = static_cast<unsigned long long>(kPartFlag) << 32;
+#pragma unroll
+  for (int nb = 0; nb < NB; ++nb)
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const uint32_t b = 2 * q + j + 8 * nb;
+      if (b < p.batch) {
+        st_relaxed_gpu_u64(part + b * 128 + rit0, flag | __float_as_uint(y[nb][j]));
+        st_relaxed_gpu_u64(part + b * 128 + rit0 + 8, flag | __float_as_uint(y[nb][2 + j]));
+      }
+    }
+}
+
+// The published word at `a`, waiting (bounded; after one timeout a warp no longer waits).
+__device__ __forceinline__ float take_flagged(unsigned long long* a, unsigned long long v, const GemvParams& p,
+                                              bool& gave_up) {
+  if ((v >> 32) != kPartFlag && !gave_up) {
+    const unsigned long long t0 = global_timer_ns();
+    for (;;) {
+      v = ld_relaxed_gpu_u64(a);
+      if ((v >> 32) == kPartFlag) break;
+      if (global_timer_ns() - t0 > kWaitLimitNs) {
+        atomicOr(p.error, HQB_DEVERR_TIMEOUT);
+        gave_up = true;
+        break;
+      }
+      __nanosleep(64);
+    }
   }
-  publish_partial<NB>(p, cta, rb <= u0 ? 0u : 1u, y, rit0, q);
-  if (split.count == 0) split.row0 = r;
-  else split.row1 = r;
-  ++split.count;
+  st_relaxed_gpu_u64(a, 0ull);
+  return __uint_as_float(static_cast<uint32_t>(v));
+}
+
+// Row r ends in this CTA (the last contributor): add the earlier contributors' parts in
+// CTA order, then this warp's own part, plus bias, and store its rows.
+template <int NB>
+__device__ __forceinline__ void reduce_split_row(const GemvParams& p, uint32_t r, uint64_t units_per_row,
+                                                 uint64_t total, uint32_t ctas, uint32_t cta,
+                                                 const float (&own)[NB][4], uint32_t rit0, uint32_t q) {
+  const uint32_t first = unit_owner(static_cast<uint64_t>(r) * units_per_row, total, ctas);
+  unsigned long long* part = reinterpret_cast<unsigned long long*>(p.partials);
+  bool gave_up = false;
+#pragma unroll
+  for (int nb = 0; nb < NB; ++nb)
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const uint32_t b = 2 * q + j + 8 * nb;
+      if (b >= p.batch) continue;
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const uint32_t rit = rit0 + 8 * h, row = r * 128 + rit;
+        float sum = 0.0f;
+        for (uint32_t i0 = first; i0 < cta; i0 += 8) {  // 8 independent loads, summed in order
+          unsigned long long v[8];
+#pragma unroll
+          for (uint32_t k = 0; k < 8; ++k)
+            v[k] = i0 + k < cta ? ld_relaxed_gpu_u64(part + (static_cast<uint64_t>(i0 + k) * p.batch + b) * 128 + rit)
+                                : 0ull;
+#pragma unroll
+          for (uint32_t k = 0; k < 8; ++k)
+            if (i0 + k < cta)
+              sum += take_flagged(part + (static_cast<uint64_t>(i0 + k) * p.batch + b) * 128 + rit, v[k], p, gave_up);
+        }
+        sum += own[nb][2 * h + j];
+        if (row >= p.rows) continue;
+        if (p.bias != nullptr)
+          sum += p.bias_dtype == HQB_F16 ? __half2float(static_cast<const __half*>(p.bias)[row])
+                                         : static_cast<const float*>(p.bias)[row];
+        put_y(p, b, row, sum);
+      }
+    }
 }
 
 // After the CTA's last tile: one barrier, then one arrival per split row on a per-row
@@ -1020,7 +1236,12 @@ __device__ __forceinline__ void finish_split_rows(const GemvParams& p, const Spl
       }
 #pragma unroll
       for (uint32_t j = 0; j < 8; ++j)
-        if (i0 + j <= last) sum += v[j];
+        if (i0 + j <= last) {
+          sum += v[j];
+          // the partials region is zero between launches
+          const uint64_t off = (i0 + j) * cta_stride + (i0 + j == first ? s_info[4 + 4 * k] * p.batch * 128 : 0u);
+          __stcg(const_cast<float*>(src) + off, 0.0f);
+        }
     }
     if (p.bias != nullptr)
       sum += p.bias_dtype == HQB_F16 ? __half2float(static_cast<const __half*>(p.bias)[row])
@@ -1043,9 +1264,6 @@ __device__ __forceinline__ void gather_signal(const GemvParams& p, uint32_t ctas
   }
 }
 
-// 2^k as a float for -126 <= k <= 127 (normal range), from the IEEE-754 bit layout.
-__device__ __forceinline__ float exp2_int(int k) { return __int_as_float((k + 127) << 23); }
-
 // Tile columns a CTA needs: one range [a0, a1], plus [b0, b1] when its tiles wrap from
 // the end of one tile row into the start of the next without covering every column.
 struct ColRanges {
@@ -1062,48 +1280,22 @@ __device__ __forceinline__ ColRanges needed_columns(uint32_t t0, uint32_t t_end,
 }
 
 // Activation fragments of the needed tile columns, built from raw x (FP16 for XL 1,
-// FP32 for XL 2) by the CTA itself with the arithmetic of prep_x_kernel (same tile
-// exponent, same rounding, same summation order), so they are bit-identical to a
-// separately prepared buffer.  Raw rows are first staged in shared memory at `raw`
-// ([batch][C * 128], only the needed columns filled).
+// FP32 for XL 2) by the CTA itself through prep_items, so they are bit-identical to a
+// separately prepared buffer.  Each warp reads its items' activations straight from
+// global memory; two items per warp at a time, so their shuffle chains interleave.
 template <int XL>
-__device__ __forceinline__ void build_xfrag_tiles(const GemvParams& p, uint8_t* xres, uint8_t* raw,
-                                                  const ColRanges& cr) {
+__device__ __forceinline__ void build_xfrag_tiles(const GemvParams& p, uint8_t* xres, const ColRanges& cr) {
   using XT = typename std::conditional<XL == 1, __half, float>::type;
-  constexpr uint32_t ES = sizeof(XT);
-  const uint32_t ncol = cr.count(), span = p.C * 128;
   const XT* x = static_cast<const XT*>(p.x_raw);
-  if (p.x_vec) {  // cols * ES is a multiple of 16: a chunk lies wholly inside or outside a row
-    constexpr uint32_t per_chunk = 16 / ES, chunks_col = 128 / per_chunk;
-    const uint32_t chunks_row = ncol * chunks_col;
-    for (uint32_t t = threadIdx.x; t < chunks_row * p.batch; t += kStreamThreads) {
-      const uint32_t b = t / chunks_row, i = t - b * chunks_row, ci = i / chunks_col;
-      const uint32_t col = cr.col(ci) * 128 + (i - ci * chunks_col) * per_chunk;
-      uint4 v = make_uint4(0u, 0u, 0u, 0u);
-      if (col < p.cols) v = __ldcg(reinterpret_cast<const uint4*>(x + static_cast<uint64_t>(b) * p.cols + col));
-      *reinterpret_cast<uint4*>(raw + (static_cast<uint64_t>(b) * span + col) * ES) = v;
-    }
-  } else {
-    const uint32_t per_row = ncol * 128;
-    for (uint32_t t = threadIdx.x; t < per_row * p.batch; t += kStreamThreads) {
-      const uint32_t b = t / per_row, i = t - b * per_row;
-      const uint32_t col = cr.col(i >> 7) * 128 + (i & 127);
-      XT v{};
-      if (col < p.cols) v = x[static_cast<uint64_t>(b) * p.cols + col];
-      reinterpret_cast<XT*>(raw)[static_cast<uint64_t>(b) * span + col] = v;
-    }
-  }
-  __syncthreads();
   const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const uint32_t m = lane & 7, which = (lane >> 3) & 3, jj = m & 3;  // lane + 32i has the same m, which
-  // Two (column, batch row) items per warp at a time: their shuffle chains interleave.
   constexpr int W = 2;
   constexpr uint32_t kWarps = kStreamThreads / 32;
-  const uint32_t items = ncol * p.batch;
+  const uint32_t items = cr.count() * p.batch;
   for (uint32_t base = warp; base < items; base += W * kWarps) {
-    float v[W][4], a[W];
-    uint32_t b[W], c[W];
+    float v[W][4];
     bool ok[W];
+    uint8_t* slot[W];
+    uint32_t b[W];
 #pragma unroll
     for (int w = 0; w < W; ++w) {
       const uint32_t item = base + w * kWarps;
@@ -1111,59 +1303,11 @@ __device__ __forceinline__ void build_xfrag_tiles(const GemvParams& p, uint8_t* 
       const uint32_t it = ok[w] ? item : base;
       const uint32_t ci = it / p.batch;
       b[w] = it - ci * p.batch;
-      c[w] = cr.col(ci);
-      const XT* rx = reinterpret_cast<const XT*>(raw) + static_cast<uint64_t>(b[w]) * span + c[w] * 128;
-      a[w] = 0.0f;
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        if constexpr (XL == 1) v[w][i] = __half2float(rx[lane + 32 * i]);
-        else v[w][i] = rx[lane + 32 * i];
-        a[w] = fmaxf(a[w], fabsf(v[w][i]));
-      }
+      const uint32_t c = cr.col(ci);
+      slot[w] = xres + c * p.xslot_bytes;
+      load_x4<XT>(x + static_cast<uint64_t>(b[w]) * p.cols, c * 128 + 4 * lane, p.cols, p.x_vec != 0, v[w]);
     }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1)
-#pragma unroll
-      for (int w = 0; w < W; ++w) a[w] = fmaxf(a[w], __shfl_xor_sync(0xffffffffu, a[w], o));
-    float part[W][4];
-    int e[W];
-#pragma unroll
-    for (int w = 0; w < W; ++w) {
-      // tile exponent: the largest |x| lands in [2^14, 2^15); |x| >= 2^-24 is a normal float
-      e[w] = 0;
-      if (a[w] > 0.0f) e[w] = max(-100, min(100, ((__float_as_int(a[w]) >> 23) & 0xff) - 127 - 14));
-      const float down = exp2_int(-e[w] - 2 * static_cast<int>(jj)), up = exp2_int(2 * static_cast<int>(jj));
-      uint8_t* slot = xres + c[w] * p.xslot_bytes;
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {  // column lane + 32i: q = i
-        const float xs = v[w][i] * down;
-        const __half hi = __float2half_rn(xs);
-        float eff = __half2float(hi);
-        const uint32_t idx = (b[w] * 4 + i) * 32 + m * 4 + which;
-        if (ok[w]) reinterpret_cast<__half*>(slot)[idx] = hi;
-        if constexpr (XL == 2) {
-          const __half lo = __float2half_rn(xs - eff);
-          eff += __half2float(lo);
-          if (ok[w]) reinterpret_cast<__half*>(slot + p.batch * 256)[idx] = lo;
-        }
-        part[w][i] = eff * up;
-      }
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1)
-#pragma unroll
-      for (int w = 0; w < W; ++w)
-#pragma unroll
-        for (int i = 0; i < 4; ++i) part[w][i] += __shfl_xor_sync(0xffffffffu, part[w][i], o);
-    if (lane == 0) {
-#pragma unroll
-      for (int w = 0; w < W; ++w) {
-        if (!ok[w]) continue;
-        const float sum = (part[w][0] + part[w][1]) + (part[w][2] + part[w][3]);
-        *reinterpret_cast<float2*>(xres + c[w] * p.xslot_bytes + p.batch * 256 * XL + b[w] * 8) =
-            make_float2(exp2_int(24 + e[w]), sum * exp2_int(e[w] + 1));
-      }
-    }
+    prep_items<XL, W>(v, ok, slot, b, p.batch, lane);
   }
 }
 
@@ -1173,7 +1317,6 @@ __global__ void __launch_bounds__(kStreamThreads, (NB == 1 && XL == 1) ? 2 : 1)
   constexpr int R = TilesAhead<D>::value;
   constexpr uint32_t kFull = (1u << D) - 1u;
   extern __shared__ __align__(16) uint8_t xres[];  // [C x xslot activation fragments]
-  __shared__ uint32_t s_info[9];
   const uint64_t total = p.total;
   const uint32_t ctas = static_cast<uint32_t>(total < gridDim.x ? total : gridDim.x), cta = blockIdx.x;
   griddep_launch_dependents();  // a following PDL kernel may be scheduled; it waits for this grid
@@ -1240,7 +1383,7 @@ __global__ void __launch_bounds__(kStreamThreads, (NB == 1 && XL == 1) ? 2 : 1)
     const bool one_row = t0 / p.C == t_end / p.C;
     const uint32_t c_lo = one_row ? c_first : 0, c_hi = one_row ? c_last : p.C - 1;
     if (p.x_raw != nullptr) {
-      build_xfrag_tiles<XL>(p, xres, xres + p.raw_offset, needed_columns(t0, t_end, p.C));
+      build_xfrag_tiles<XL>(p, xres, needed_columns(t0, t_end, p.C));
     } else {
       const uint4* src = reinterpret_cast<const uint4*>(p.xfrag + static_cast<uint64_t>(c_lo) * p.xslot_bytes);
       uint4* dst = reinterpret_cast<uint4*>(xres + c_lo * p.xslot_bytes);
@@ -1260,71 +1403,28 @@ __global__ void __launch_bounds__(kStreamThreads, (NB == 1 && XL == 1) ? 2 : 1)
 #pragma unroll
     for (int e = 0; e < 4; ++e) y[nb][e] = 0.0f;
 
-  // Tensor-core part of one tile from ring slot j: D independent MMA chains (two for
-  // D == 1); the first MMA of each chain starts from zero.
-  constexpr int CH = D == 1 ? 2 : D;  // depth 1 alternates two chains
-  auto mma_tile = [&](int j, const XFrag<NB, XL>& xf, float (&acc)[CH][NB][4]) {
-    uint32_t hi[D][4];
-#pragma unroll
-    for (int s = 0; s < D; ++s) {
-      hi[s][0] = __umulhi(w[j][s].x, p.shift_mul);
-      hi[s][1] = __umulhi(w[j][s].y, p.shift_mul);
-      hi[s][2] = __umulhi(w[j][s].z, p.shift_mul);
-      hi[s][3] = __umulhi(w[j][s].w, p.shift_mul);
-    }
-#pragma unroll
-    for (int m = 0; m < 8; ++m) {
-#pragma unroll
-      for (int s = 0; s < D; ++s) {
-        const int c = D == 1 ? (m & 1) : s;
-        const bool first = D == 1 ? m < 2 : m == 0;
-        const uint32_t a0 = int2_pair(w[j][s].x, hi[s][0], m), a1 = int2_pair(w[j][s].y, hi[s][1], m);
-        const uint32_t a2 = int2_pair(w[j][s].z, hi[s][2], m), a3 = int2_pair(w[j][s].w, hi[s][3], m);
-#pragma unroll
-        for (int nb = 0; nb < NB; ++nb)
-#pragma unroll
-          for (int l = 0; l < XL; ++l) {
-            if (first && l == 0) mma_f16_zero(acc[c][nb], a0, a1, a2, a3, xf.bf[nb][l][m][0], xf.bf[nb][l][m][1]);
-            else mma_f16(acc[c][nb], a0, a1, a2, a3, xf.bf[nb][l][m][0], xf.bf[nb][l][m][1]);
-          }
-      }
-    }
-  };
-  // Scale epilogue of one tile into y.
-  // With B1 (batch 1) only accumulator column 0 is ever stored: the others are skipped.
-  auto epi_tile = [&](int j, const XFrag<NB, XL>& xf, float (&acc)[CH][NB][4]) {
-    if (D == 1) {
-#pragma unroll
-      for (int nb = 0; nb < NB; ++nb) {
-        acc[0][nb][0] += acc[CH - 1][nb][0];
-        acc[0][nb][2] += acc[CH - 1][nb][2];
-        if (!B1) {
-          acc[0][nb][1] += acc[CH - 1][nb][1];
-          acc[0][nb][3] += acc[CH - 1][nb][3];
-        }
-      }
-    }
-#pragma unroll
-    for (int s = 0; s < D; ++s) {
-      const __half2 s2 = *reinterpret_cast<const __half2*>(&sc[j][s]);
-      const float s_lo = __low2float(s2), s_hi = __high2float(s2);
-#pragma unroll
-      for (int nb = 0; nb < NB; ++nb) {
-        y[nb][0] = fmaf(s_lo, fmaf(acc[s][nb][0], xf.f[nb][0], -xf.gsum[nb][0]), y[nb][0]);
-        y[nb][2] = fmaf(s_hi, fmaf(acc[s][nb][2], xf.f[nb][0], -xf.gsum[nb][0]), y[nb][2]);
-        if (!B1) {
-          y[nb][1] = fmaf(s_lo, fmaf(acc[s][nb][1], xf.f[nb][1], -xf.gsum[nb][1]), y[nb][1]);
-          y[nb][3] = fmaf(s_hi, fmaf(acc[s][nb][3], xf.f[nb][1], -xf.gsum[nb][1]), y[nb][3]);
-        }
-      }
-    }
-  };
-  // After tile k: the row may end (its last tile, or the CTA's last tile).
-  SplitRows split{0u, 0u, 0u};
+  constexpr int CH = TileChains<D>::value;
+  // After tile k: the row may end (its last tile, or the CTA's last tile).  A row wholly
+  // inside the range is stored; one that goes on in later CTAs is published; the CTA's
+  // first row, when it began in an earlier CTA and ends here, is kept and summed after
+  // the last tile.
+  float kept[NB][4];
+  bool keep = false;
   auto advance = [&](uint32_t k) {
     xs += p.xslot_bytes;
     if (--left == 0 || k + 1 == ntiles) {
-      end_row<NB>(p, row, units_per_row, u0, u1, cta, y, rit0, q, split);
+      const uint64_t rb = static_cast<uint64_t>(row) * units_per_row, re = rb + units_per_row;
+      if (rb >= u0 && re <= u1) {
+        store_out<NB>(p, y, row * 128 + rit0, q);
+      } else if (re > u1) {
+        publish_flagged<NB>(p, cta, y, rit0, q);
+      } else {
+        keep = true;
+#pragma unroll
+        for (int nb = 0; nb < NB; ++nb)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) kept[nb][e] = y[nb][e];
+      }
 #pragma unroll
       for (int nb = 0; nb < NB; ++nb)
 #pragma unroll
@@ -1338,8 +1438,8 @@ __global__ void __launch_bounds__(kStreamThreads, (NB == 1 && XL == 1) ? 2 : 1)
     XFrag<NB, XL> xf;
     load_xfrag<NB, XL>(xf, xlane, xs);
     float acc[CH][NB][4];
-    mma_tile(j, xf, acc);
-    epi_tile(j, xf, acc);
+    tile_mma<NB, XL, D>(w[j], xf, p.shift_mul, acc);
+    tile_epilogue<NB, XL, D, B1>(sc[j], xf, acc, y);
   };
 
   uint32_t k0 = 0;
@@ -1361,8 +1461,236 @@ __global__ void __launch_bounds__(kStreamThreads, (NB == 1 && XL == 1) ? 2 : 1)
     one_tile(j);
     advance(k);
   }
-  if (split.count != 0) finish_split_rows<NB>(p, split, units_per_row, total, ctas, s_info);
+  if (keep) reduce_split_row<NB>(p, t0 / p.C, units_per_row, total, ctas, cta, kept, rit0, q);
   if (p.g_world > 1) gather_signal(p, ctas);
+}
+
+// --------------------------------------------------------------------------------------
+// Row-block GEMV (uniform depth, batch <= 8): the default for a uniform prefix.
+//
+// Work item: row block b (16 output rows) of tile row r across all C tiles and the D
+// selected stages, item index 8r + b.  CTA c (one CTA of kRowsWarps warps per SM) takes
+// items c, c + G, c + 2G, ...; the 8 row blocks of a tile row go to 8 consecutive CTAs,
+// which together read whole tile records at about the same time.  An item's C·D
+// (tile, stage) units are split over the warps in contiguous ranges, the same range for
+// every item, so a warp needs the activation fragments of the same few tile columns
+// throughout and prepares them once, in its own shared-memory area.
+//
+// At the end of its range of an item a warp stores its partial sums (16 rows x batch)
+// into a shared-memory slot and signals a named barrier without waiting (bar.arrive);
+// the item's reducer warp (item j: warp j % 16, which spreads the waiting) completes the
+// barrier with bar.sync, adds the parts in warp order, adds the bias and stores the
+// rows.  No memory fence is needed, so the register prefetch of the other warps stays in
+// flight, and no tile row is split between CTAs, so no partial sums travel through
+// global memory.  Reduction slots (one named barrier each) alternate between items; a
+// warp that gets kRedSlots items ahead waits (bounded) until the older item is summed.
+
+constexpr uint32_t kRowsWarps = 16;
+constexpr uint32_t kRowsThreads = kRowsWarps * 32;
+constexpr uint32_t kRedSlots = 2;
+constexpr uint32_t kRedSlotFloats = kRowsWarps * 16 * 8;  // [warp][row 0..15][batch 0..7]
+constexpr uint32_t kRowsHeadBytes = kRedSlots * kRedSlotFloats * 4 + 256;
+constexpr uint32_t kRowsSmemMax = 200 * 1024;
+constexpr uint32_t kRowsUnitsMax = 16;  // size rule of the default kernel choice
+
+// First unit of warp w's range among the U units of an item.
+__host__ __device__ inline uint32_t rows_unit_start(uint32_t w, uint32_t U) {
+  return static_cast<uint32_t>(static_cast<uint64_t>(w) * U / kRowsWarps);
+}
+
+template <int XL, int D, bool B1>
+__global__ void __launch_bounds__(kRowsThreads, 1) gemv_rows_kernel(const __grid_constant__ GemvParams p) {
+  using XT = typename std::conditional<XL == 1, __half, float>::type;
+  constexpr int R = TilesAhead<D>::value;
+  constexpr int CH = TileChains<D>::value;
+  constexpr uint32_t kFull = (1u << D) - 1u;
+  extern __shared__ __align__(128) uint8_t smem[];
+  // [kRedSlots][kRowsWarps][16][8] partial sums | slot generations | fragments
+  float* red = reinterpret_cast<float*>(smem);
+  volatile uint32_t* gen = reinterpret_cast<uint32_t*>(smem + kRedSlots * kRedSlotFloats * 4);
+  volatile uint32_t* gave_up = gen + kRedSlots;  // a slot wait timed out: no warp waits again
+  griddep_launch_dependents();  // a following PDL kernel may be scheduled; it waits for this grid
+  const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, q = lane & 3;
+  const uint32_t C = p.C, U = C * D, G = gridDim.x, cta = blockIdx.x;
+  const uint32_t items = p.R * 8;
+  const uint32_t n_items = cta < items ? (items - cta - 1) / G + 1 : 0;
+  // this warp's units [ua, ub) of every item: tiles ta..te, the first and last partial
+  const uint32_t ua = rows_unit_start(warp, U), ub = rows_unit_start(warp + 1, U);
+  uint32_t ta = 0, te = 0, mask_first = kFull, mask_last = kFull;
+  if (ua < ub) {
+    ta = ua / D;
+    te = (ub - 1) / D;
+    mask_first = kFull & ~((1u << (ua % D)) - 1u);
+    mask_last = (1u << ((ub - 1) % D + 1)) - 1u;
+  }
+  const uint32_t nt = te - ta + 1;
+  const uint32_t total = ua < ub ? n_items * nt : 0;  // tiles this warp streams
+  // byte offset of this lane's code slot in tile column ta of item i (planes < 4 GiB)
+  const uint32_t scale_rel = 512 + g * 4 - lane * 16;
+  auto item_off = [&](uint32_t i) -> uint32_t {
+    return ((i >> 3) * C + ta) * kRecordBytes + (i & 7) * kRowBlockBytes + lane * 16;
+  };
+
+  // Register ring of R tiles x D stages, filled in the warp's tile order.  A stage
+  // outside the warp's units gets scale 0 (codes 0): it contributes exactly zero.
+  uint4 w[R][D];
+  uint32_t sc[R][D];
+  uint32_t lt = ta, lj = 0;  // next tile to load: column lt of the CTA's item lj
+  uint32_t loff = item_off(cta);  // its code-slot offset
+  auto load_next = [&](int slot) {
+    const uint32_t mask = (lt == ta ? mask_first : kFull) & (lt == te ? mask_last : kFull);
+    const uint32_t soff = loff + scale_rel;
+#pragma unroll
+    for (int s = 0; s < D; ++s) {
+      if (D == 1 || (mask & (1u << s))) {
+        asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                     : "=r"(w[slot][s].x), "=r"(w[slot][s].y), "=r"(w[slot][s].z), "=r"(w[slot][s].w)
+                     : "l"(p.planes[s] + loff));
+        asm volatile("ld.global.nc.L1::no_allocate.u32 %0, [%1];" : "=r"(sc[slot][s]) : "l"(p.planes[s] + soff));
+      } else {
+        w[slot][s] = make_uint4(0u, 0u, 0u, 0u);
+        sc[slot][s] = 0u;
+      }
+    }
+    if (++lt > te) {
+      lt = ta;
+      ++lj;
+      loff = item_off(cta + lj * G);
+    } else {
+      loff += kRecordBytes;
+    }
+  };
+#pragma unroll
+  for (int j = 0; j < R; ++j)
+    if (static_cast<uint32_t>(j) < total) load_next(j);
+  if (threadIdx.x < kRedSlots) gen[threadIdx.x] = threadIdx.x;
+  if (threadIdx.x == 0) *gave_up = 0u;
+  __syncthreads();
+  griddep_wait();
+
+  // activation fragments of tile columns ta..te, in this warp's own area
+  uint8_t* xw = smem + kRowsHeadBytes + warp * p.xw_bytes;
+  if (total != 0) {
+    if (p.x_raw != nullptr) {
+      const XT* x = static_cast<const XT*>(p.x_raw);
+      const uint32_t n = nt * p.batch;
+      for (uint32_t base = 0; base < n; base += 2) {
+        float v[2][4];
+        bool ok[2];
+        uint8_t* slot[2];
+        uint32_t b[2];
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+          ok[i] = base + i < n;
+          const uint32_t it = ok[i] ? base + i : base;
+          const uint32_t t = B1 ? it : it / p.batch;
+          b[i] = it - t * p.batch;
+          slot[i] = xw + t * p.xslot_bytes;
+          load_x4<XT>(x + static_cast<uint64_t>(b[i]) * p.cols, (ta + t) * 128 + 4 * lane, p.cols, p.x_vec != 0,
+                      v[i]);
+        }
+        prep_items<XL, 2>(v, ok, slot, b, p.batch, lane);
+      }
+    } else {
+      const uint4* src = reinterpret_cast<const uint4*>(p.xfrag + static_cast<uint64_t>(ta) * p.xslot_bytes);
+      uint4* dst = reinterpret_cast<uint4*>(xw);
+      const uint32_t chunks = nt * p.xslot_bytes / 16;
+      for (uint32_t k = lane; k < chunks; k += 32) dst[k] = __ldcg(src + k);
+    }
+    __syncwarp();
+  }
+
+  // warps with a non-empty range take part in every item; with fewer units than warps
+  // warp 15 (whose range is never empty) reduces every item
+  uint32_t members = 0;
+#pragma unroll
+  for (uint32_t k = 0; k < kRowsWarps; ++k)
+    if (rows_unit_start(k, U) < rows_unit_start(k + 1, U)) members |= 1u << k;
+  const uint32_t bar_threads = 32u * __popc(members);
+  const bool all_members = U >= kRowsWarps;
+
+  const XLane<1, XL> xlane(p.batch, lane);
+  float y[1][4] = {{0.0f, 0.0f, 0.0f, 0.0f}};
+  uint32_t ct = ta, cj = 0;  // tile being computed: column ct of the CTA's item cj
+  const uint8_t* xs = xw;
+
+  // End of this warp's range of item j: publish its part; the item's reducer sums.
+  auto finish_item = [&](uint32_t j) {
+    const uint32_t s = j & (kRedSlots - 1);
+    if (lane == 0 && gen[s] != j && *gave_up == 0u) {  // free once item j - kRedSlots is summed
+      const unsigned long long t0 = global_timer_ns();
+      while (gen[s] != j) {
+        if (global_timer_ns() - t0 > kWaitLimitNs) {
+          atomicOr(p.error, HQB_DEVERR_TIMEOUT);
+          *gave_up = 1u;
+          break;
+        }
+        __nanosleep(32);
+      }
+    }
+    __syncwarp();
+    float* part = red + s * kRedSlotFloats;
+    if (B1) {
+      if (q == 0) {
+        part[warp * 16 + g] = y[0][0];
+        part[warp * 16 + g + 8] = y[0][2];
+      }
+    } else {
+      float* mine = part + warp * 128;
+      *reinterpret_cast<float2*>(mine + g * 8 + 2 * q) = make_float2(y[0][0], y[0][1]);
+      *reinterpret_cast<float2*>(mine + (g + 8) * 8 + 2 * q) = make_float2(y[0][2], y[0][3]);
+    }
+    y[0][0] = y[0][1] = y[0][2] = y[0][3] = 0.0f;
+    __syncwarp();
+    const uint32_t reducer = all_members ? (j & (kRowsWarps - 1)) : kRowsWarps - 1;
+    if (warp != reducer) {
+      named_bar_arrive(1 + s, bar_threads);
+    } else {
+      named_bar_sync(1 + s, bar_threads);
+      const uint32_t i = cta + j * G, row0 = (i >> 3) * 128 + (i & 7) * 16;
+      for (uint32_t e = lane; e < (B1 ? 16u : 128u); e += 32) {
+        const uint32_t rr = B1 ? e : e >> 3, b = B1 ? 0u : e & 7;
+        const uint32_t row = row0 + rr;
+        if (b >= p.batch || row >= p.rows) continue;
+        float sum = 0.0f;
+#pragma unroll
+        for (uint32_t k = 0; k < kRowsWarps; ++k)
+          if (members & (1u << k)) sum += B1 ? part[k * 16 + rr] : part[k * 128 + e];
+        if (p.bias != nullptr)
+          sum += p.bias_dtype == HQB_F16 ? __half2float(static_cast<const __half*>(p.bias)[row])
+                                         : static_cast<const float*>(p.bias)[row];
+        put_y(p, b, row, sum);
+      }
+      __syncwarp();  // every lane has read the slot
+      if (lane == 0) gen[s] = j + kRedSlots;
+    }
+  };
+  auto one_tile = [&](int j) {
+    XFrag<1, XL> xf;
+    load_xfrag<1, XL>(xf, xlane, xs);
+    float acc[CH][1][4];
+    tile_mma<1, XL, D>(w[j], xf, p.shift_mul, acc);
+    tile_epilogue<1, XL, D, B1>(sc[j], xf, acc, y);
+  };
+  for (uint32_t k0 = 0; k0 < total; k0 += R) {
+#pragma unroll
+    for (int j = 0; j < R; ++j) {
+      if (k0 + j < total) {
+        one_tile(j);
+        if (k0 + j + R < total) load_next(j);  // refill slot j with tile k0 + j + R
+        if (ct == te) {
+          finish_item(cj);
+          ct = ta;
+          ++cj;
+          xs = xw;
+        } else {
+          ++ct;
+          xs += p.xslot_bytes;
+        }
+      }
+    }
+  }
+  if (p.g_world > 1) gather_signal(p, G);
 }
 
 // --------------------------------------------------------------------------------------
@@ -1729,6 +2057,9 @@ __global__ void __launch_bounds__(256) fixup_kernel(const __grid_constant__ Gemv
       sum += v3;
     }
     for (; i <= rs.last; ++i) sum += src[i * cta_stride];
+    // the partials region is zero between launches
+    const_cast<float*>(src)[rs.first * cta_stride + first_slot * p.batch * 128] = 0.0f;
+    for (i = rs.first + 1; i <= rs.last; ++i) const_cast<float*>(src)[i * cta_stride] = 0.0f;
     if (p.bias != nullptr)
       sum += p.bias_dtype == HQB_F16 ? __half2float(static_cast<const __half*>(p.bias)[row])
                                      : static_cast<const float*>(p.bias)[row];
@@ -1857,8 +2188,10 @@ struct WsLayout {
 };
 
 // [error word][split-row counters: R uint32][split-row partials: G x 2 x batch x 128
-// FP32][prepared activations: mma fragments][prepared activations: tcgen05 B blocks].  The error word and the counters must start at zero
-// (hqb_workspace_init); the counters return to zero at the end of every launch.
+// FP32, or G x batch x 128 flagged 64-bit words for the uniform stream-K kernel]
+// [prepared activations: mma fragments][prepared activations: tcgen05 B blocks].  The
+// error word, the counters and the partials must start at zero (hqb_workspace_init);
+// counters and partials return to zero at the end of every launch.
 WsLayout ws_layout(uint32_t R, uint32_t C, uint32_t batch, uint32_t xl, int sms) {
   WsLayout L{};
   L.counters = 256;
@@ -1903,6 +2236,33 @@ GemvKernel pick_uniform_kernel(uint32_t nb, uint32_t xl, uint32_t d, uint32_t ba
   return xl == 1 ? pick_uniform_depth<2, 1>(d) : pick_uniform_depth<2, 2>(d);
 }
 
+template <int XL, bool B1>
+GemvKernel pick_rows_depth(uint32_t d) {
+  switch (d) {
+    case 1: return gemv_rows_kernel<XL, 1, B1>;
+    case 2: return gemv_rows_kernel<XL, 2, B1>;
+    case 3: return gemv_rows_kernel<XL, 3, B1>;
+    default: return gemv_rows_kernel<XL, 4, B1>;
+  }
+}
+
+GemvKernel pick_rows_kernel(uint32_t xl, uint32_t d, uint32_t batch) {
+  if (xl == 1) return batch == 1 ? pick_rows_depth<1, true>(d) : pick_rows_depth<1, false>(d);
+  return pick_rows_depth<2, false>(d);
+}
+
+// Fragment bytes per warp area of the row-block kernel: the most tile columns any warp's
+// unit range touches, times the slot size.
+uint32_t rows_xw_bytes(uint32_t C, uint32_t d, uint32_t xslot) {
+  const uint32_t U = C * d;
+  uint32_t nt = 0;
+  for (uint32_t w = 0; w < kRowsWarps; ++w) {
+    const uint32_t ua = rows_unit_start(w, U), ub = rows_unit_start(w + 1, U);
+    if (ua < ub) nt = std::max(nt, (ub - 1) / d - ua / d + 1);
+  }
+  return nt * xslot;
+}
+
 GemvKernel pick_stream_kernel(uint32_t nb, uint32_t xl) {
   if (nb == 1) return xl == 1 ? gemv_stream_kernel<1, 1> : gemv_stream_kernel<1, 2>;
   return xl == 1 ? gemv_stream_kernel<2, 1> : gemv_stream_kernel<2, 2>;
@@ -1931,8 +2291,6 @@ RingShape ring_shape(uint32_t slot_x, uint32_t cap, uint32_t resident) {
 }
 
 constexpr uint32_t kXResidentMax = 64 * 1024;
-// Shared memory for in-kernel activation preparation: fragments plus staged raw rows.
-constexpr uint64_t kFusedXMax = 96 * 1024;
 constexpr uint64_t kFusedTilesMax = 24;
 
 uint32_t gemv_smem_cap() {
@@ -1941,7 +2299,7 @@ uint32_t gemv_smem_cap() {
     m = std::max(m, ring_shape(xslot_bytes_for(HQB_MAX_BATCH, 2), cap, 0).smem);
   for (uint32_t cap = 1; cap <= HQB_MAX_STAGES; ++cap)
     m = std::max(m, ring_shape(0, cap, kXResidentMax).smem);
-  return std::max(m, kSmemBudget + 1024);
+  return std::max(std::max(m, kSmemBudget + 1024), kRowsSmemMax);
 }
 
 // Resident CTAs per SM for a kernel variant at a given shared-memory size (cached).
@@ -1999,17 +2357,24 @@ cudaError_t launch_tc(const GemvParams& p, uint32_t grid, uint32_t smem, bool pd
   return cudaLaunchKernelEx(&cfg, gemv_tc_kernel<D>, p);
 }
 
+// Raw activation rows that load as aligned vectors: a 16-byte aligned start and rows of
+// a multiple of 16 bytes.
+bool x_rows_vec(const void* x, uint64_t cols, uint32_t xl) {
+  return (reinterpret_cast<uintptr_t>(x) & 15u) == 0 && (cols * (xl == 1 ? 2 : 4)) % 16 == 0;
+}
+
 cudaError_t launch_prep(const void* x, int x_dtype, uint64_t cols, uint32_t batch, void* xfrag, cudaStream_t st) {
   const uint32_t C = static_cast<uint32_t>((cols + 127) / 128);
   const uint32_t xl = x_dtype == HQB_F32 ? 2 : 1;
-  const dim3 grid(C, batch);
+  const uint32_t blocks = (C * batch + 3) / 4;  // one warp per (tile column, batch row)
   const uint32_t xs = xslot_bytes_for(batch, xl);
+  const uint32_t vec = x_rows_vec(x, cols, xl) ? 1u : 0u;
   if (x_dtype == HQB_F32)
-    prep_x_kernel<2, float><<<grid, 128, 0, st>>>(static_cast<const float*>(x), static_cast<uint32_t>(cols), batch,
-                                                  static_cast<uint8_t*>(xfrag), xs);
+    prep_x_kernel<2, float><<<blocks, 128, 0, st>>>(static_cast<const float*>(x), static_cast<uint32_t>(cols), batch,
+                                                    C, static_cast<uint8_t*>(xfrag), xs, vec);
   else
-    prep_x_kernel<1, __half><<<grid, 128, 0, st>>>(static_cast<const __half*>(x), static_cast<uint32_t>(cols), batch,
-                                                   static_cast<uint8_t*>(xfrag), xs);
+    prep_x_kernel<1, __half><<<blocks, 128, 0, st>>>(static_cast<const __half*>(x), static_cast<uint32_t>(cols),
+                                                     batch, C, static_cast<uint8_t*>(xfrag), xs, vec);
   return cudaGetLastError();
 }
 
@@ -2136,6 +2501,7 @@ int gemv_impl(const hqb_plane_matrix* m, uint32_t prefix, const uint8_t* depth, 
   if ((x_dtype != HQB_F16 && x_dtype != HQB_F32) || (y_dtype != HQB_F16 && y_dtype != HQB_F32)) return HQB_ERR_INVALID;
   if (bias != nullptr && bias_dtype != HQB_F16 && bias_dtype != HQB_F32) return HQB_ERR_INVALID;
   if ((depth == nullptr) != (depth_plan == nullptr)) return HQB_ERR_INVALID;
+  if ((flags & HQB_FLAG_STREAMK) && (flags & HQB_FLAG_ROWBLOCK)) return HQB_ERR_INVALID;
   const bool mixed = depth != nullptr;
   if (!mixed && prefix > m->stage_count) return HQB_ERR_INVALID;
   const bool simt = (flags & HQB_FLAG_SIMT) != 0;
@@ -2208,18 +2574,26 @@ int gemv_impl(const hqb_plane_matrix* m, uint32_t prefix, const uint8_t* depth, 
     return cudaGetLastError();
   }
   const uint8_t* xfrag = static_cast<const uint8_t*>(x);
-  // The uniform streaming kernel prepares raw activations itself when they fit beside
-  // the fragments in shared memory (no separate preparation launch).
   const uint32_t xslot = xslot_bytes_for(batch, xl);
+  // Row-block kernel (uniform prefix, batch <= 8, every warp's activation fragments in its
+  // shared memory; it always prepares raw activations itself): the default while a
+  // stream-K CTA would hold at most kRowsUnitsMax (tile, stage) units, where the stream-K
+  // kernel's fixed cost (activation staging, cross-CTA split-row sums) dominates.
+  const uint32_t rows_xw = mixed ? 0u : rows_xw_bytes(m->grid_cols, prefix, xslot);
+  const bool rows_small = static_cast<uint64_t>(m->grid_rows) * m->grid_cols * prefix <=
+                          static_cast<uint64_t>(kRowsUnitsMax) * 2 * sms;
+  const bool rows_path = !mixed && !simt && batch <= 8 && !(flags & (HQB_FLAG_RING | HQB_FLAG_STREAMK)) &&
+                         (rows_small || (flags & HQB_FLAG_ROWBLOCK)) &&
+                         static_cast<uint64_t>(m->grid_rows) * m->grid_cols * kRecordBytes < (1ull << 32) &&
+                         kRowsHeadBytes + static_cast<uint64_t>(kRowsWarps) * rows_xw <= kRowsSmemMax;
   const uint64_t x_all_bytes = static_cast<uint64_t>(m->grid_cols) * xslot;
-  const bool streaming_path = !simt && x_all_bytes <= kXResidentMax && !(flags & HQB_FLAG_RING);
-  const uint64_t raw_offset = round_up(x_all_bytes, 16);
-  const uint64_t raw_bytes = static_cast<uint64_t>(m->grid_cols) * 128 * batch * (xl == 1 ? 2 : 4);
-  // Each CTA builds the fragments of the columns its tiles touch; when CTAs hold more
-  // than kFusedTilesMax tiles on average, one preparation launch shared by all is cheaper.
+  // stream-K kernels: all fragments resident in shared memory (else the ring kernel)
+  const bool streaming = !rows_path && !simt && x_all_bytes <= kXResidentMax && !(flags & HQB_FLAG_RING);
+  // The uniform stream-K kernel builds the fragments of the columns its tiles touch; when
+  // CTAs hold more than kFusedTilesMax tiles on average, one preparation launch shared by
+  // all is cheaper.
   const uint64_t avg_tiles = static_cast<uint64_t>(m->grid_rows) * m->grid_cols / (static_cast<uint64_t>(sms) * 2);
-  const bool fuse_prep = !x_prepared && !mixed && streaming_path && raw_offset + raw_bytes <= kFusedXMax &&
-                         avg_tiles <= kFusedTilesMax;
+  const bool fuse_prep = !x_prepared && (rows_path || (streaming && !mixed && avg_tiles <= kFusedTilesMax));
   if (!x_prepared && !fuse_prep) {
     e = launch_prep(x, x_dtype, m->cols, batch, ws + L.xfrag, st);
     if (e != cudaSuccess) {
@@ -2244,12 +2618,15 @@ int gemv_impl(const hqb_plane_matrix* m, uint32_t prefix, const uint8_t* depth, 
   p.prefix = mixed ? 0 : prefix;
   p.stage_count = m->stage_count;
   p.batch = batch;
-  p.xslot_bytes = xslot_bytes_for(batch, xl);
+  p.xslot_bytes = xslot;
   p.bias_dtype = bias_dtype;
   p.y_dtype = y_dtype;
   p.cols = static_cast<uint32_t>(m->cols);
+  p.shift_mul = 1u << 24;
+  p.pdl = (flags & HQB_FLAG_PDL) ? 1u : 0u;
   if (gather != nullptr) {
-    if (!streaming_path) return HQB_ERR_UNSUPPORTED;  // only the uniform streaming kernel gathers
+    // only the row-block and uniform stream-K kernels gather
+    if (!rows_path && !streaming) return HQB_ERR_UNSUPPORTED;
     p.g_world = gather->world;
     p.g_rank = gather->rank;
     p.g_slot_rows = gather->slot_rows;
@@ -2261,33 +2638,36 @@ int gemv_impl(const hqb_plane_matrix* m, uint32_t prefix, const uint8_t* depth, 
   }
   if (fuse_prep) {
     p.x_raw = x;
-    p.raw_offset = static_cast<uint32_t>(raw_offset);
-    p.x_vec = ((reinterpret_cast<uintptr_t>(x) & 15u) == 0 && (m->cols * (xl == 1 ? 2 : 4)) % 16 == 0) ? 1u : 0u;
+    p.x_vec = x_rows_vec(x, m->cols, xl) ? 1u : 0u;
   }
   const uint64_t tiles = static_cast<uint64_t>(m->grid_rows) * m->grid_cols;
   p.total = mixed ? 0 : tiles * prefix;
-  const bool streaming = !simt && static_cast<uint64_t>(m->grid_cols) * p.xslot_bytes <= kXResidentMax &&
-                         !(flags & HQB_FLAG_RING);
-  const GemvKernel k = !streaming ? pick_kernel(batch > 8 ? 2 : 1, xl, simt)
-                       : mixed    ? pick_stream_kernel(batch > 8 ? 2 : 1, xl)
-                                  : pick_uniform_kernel(batch > 8 ? 2 : 1, xl, prefix, batch);
-  const uint64_t x_all = static_cast<uint64_t>(m->grid_cols) * p.xslot_bytes;
-  p.x_resident = x_all <= kXResidentMax ? 1u : 0u;
-  p.slot_x_bytes = p.x_resident ? 0u : p.xslot_bytes;
-  const RingShape rs = ring_shape(p.slot_x_bytes, mixed ? m->stage_count : prefix,
-                                  p.x_resident ? static_cast<uint32_t>(x_all) : 0u);
-  p.ring_slots = rs.slots;
-  p.slot_stride = rs.stride;
-  p.shift_mul = 1u << 24;
-  p.pdl = (flags & HQB_FLAG_PDL) ? 1u : 0u;
-  const uint32_t smem = !streaming ? rs.smem
-                       : fuse_prep ? static_cast<uint32_t>(raw_offset + raw_bytes)
-                                   : static_cast<uint32_t>(x_all) + 256;
-  const uint32_t threads = streaming ? kStreamThreads : kGemvThreads;
+  GemvKernel k = nullptr;
+  uint32_t smem = 0, threads = 0;
+  uint64_t work = p.total;  // upper bound on useful CTAs
+  if (rows_path) {
+    p.xw_bytes = rows_xw;
+    k = pick_rows_kernel(xl, prefix, batch);
+    smem = kRowsHeadBytes + kRowsWarps * rows_xw;
+    threads = kRowsThreads;
+    work = static_cast<uint64_t>(m->grid_rows) * 8;  // row-block items
+  } else {
+    k = !streaming ? pick_kernel(batch > 8 ? 2 : 1, xl, simt)
+        : mixed    ? pick_stream_kernel(batch > 8 ? 2 : 1, xl)
+                   : pick_uniform_kernel(batch > 8 ? 2 : 1, xl, prefix, batch);
+    p.x_resident = x_all_bytes <= kXResidentMax ? 1u : 0u;
+    p.slot_x_bytes = p.x_resident ? 0u : xslot;
+    const RingShape rs = ring_shape(p.slot_x_bytes, mixed ? m->stage_count : prefix,
+                                    p.x_resident ? static_cast<uint32_t>(x_all_bytes) : 0u);
+    p.ring_slots = rs.slots;
+    p.slot_stride = rs.stride;
+    smem = !streaming ? rs.smem : static_cast<uint32_t>(x_all_bytes) + 256;
+    threads = streaming ? kStreamThreads : kGemvThreads;
+  }
   const int per_sm = ctas_per_sm(k, smem, device, threads);
   if (per_sm <= 0) return cudaErrorLaunchOutOfResources;
   uint64_t grid = static_cast<uint64_t>(sms) * per_sm;
-  if (!mixed) grid = std::max<uint64_t>(1, std::min<uint64_t>(grid, p.total));
+  if (!mixed) grid = std::max<uint64_t>(1, std::min<uint64_t>(grid, work));
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(static_cast<unsigned>(grid));
   cfg.blockDim = dim3(threads);
@@ -2305,10 +2685,10 @@ int gemv_impl(const hqb_plane_matrix* m, uint32_t prefix, const uint8_t* depth, 
     cudaGetLastError();  // do not leave a refused launch pending for the next call
     return e;
   }
-  // Split tile rows exist whenever more than one CTA shares the work; the uniform
-  // streaming kernel finishes them itself.
-  const bool uniform_streaming = streaming && !mixed;
-  if (!uniform_streaming && (mixed || std::min<uint64_t>(grid, p.total) > 1)) {
+  // Split tile rows exist whenever more than one CTA shares the work; the row-block and
+  // uniform stream-K kernels finish them (or have none) themselves.
+  const bool self_finishing = rows_path || (streaming && !mixed);
+  if (!self_finishing && (mixed || std::min<uint64_t>(grid, p.total) > 1)) {
     cudaLaunchConfig_t fc{};
     fc.gridDim = dim3(m->grid_rows);
     fc.blockDim = dim3(256);

@@ -8,10 +8,11 @@
 // the same kernels as hqb_gemv.
 //
 // Scratch contents (the layout hqb_gemv uses for a caller workspace):
-//   error word (HQB_DEVERR_* bits that kernels OR in) and split-row arrival counters:
-//       must start at zero.  The counters return to zero at the end of every call.
-//   split-row partial sums and prepared activations: each call writes them before it
-//       reads them, so they need no initial value.
+//   error word (HQB_DEVERR_* bits that kernels OR in), split-row arrival counters and
+//       split-row partial sums: must start at zero.  Counters and partial sums return
+//       to zero at the end of every call.
+//   prepared activations: each call writes them before it reads them, so they need no
+//       initial value.
 //
 // Set-up: the first call on a device, with that device current, resolves the array's
 // address on that device with cudaGetSymbolAddress and enqueues a clear of the whole

@@ -22,7 +22,23 @@ PKG = Path(__file__).resolve().parent
 LIB_PATH = PKG / "lib" / "libharpq_b200.so"
 
 F32, F16 = 0, 1
-FLAG_PDL, FLAG_SIMT, FLAG_RING, FLAG_TCGEN05 = 1, 2, 4, 8
+FLAG_PDL, FLAG_SIMT, FLAG_RING, FLAG_TCGEN05, FLAG_STREAMK, FLAG_ROWBLOCK = 1, 2, 4, 8, 16, 32
+# row-block kernel geometry (mirrors hqb_plane.cu): warps per CTA, shared-memory head
+# (reduction slots), shared-memory limit, and the size rule: the row-block kernel runs by
+# default while a stream-K CTA would hold at most ROWS_UNITS_MAX (tile, stage) units
+ROWS_WARPS, ROWS_HEAD_BYTES, ROWS_SMEM_MAX, ROWS_UNITS_MAX = 16, 2 * 16 * 16 * 8 * 4 + 256, 200 * 1024, 16
+
+
+def rows_xw_bytes(grid_cols: int, depth: int, xslot: int) -> int:
+    """Fragment bytes of one warp's area in the row-block kernel: the most tile columns
+    any warp's contiguous range of the C*depth (tile, stage) units touches."""
+    units = grid_cols * depth
+    nt = 0
+    for w in range(ROWS_WARPS):
+        ua, ub = w * units // ROWS_WARPS, (w + 1) * units // ROWS_WARPS
+        if ua < ub:
+            nt = max(nt, (ub - 1) // depth - ua // depth + 1)
+    return nt * xslot
 TILE = 128
 RECORD_BYTES = 4352
 MAX_STAGES = 4
@@ -308,9 +324,11 @@ class PlaneMatrix:
 
     def gemv_launches(self, batch: int, x_dtype: int, prefix: int, mixed: bool = False, flags: int = 0,
                       x_prepared: bool = False) -> int:
-        """Kernels one gemv() call launches, by the library's dispatch rule: activation
-        preparation unless x is prepared; the GEMV; and, unless the uniform streaming
-        kernel runs (it reduces split tile rows itself), the split-row fix-up."""
+        """Kernels one gemv() call launches, by the library's dispatch rule: the row-block
+        kernel alone (uniform prefix, batch <= 8: it prepares raw activations itself and
+        has no split tile rows); otherwise activation preparation unless x is prepared or
+        the uniform stream-K kernel prepares it, the GEMV and, unless that kernel runs
+        (it reduces split tile rows itself), the split-row fix-up."""
         if not mixed and prefix == 0:
             return 1  # bias / zero fill only
         if (flags & FLAG_TCGEN05) and not mixed and not x_prepared and x_dtype == F16 and batch <= 8 \
@@ -318,14 +336,15 @@ class PlaneMatrix:
             return 2  # activation blocks, then the tcgen05 kernel
         xl = 2 if x_dtype == F32 else 1
         xslot = -(-(batch * (256 * xl + 8)) // 16) * 16
-        streaming = not (flags & FLAG_SIMT) and self.grid_cols * xslot <= 64 * 1024 and not (flags & FLAG_RING)
-        # the uniform streaming kernel prepares raw activations itself when fragments and
-        # staged raw rows fit its shared memory
-        raw_offset = -(-(self.grid_cols * xslot) // 16) * 16
-        raw_bytes = self.grid_cols * 128 * batch * (2 if xl == 1 else 4)
         sms = torch.cuda.get_device_properties(self.device).multi_processor_count
+        small = self.grid_rows * self.grid_cols * prefix <= ROWS_UNITS_MAX * 2 * sms
+        if not mixed and not (flags & (FLAG_SIMT | FLAG_RING | FLAG_STREAMK)) and batch <= 8 \
+                and (small or (flags & FLAG_ROWBLOCK)) \
+                and ROWS_HEAD_BYTES + ROWS_WARPS * rows_xw_bytes(self.grid_cols, prefix, xslot) <= ROWS_SMEM_MAX:
+            return 1
+        streaming = not (flags & FLAG_SIMT) and self.grid_cols * xslot <= 64 * 1024 and not (flags & FLAG_RING)
         avg_tiles = self.grid_rows * self.grid_cols // (sms * 2)
-        fused = streaming and not mixed and raw_offset + raw_bytes <= 96 * 1024 and avg_tiles <= 24
+        fused = streaming and not mixed and avg_tiles <= 24
         n = 0 if (x_prepared or fused) else 1
         n += 1
         if not (streaming and not mixed):

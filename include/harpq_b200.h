@@ -48,6 +48,14 @@ extern "C" {
 #define HQB_FLAG_TCGEN05 8u /* tcgen05 (UMMA, TMEM accumulators) kernel: FP16 x, batch <= 8,
                                  uniform prefix; a comparison path, slower than the default
                                  mma.sync kernels at these shapes */
+/* Uniform prefix at batch <= 8 runs one of two kernels, chosen by size: the row-block
+ * kernel (no tile row split between CTAs; lowest fixed cost, for small layers) or the
+ * stream-K kernel (tile rows split between CTAs, their sums finished through the
+ * workspace; best streaming rate, for large layers).  These flags force one of them
+ * (both set: HQB_ERR_INVALID; the row-block flag is ignored where its activation
+ * fragments would not fit shared memory). */
+#define HQB_FLAG_STREAMK 16u
+#define HQB_FLAG_ROWBLOCK 32u
 
 /* Fast-path tiling: 128x128 tiles, one scale group per tile row (group 128). */
 #define HQB_TILE 128
@@ -145,9 +153,9 @@ HQB_API int hqb_prepare_x(const void* x, int x_dtype, uint64_t cols, uint32_t ba
  * GPU must not share a workspace. */
 HQB_API uint64_t hqb_workspace_bytes(const hqb_plane_matrix* m, uint32_t batch, int x_dtype,
                                      int device);
-/* Clears a workspace: its error word and its split-row counters must start at zero.
- * Call once after allocation and after a reported device error; the counters return
- * to zero at the end of every GEMV. */
+/* Clears a workspace: its error word, split-row counters and split-row partial sums
+ * must start at zero.  Call once after allocation and after a reported device error;
+ * counters and partial sums return to zero at the end of every GEMV. */
 HQB_API int hqb_workspace_init(void* workspace, uint64_t bytes, void* stream);
 /* Copies the workspace error word (HQB_DEVERR_* bits) to *host_flags, synchronously. */
 HQB_API int hqb_workspace_error(const void* workspace, int* host_flags, void* stream);
@@ -215,8 +223,9 @@ HQB_API int hqb_gemv_ex(const hqb_plane_matrix* m, uint32_t prefix, const uint8_
  * - The first call on a device sets up: it resolves the array's address on that device
  *   (cudaGetSymbolAddress) and enqueues a clear of the whole array on `stream`.  Make
  *   that first call before any stream capture.
- * - What must start at zero: the error word and the split-row counters (they return to
- *   zero at the end of every call).  The rest is written before it is read.
+ * - What must start at zero: the error word, the split-row counters and partial sums
+ *   (they return to zero at the end of every call).  The rest is written before it is
+ *   read.
  * - One scratch per device: calls whose GPU work overlaps (other streams, other host
  *   threads) race on it.  Order them on one stream or with events.
  * - Device error bits land in the scratch's error word, which is not exposed; the

@@ -108,17 +108,91 @@ def test_prefix_zero_writes_bias_or_zeros():
     assert torch.equal(y, bias.expand(3, -1))
 
 
-def test_split_rows_deterministic():
-    """Many split tile rows (stream-K fix-up kernel) give identical bytes run to run."""
+@pytest.mark.parametrize("streamk", [False, True])
+def test_split_rows_deterministic(streamk):
+    """Split tile rows (stream-K kernel) and warp-split row blocks (row-block kernel) give
+    identical bytes run to run."""
+    import harpq_b200 as hqb
+
     rng = np.random.default_rng(11)
     m = random_matrix(rng, 1000, 3000)
     pm = plane_matrix(m)
     x = torch.from_numpy(rng.standard_normal((4, m.cols)).astype(np.float16)).cuda()
     ws = pm.workspace(4)
-    outs = [pm.gemv(x, prefix=p, y_dtype=torch.float32, workspace=ws).cpu().numpy() for p in (1, 3, 4, 3)]
+    fl = hqb.FLAG_STREAMK if streamk else hqb.FLAG_ROWBLOCK
+    outs = [pm.gemv(x, prefix=p, y_dtype=torch.float32, workspace=ws, flags=fl).cpu().numpy() for p in (1, 3, 4, 3)]
     assert outs[1].tobytes() == outs[3].tobytes()
     e64 = _fp64_reference(m, x.float().cpu().numpy(), 4)
     assert_close(outs[2], e64, 2e-4, 2e-4, "split rows p4")
+    assert ws.error_flags() == 0
+
+
+@pytest.mark.parametrize("rows,cols", [(16, 300), (1000, 3000), (1024, 4096), (200, 11008), (7168, 256)])
+def test_row_block_kernel_matches_stream_k(rows, cols):
+    """The row-block kernel (no tile row split between CTAs; the warps' parts of a row
+    block summed in shared memory in warp order) against the FP64 reference and the
+    stream-K kernel at every depth, batch 1/3/8, FP16 and FP32 activations, with bias.
+    The shapes cover fewer (tile, stage) units than warps (16x300 at depth 1), a single
+    CTA wave, 86 tile columns, and CTAs that take several row blocks in turn (7168x256).
+    Repeated calls are bit-identical and leave no device error."""
+    import harpq_b200 as hqb
+
+    rng = np.random.default_rng(rows * 3 + cols)
+    m = random_matrix(rng, rows, cols)
+    pm = plane_matrix(m)
+    ws = pm.workspace(8, hqb.F32)  # large enough for FP16 activations too
+    bias = rng.standard_normal(rows).astype(np.float32)
+    bt = torch.from_numpy(bias).cuda()
+    w64 = {p: orc.dequantize_prefix_np(m, p).astype(np.float64) for p in (1, 2, 3, 4)}
+    for batch in (1, 3, 8):
+        x = rng.standard_normal((batch, cols)).astype(np.float16).astype(np.float32)
+        for xdt in (torch.float16, torch.float32):
+            xt = torch.from_numpy(x).cuda().to(xdt)
+            for p in (1, 2, 3, 4):
+                rb = hqb.FLAG_ROWBLOCK
+                a = pm.gemv(xt, prefix=p, bias=bt, y_dtype=torch.float32, workspace=ws, flags=rb)
+                a2 = pm.gemv(xt, prefix=p, bias=bt, y_dtype=torch.float32, workspace=ws, flags=rb | hqb.FLAG_PDL)
+                b = pm.gemv(xt, prefix=p, bias=bt, y_dtype=torch.float32, workspace=ws, flags=hqb.FLAG_STREAMK)
+                torch.cuda.synchronize()
+                assert torch.equal(a, a2), (batch, xdt, p)
+                e64 = x.astype(np.float64) @ w64[p].T + bias[None, :]
+                an = a.cpu().numpy()
+                assert_close(an, e64, 2e-4, 2e-4, f"row-block b{batch} {xdt} p{p}")
+                assert rel_l2(an, e64) <= 1e-3
+                assert_close(an, b.cpu().numpy(), 2e-4, 2e-4, f"row-block vs stream-K b{batch} {xdt} p{p}")
+    assert ws.error_flags() == 0
+
+
+def test_workspace_shared_across_kernels():
+    """One workspace through every kernel in turn: the stream-K kernel's flagged split-row
+    words, the fix-up kernel's and the tcgen05 kernel's partial sums all leave the
+    partials region zero, so each later call is right and the stream-K results repeat
+    bit for bit."""
+    import harpq_b200 as hqb
+
+    rng = np.random.default_rng(31)
+    m = random_matrix(rng, 1000, 3000)
+    pm = plane_matrix(m)
+    depth = torch.from_numpy(rng.integers(1, 5, size=(pm.grid_rows, pm.grid_cols)).astype(np.uint8)).cuda()
+    plan = hqb.DepthPlan(depth, 4)
+    ws = pm.workspace(4)
+    w64 = {p: orc.dequantize_prefix_np(m, p).astype(np.float64) for p in (2, 3)}
+    for batch in (1, 4):
+        x = rng.standard_normal((batch, m.cols)).astype(np.float16).astype(np.float32)
+        xt = torch.from_numpy(x).cuda().half()
+        ref = {p: x.astype(np.float64) @ w64[p].T for p in (2, 3)}
+        sk = []
+        for fl, p in ((hqb.FLAG_STREAMK, 3), (hqb.FLAG_RING, 3), (hqb.FLAG_STREAMK, 3), (hqb.FLAG_TCGEN05, 2),
+                      (hqb.FLAG_STREAMK, 3), (None, None), (hqb.FLAG_STREAMK, 3), (hqb.FLAG_ROWBLOCK, 2),
+                      (hqb.FLAG_STREAMK, 3)):
+            if fl is None:  # per-tile depth: the depth-map kernel and the fix-up kernel
+                pm.gemv(xt, depth=plan, y_dtype=torch.float32, workspace=ws)
+                continue
+            y = pm.gemv(xt, prefix=p, y_dtype=torch.float32, workspace=ws, flags=fl).cpu().numpy()
+            assert_close(y, ref[p], 2e-4, 2e-4, f"b{batch} flags {fl}")
+            if fl == hqb.FLAG_STREAMK:
+                sk.append(y)
+        assert all(a.tobytes() == sk[0].tobytes() for a in sk)
     assert ws.error_flags() == 0
 
 
@@ -250,6 +324,9 @@ def test_invalid_arguments_rejected_without_launch():
         pm.gemv(torch.randn(17, 128, device="cuda").half(), prefix=1)
     with pytest.raises(hqb.HQBError):
         pm.gemv(x, prefix=1, flags=hqb.FLAG_SIMT, y_dtype=torch.float32, workspace=hqb.Workspace(256))
+    with pytest.raises(hqb.HQBError) as e:
+        pm.gemv(x, prefix=1, flags=hqb.FLAG_STREAMK | hqb.FLAG_ROWBLOCK)
+    assert e.value.status == 1
 
 
 @pytest.mark.parametrize("rows,cols", [(128, 128), (256, 1024), (1024, 512), (2048, 2048), (4096, 4096),
