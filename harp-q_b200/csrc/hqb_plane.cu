@@ -1007,6 +1007,17 @@ __device__ __forceinline__ void load_xfrag(XFrag<NB, XL>& xf, const XLane<NB, XL
   }
 }
 
+// One lane's part of one row block of a plane record: its 16-byte code slot and its
+// 4-byte scale pair, read once (no L1 allocation) and marked evict-first in L2, so the
+// streamed planes do not push activations and other reused data out of L2.
+__device__ __forceinline__ void ld_plane(uint4& w, uint32_t& sc, const uint8_t* codes, const uint8_t* scales,
+                                         uint64_t policy) {
+  asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.v4.u32 {%0,%1,%2,%3}, [%4], %5;"
+               : "=r"(w.x), "=r"(w.y), "=r"(w.z), "=r"(w.w)
+               : "l"(codes), "l"(policy));
+  asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.u32 %0, [%1], %2;" : "=r"(sc) : "l"(scales), "l"(policy));
+}
+
 // Accumulator chains per tile: one per stage; depth 1 alternates two chains.
 template <int D>
 struct TileChains {
@@ -1120,64 +1131,91 @@ __device__ __forceinline__ void publish_flagged(const GemvParams& p, uint32_t ct
     }
 }
 
-// The published word at `a`, waiting (bounded; after one timeout a warp no longer waits).
-__device__ __forceinline__ float take_flagged(unsigned long long* a, unsigned long long v, const GemvParams& p,
-                                              bool& gave_up) {
-  if ((v >> 32) != kPartFlag && !gave_up) {
-    const unsigned long long t0 = global_timer_ns();
+// Row r ends in this CTA (the last contributor): add the earlier contributors' parts in
+// CTA order, then this warp's own part, plus bias, and store its rows.  The lane's
+// elements (batch columns 2q + j, rows rit0 and rit0 + 8; with B1 only column 0) are
+// gathered together: all loads of a group of contributors are issued at once, and the
+// words not yet published are read again together (bounded), so waiting costs one
+// round trip to L2 per round, not one per word.  Consumed words are cleared to zero.
+template <int NB, bool B1>
+__device__ __forceinline__ void reduce_split_row(const GemvParams& p, uint32_t r, uint64_t units_per_row,
+                                                 uint64_t total, uint32_t ctas, uint32_t cta,
+                                                 const float (&own)[NB][4], uint32_t rit0, uint32_t q) {
+  constexpr int J = B1 ? 1 : 2;                  // batch columns per lane and accumulator block
+  constexpr int E = NB * J * 2;                  // elements per lane
+  constexpr uint32_t K = E <= 2 ? 8 : (E <= 4 ? 4 : 2);  // contributors per group (16 words)
+  const uint32_t first = unit_owner(static_cast<uint64_t>(r) * units_per_row, total, ctas);
+  unsigned long long* part = reinterpret_cast<unsigned long long*>(p.partials);
+  uint64_t off[E];
+  bool ok[E];
+  float sum[E];
+#pragma unroll
+  for (int nb = 0; nb < NB; ++nb)
+#pragma unroll
+    for (int j = 0; j < J; ++j)
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int e = (nb * J + j) * 2 + h;
+        const uint32_t b = 2 * q + j + 8 * nb;
+        ok[e] = b < p.batch && (!B1 || q == 0);
+        off[e] = static_cast<uint64_t>(ok[e] ? b : 0u) * 128 + rit0 + 8 * h;
+        sum[e] = 0.0f;
+      }
+  bool gave_up = false;
+  const uint64_t cta_words = static_cast<uint64_t>(p.batch) * 128;
+  for (uint32_t i0 = first; i0 < cta; i0 += K) {
+    unsigned long long v[K][E];
+    const unsigned long long ready = static_cast<unsigned long long>(kPartFlag) << 32;
+#pragma unroll
+    for (uint32_t k = 0; k < K; ++k)
+#pragma unroll
+      for (int e = 0; e < E; ++e)
+        v[k][e] = (i0 + k < cta && ok[e]) ? ld_relaxed_gpu_u64(part + (i0 + k) * cta_words + off[e]) : ready;
+    unsigned long long t0 = 0;
     for (;;) {
-      v = ld_relaxed_gpu_u64(a);
-      if ((v >> 32) == kPartFlag) break;
-      if (global_timer_ns() - t0 > kWaitLimitNs) {
+      bool all = true;
+#pragma unroll
+      for (uint32_t k = 0; k < K; ++k)
+#pragma unroll
+        for (int e = 0; e < E; ++e) all = all && (v[k][e] >> 32) == kPartFlag;
+      if (all || gave_up) break;
+      if (t0 == 0) {
+        t0 = global_timer_ns();
+      } else if (global_timer_ns() - t0 > kWaitLimitNs) {
         atomicOr(p.error, HQB_DEVERR_TIMEOUT);
         gave_up = true;
         break;
       }
-      __nanosleep(64);
+#pragma unroll
+      for (uint32_t k = 0; k < K; ++k)
+#pragma unroll
+        for (int e = 0; e < E; ++e)
+          if ((v[k][e] >> 32) != kPartFlag) v[k][e] = ld_relaxed_gpu_u64(part + (i0 + k) * cta_words + off[e]);
     }
+#pragma unroll
+    for (uint32_t k = 0; k < K; ++k)
+#pragma unroll
+      for (int e = 0; e < E; ++e)
+        if (i0 + k < cta && ok[e]) {
+          sum[e] += __uint_as_float(static_cast<uint32_t>(v[k][e]));
+          st_relaxed_gpu_u64(part + (i0 + k) * cta_words + off[e], 0ull);
+        }
   }
-  st_relaxed_gpu_u64(a, 0ull);
-  return __uint_as_float(static_cast<uint32_t>(v));
-}
-
-// Row r ends in this CTA (the last contributor): add the earlier contributors' parts in
-// CTA order, then this warp's own part, plus bias, and store its rows.
-template <int NB>
-__device__ __forceinline__ void reduce_split_row(const GemvParams& p, uint32_t r, uint64_t units_per_row,
-                                                 uint64_t total, uint32_t ctas, uint32_t cta,
-                                                 const float (&own)[NB][4], uint32_t rit0, uint32_t q) {
-  const uint32_t first = unit_owner(static_cast<uint64_t>(r) * units_per_row, total, ctas);
-  unsigned long long* part = reinterpret_cast<unsigned long long*>(p.partials);
-  bool gave_up = false;
 #pragma unroll
   for (int nb = 0; nb < NB; ++nb)
 #pragma unroll
-    for (int j = 0; j < 2; ++j) {
-      const uint32_t b = 2 * q + j + 8 * nb;
-      if (b >= p.batch) continue;
+    for (int j = 0; j < J; ++j)
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
-        const uint32_t rit = rit0 + 8 * h, row = r * 128 + rit;
-        float sum = 0.0f;
-        for (uint32_t i0 = first; i0 < cta; i0 += 8) {  // 8 independent loads, summed in order
-          unsigned long long v[8];
-#pragma unroll
-          for (uint32_t k = 0; k < 8; ++k)
-            v[k] = i0 + k < cta ? ld_relaxed_gpu_u64(part + (static_cast<uint64_t>(i0 + k) * p.batch + b) * 128 + rit)
-                                : 0ull;
-#pragma unroll
-          for (uint32_t k = 0; k < 8; ++k)
-            if (i0 + k < cta)
-              sum += take_flagged(part + (static_cast<uint64_t>(i0 + k) * p.batch + b) * 128 + rit, v[k], p, gave_up);
-        }
-        sum += own[nb][2 * h + j];
-        if (row >= p.rows) continue;
+        const int e = (nb * J + j) * 2 + h;
+        const uint32_t b = 2 * q + j + 8 * nb, row = r * 128 + rit0 + 8 * h;
+        if (!ok[e] || row >= p.rows) continue;
+        float y = sum[e] + own[nb][2 * h + j];
         if (p.bias != nullptr)
-          sum += p.bias_dtype == HQB_F16 ? __half2float(static_cast<const __half*>(p.bias)[row])
-                                         : static_cast<const float*>(p.bias)[row];
-        put_y(p, b, row, sum);
+          y += p.bias_dtype == HQB_F16 ? __half2float(static_cast<const __half*>(p.bias)[row])
+                                       : static_cast<const float*>(p.bias)[row];
+        put_y(p, b, row, y);
       }
-    }
 }
 
 // After the CTA's last tile: one barrier, then one arrival per split row on a per-row
@@ -1282,7 +1320,7 @@ __device__ __forceinline__ ColRanges needed_columns(uint32_t t0, uint32_t t_end,
 // Activation fragments of the needed tile columns, built from raw x (FP16 for XL 1,
 // FP32 for XL 2) by the CTA itself through prep_items, so they are bit-identical to a
 // separately prepared buffer.  Each warp reads its items' activations straight from
-// global memory; two items per warp at a time, so their shuffle chains interleave.
+// global memory, two items at a time, so their shuffle chains interleave.
 template <int XL>
 __device__ __forceinline__ void build_xfrag_tiles(const GemvParams& p, uint8_t* xres, const ColRanges& cr) {
   using XT = typename std::conditional<XL == 1, __half, float>::type;
@@ -1329,8 +1367,11 @@ __global__ void __launch_bounds__(kStreamThreads, (NB == 1 && XL == 1) ? 2 : 1)
   const uint32_t t_end = static_cast<uint32_t>((u1 - 1) / D), s_end = static_cast<uint32_t>((u1 - 1) % D) + 1;
   const uint32_t ntiles = t_end - t0 + 1;
   const uint32_t mask_first = kFull & ~((1u << s0) - 1u), mask_last = (1u << s_end) - 1u;
+  // The CTA walks its tiles in descending order: its last tile row, which goes on in the
+  // next CTA, comes first and its part is published early; its first row, which it sums
+  // when that row began in an earlier CTA, comes last.
   // Per-stage code and scale pointers of this lane, at the first tile of the group of R
-  // tiles that the next refills load; slot j of a group is at +j*4352 bytes.
+  // tiles that the next refills load; slot j of a group is at -j*4352 bytes.
   // Deep prefixes derive the scale address from the code address (fewer registers).
   constexpr bool kScalePtr = D <= 2;
   constexpr int SB = kScalePtr ? D : 1;
@@ -1340,24 +1381,22 @@ __global__ void __launch_bounds__(kStreamThreads, (NB == 1 && XL == 1) ? 2 : 1)
   const uint32_t scale_rel = scale_off - lane_off;
 #pragma unroll
   for (int s = 0; s < D; ++s) {
-    cb[s] = p.planes[s] + static_cast<uint64_t>(t0) * kRecordBytes + lane_off;
-    if (kScalePtr) sb[s < SB ? s : 0] = p.planes[s] + static_cast<uint64_t>(t0) * kRecordBytes + scale_off;
+    cb[s] = p.planes[s] + static_cast<uint64_t>(t_end) * kRecordBytes + lane_off;
+    if (kScalePtr) sb[s < SB ? s : 0] = p.planes[s] + static_cast<uint64_t>(t_end) * kRecordBytes + scale_off;
   }
 
   // Register ring of R tiles x D stages.  A stage outside the CTA's units gets scale 0
   // (codes 0): its products are finite and its contribution is exactly zero.
   uint4 w[R][D];
   uint32_t sc[R][D];
+  const uint64_t l2_first = policy_evict_first();
   auto load_tile = [&](int slot, uint32_t mask) {
 #pragma unroll
     for (int s = 0; s < D; ++s) {
       if (D == 1 || (mask & (1u << s))) {
-        const uint8_t* a = cb[s] + slot * kRecordBytes;
-        const uint8_t* as = kScalePtr ? sb[s < SB ? s : 0] + slot * kRecordBytes : a + scale_rel;
-        asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
-                     : "=r"(w[slot][s].x), "=r"(w[slot][s].y), "=r"(w[slot][s].z), "=r"(w[slot][s].w)
-                     : "l"(a));
-        asm volatile("ld.global.nc.L1::no_allocate.u32 %0, [%1];" : "=r"(sc[slot][s]) : "l"(as));
+        const uint8_t* a = cb[s] - slot * kRecordBytes;
+        const uint8_t* as = kScalePtr ? sb[s < SB ? s : 0] - slot * kRecordBytes : a + scale_rel;
+        ld_plane(w[slot][s], sc[slot][s], a, as, l2_first);
       } else {
         w[slot][s] = make_uint4(0u, 0u, 0u, 0u);
         sc[slot][s] = 0u;
@@ -1367,14 +1406,14 @@ __global__ void __launch_bounds__(kStreamThreads, (NB == 1 && XL == 1) ? 2 : 1)
   auto next_group = [&]() {
 #pragma unroll
     for (int s = 0; s < D; ++s) {
-      cb[s] += R * kRecordBytes;
-      if (kScalePtr) sb[s < SB ? s : 0] += R * kRecordBytes;
+      cb[s] -= R * kRecordBytes;
+      if (kScalePtr) sb[s < SB ? s : 0] -= R * kRecordBytes;
     }
   };
 #pragma unroll
   for (int j = 0; j < R; ++j) {
     if (static_cast<uint32_t>(j) < ntiles)
-      load_tile(j, (j == 0 ? mask_first : kFull) & (static_cast<uint32_t>(j) == ntiles - 1 ? mask_last : kFull));
+      load_tile(j, (j == 0 ? mask_last : kFull) & (static_cast<uint32_t>(j) == ntiles - 1 ? mask_first : kFull));
   }
   next_group();
   griddep_wait();
@@ -1394,9 +1433,9 @@ __global__ void __launch_bounds__(kStreamThreads, (NB == 1 && XL == 1) ? 2 : 1)
   __syncthreads();
   const XLane<NB, XL> xlane(p.batch, lane);
   const uint64_t units_per_row = static_cast<uint64_t>(p.C) * D;
-  uint32_t row = t0 / p.C;
-  const uint8_t* xs = xres + (t0 % p.C) * p.xslot_bytes;  // activation slot of the current tile
-  uint32_t left = p.C - t0 % p.C;  // tiles of the current row still ahead (may run past ntiles)
+  uint32_t row = t_end / p.C;
+  const uint8_t* xs = xres + (t_end % p.C) * p.xslot_bytes;  // activation slot of the current tile
+  uint32_t left = t_end % p.C + 1;  // tiles of the current row still ahead (may run past ntiles)
   float y[NB][4];
 #pragma unroll
   for (int nb = 0; nb < NB; ++nb)
@@ -1404,14 +1443,13 @@ __global__ void __launch_bounds__(kStreamThreads, (NB == 1 && XL == 1) ? 2 : 1)
     for (int e = 0; e < 4; ++e) y[nb][e] = 0.0f;
 
   constexpr int CH = TileChains<D>::value;
-  // After tile k: the row may end (its last tile, or the CTA's last tile).  A row wholly
+  // After tile k: the row may end (its column 0, or the CTA's last tile).  A row wholly
   // inside the range is stored; one that goes on in later CTAs is published; the CTA's
   // first row, when it began in an earlier CTA and ends here, is kept and summed after
   // the last tile.
   float kept[NB][4];
   bool keep = false;
   auto advance = [&](uint32_t k) {
-    xs += p.xslot_bytes;
     if (--left == 0 || k + 1 == ntiles) {
       const uint64_t rb = static_cast<uint64_t>(row) * units_per_row, re = rb + units_per_row;
       if (rb >= u0 && re <= u1) {
@@ -1429,9 +1467,11 @@ __global__ void __launch_bounds__(kStreamThreads, (NB == 1 && XL == 1) ? 2 : 1)
       for (int nb = 0; nb < NB; ++nb)
 #pragma unroll
         for (int e = 0; e < 4; ++e) y[nb][e] = 0.0f;
-      ++row;
-      xs = xres;
+      --row;
+      xs = xres + (p.C - 1) * p.xslot_bytes;
       left = p.C;
+    } else {
+      xs -= p.xslot_bytes;
     }
   };
   auto one_tile = [&](int j) {
@@ -1449,7 +1489,7 @@ __global__ void __launch_bounds__(kStreamThreads, (NB == 1 && XL == 1) ? 2 : 1)
       const uint32_t k = k0 + j;
       one_tile(j);
       const uint32_t kn = k + R;  // refill slot j with tile kn (group base cb/sb)
-      if (kn < ntiles) load_tile(j, kn == ntiles - 1 ? mask_last : kFull);
+      if (kn < ntiles) load_tile(j, kn == ntiles - 1 ? mask_first : kFull);
       advance(k);
     }
     next_group();
@@ -1461,7 +1501,7 @@ __global__ void __launch_bounds__(kStreamThreads, (NB == 1 && XL == 1) ? 2 : 1)
     one_tile(j);
     advance(k);
   }
-  if (keep) reduce_split_row<NB>(p, t0 / p.C, units_per_row, total, ctas, cta, kept, rit0, q);
+  if (keep) reduce_split_row<NB, B1>(p, t0 / p.C, units_per_row, total, ctas, cta, kept, rit0, q);
   if (p.g_world > 1) gather_signal(p, ctas);
 }
 
@@ -1535,6 +1575,7 @@ __global__ void __launch_bounds__(kRowsThreads, 1) gemv_rows_kernel(const __grid
   // outside the warp's units gets scale 0 (codes 0): it contributes exactly zero.
   uint4 w[R][D];
   uint32_t sc[R][D];
+  const uint64_t l2_first = policy_evict_first();
   uint32_t lt = ta, lj = 0;  // next tile to load: column lt of the CTA's item lj
   uint32_t loff = item_off(cta);  // its code-slot offset
   auto load_next = [&](int slot) {
@@ -1543,10 +1584,7 @@ __global__ void __launch_bounds__(kRowsThreads, 1) gemv_rows_kernel(const __grid
 #pragma unroll
     for (int s = 0; s < D; ++s) {
       if (D == 1 || (mask & (1u << s))) {
-        asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
-                     : "=r"(w[slot][s].x), "=r"(w[slot][s].y), "=r"(w[slot][s].z), "=r"(w[slot][s].w)
-                     : "l"(p.planes[s] + loff));
-        asm volatile("ld.global.nc.L1::no_allocate.u32 %0, [%1];" : "=r"(sc[slot][s]) : "l"(p.planes[s] + soff));
+        ld_plane(w[slot][s], sc[slot][s], p.planes[s] + loff, p.planes[s] + soff, l2_first);
       } else {
         w[slot][s] = make_uint4(0u, 0u, 0u, 0u);
         sc[slot][s] = 0u;
@@ -2576,12 +2614,17 @@ int gemv_impl(const hqb_plane_matrix* m, uint32_t prefix, const uint8_t* depth, 
   const uint8_t* xfrag = static_cast<const uint8_t*>(x);
   const uint32_t xslot = xslot_bytes_for(batch, xl);
   // Row-block kernel (uniform prefix, batch <= 8, every warp's activation fragments in its
-  // shared memory; it always prepares raw activations itself): the default while a
-  // stream-K CTA would hold at most kRowsUnitsMax (tile, stage) units, where the stream-K
-  // kernel's fixed cost (activation staging, cross-CTA split-row sums) dominates.
+  // shared memory; it always prepares raw activations itself): the default for small
+  // layers, where the stream-K kernel's fixed cost (activation staging, cross-CTA
+  // split-row sums) dominates.  Rule, from B200 timings of both kernels: a stream-K CTA
+  // would hold u <= kRowsUnitsMax (tile, stage) units, and a row-block warp streams at
+  // most u + 2.5 units (its items per CTA times its share of a row block).
   const uint32_t rows_xw = mixed ? 0u : rows_xw_bytes(m->grid_cols, prefix, xslot);
-  const bool rows_small = static_cast<uint64_t>(m->grid_rows) * m->grid_cols * prefix <=
-                          static_cast<uint64_t>(kRowsUnitsMax) * 2 * sms;
+  const uint64_t all_units = static_cast<uint64_t>(m->grid_rows) * m->grid_cols * prefix;
+  const uint64_t warp_units = ((static_cast<uint64_t>(m->grid_rows) * 8 + sms - 1) / sms) *
+                              ((static_cast<uint64_t>(m->grid_cols) * prefix + kRowsWarps - 1) / kRowsWarps);
+  const bool rows_small = all_units <= static_cast<uint64_t>(kRowsUnitsMax) * 2 * sms &&
+                          warp_units * 2 * sms <= all_units + 5ull * sms;
   const bool rows_path = !mixed && !simt && batch <= 8 && !(flags & (HQB_FLAG_RING | HQB_FLAG_STREAMK)) &&
                          (rows_small || (flags & HQB_FLAG_ROWBLOCK)) &&
                          static_cast<uint64_t>(m->grid_rows) * m->grid_cols * kRecordBytes < (1ull << 32) &&

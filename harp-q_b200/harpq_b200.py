@@ -25,7 +25,8 @@ F32, F16 = 0, 1
 FLAG_PDL, FLAG_SIMT, FLAG_RING, FLAG_TCGEN05, FLAG_STREAMK, FLAG_ROWBLOCK = 1, 2, 4, 8, 16, 32
 # row-block kernel geometry (mirrors hqb_plane.cu): warps per CTA, shared-memory head
 # (reduction slots), shared-memory limit, and the size rule: the row-block kernel runs by
-# default while a stream-K CTA would hold at most ROWS_UNITS_MAX (tile, stage) units
+# default while a stream-K CTA would hold at most ROWS_UNITS_MAX (tile, stage) units and
+# a row-block warp would stream at most 2.5 units more than that
 ROWS_WARPS, ROWS_HEAD_BYTES, ROWS_SMEM_MAX, ROWS_UNITS_MAX = 16, 2 * 16 * 16 * 8 * 4 + 256, 200 * 1024, 16
 
 
@@ -337,7 +338,9 @@ class PlaneMatrix:
         xl = 2 if x_dtype == F32 else 1
         xslot = -(-(batch * (256 * xl + 8)) // 16) * 16
         sms = torch.cuda.get_device_properties(self.device).multi_processor_count
-        small = self.grid_rows * self.grid_cols * prefix <= ROWS_UNITS_MAX * 2 * sms
+        all_units = self.grid_rows * self.grid_cols * prefix
+        warp_units = -(-self.grid_rows * 8 // sms) * -(-self.grid_cols * prefix // ROWS_WARPS)
+        small = all_units <= ROWS_UNITS_MAX * 2 * sms and warp_units * 2 * sms <= all_units + 5 * sms
         if not mixed and not (flags & (FLAG_SIMT | FLAG_RING | FLAG_STREAMK)) and batch <= 8 \
                 and (small or (flags & FLAG_ROWBLOCK)) \
                 and ROWS_HEAD_BYTES + ROWS_WARPS * rows_xw_bytes(self.grid_cols, prefix, xslot) <= ROWS_SMEM_MAX:
