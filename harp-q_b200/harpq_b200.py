@@ -323,6 +323,30 @@ class PlaneMatrix:
         check(status, "hqb_gemv_ex")
         return out
 
+    def gemv_kernel(self, batch: int, x_dtype: int, prefix: int, mixed: bool = False, flags: int = 0) -> str:
+        """Name of the GEMV kernel one gemv() call runs, by the library's dispatch rule."""
+        if not mixed and prefix == 0:
+            return "fill_kernel"
+        if (flags & FLAG_TCGEN05) and not mixed and x_dtype == F16 and batch <= 8 \
+                and not (flags & (FLAG_SIMT | FLAG_RING)):
+            return "gemv_tc_kernel"
+        xl = 2 if x_dtype == F32 else 1
+        xslot = -(-(batch * (256 * xl + 8)) // 16) * 16
+        sms = torch.cuda.get_device_properties(self.device).multi_processor_count
+        if not mixed:
+            all_units = self.grid_rows * self.grid_cols * prefix
+            warp_units = -(-self.grid_rows * 8 // sms) * -(-self.grid_cols * prefix // ROWS_WARPS)
+            small = all_units <= ROWS_UNITS_MAX * 2 * sms and warp_units * 2 * sms <= all_units + 5 * sms
+            if not (flags & (FLAG_SIMT | FLAG_RING | FLAG_STREAMK)) and batch <= 8 \
+                    and (small or (flags & FLAG_ROWBLOCK)) \
+                    and ROWS_HEAD_BYTES + ROWS_WARPS * rows_xw_bytes(self.grid_cols, prefix, xslot) <= ROWS_SMEM_MAX \
+                    and self.grid_rows * self.grid_cols * 4352 < 2 ** 32:
+                return "gemv_rows_kernel"
+        streaming = not (flags & FLAG_SIMT) and self.grid_cols * xslot <= 64 * 1024 and not (flags & FLAG_RING)
+        if not streaming:
+            return "gemv_kernel"
+        return "gemv_stream_kernel" if mixed else "gemv_uniform_kernel"
+
     def gemv_launches(self, batch: int, x_dtype: int, prefix: int, mixed: bool = False, flags: int = 0,
                       x_prepared: bool = False) -> int:
         """Kernels one gemv() call launches, by the library's dispatch rule: the row-block
@@ -337,14 +361,9 @@ class PlaneMatrix:
             return 2  # activation blocks, then the tcgen05 kernel
         xl = 2 if x_dtype == F32 else 1
         xslot = -(-(batch * (256 * xl + 8)) // 16) * 16
-        sms = torch.cuda.get_device_properties(self.device).multi_processor_count
-        all_units = self.grid_rows * self.grid_cols * prefix
-        warp_units = -(-self.grid_rows * 8 // sms) * -(-self.grid_cols * prefix // ROWS_WARPS)
-        small = all_units <= ROWS_UNITS_MAX * 2 * sms and warp_units * 2 * sms <= all_units + 5 * sms
-        if not mixed and not (flags & (FLAG_SIMT | FLAG_RING | FLAG_STREAMK)) and batch <= 8 \
-                and (small or (flags & FLAG_ROWBLOCK)) \
-                and ROWS_HEAD_BYTES + ROWS_WARPS * rows_xw_bytes(self.grid_cols, prefix, xslot) <= ROWS_SMEM_MAX:
+        if self.gemv_kernel(batch, x_dtype, prefix, mixed, flags) == "gemv_rows_kernel":
             return 1
+        sms = torch.cuda.get_device_properties(self.device).multi_processor_count
         streaming = not (flags & FLAG_SIMT) and self.grid_cols * xslot <= 64 * 1024 and not (flags & FLAG_RING)
         avg_tiles = self.grid_rows * self.grid_cols // (sms * 2)
         fused = streaming and not mixed and avg_tiles <= 24
