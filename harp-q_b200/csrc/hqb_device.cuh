@@ -143,6 +143,26 @@ __device__ __forceinline__ void mma_f16_zero(float (&d)[4], uint32_t a0, uint32_
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(0.0f));
 }
 
+// D = A·B + C, m16n8k32, unsigned 8-bit A, signed 8-bit B, exact 32-bit integer
+// accumulate (the sums never leave the int32 range at the operand bounds used here).
+__device__ __forceinline__ void mma_u8s8(uint32_t (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1) {
+  asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%0,%1,%2,%3};"
+      : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// D = A·B + {c, c, c, c}: the first MMA of a chain, its four accumulators seeded from one
+// register.
+__device__ __forceinline__ void mma_u8s8_seed(uint32_t (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                              uint32_t b0, uint32_t b1, uint32_t c) {
+  asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%10,%10,%10,%10};"
+      : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(c));
+}
+
 // ---- tcgen05 (5th-generation tensor cores, tensor memory) -----------------------------
 
 // Allocates `cols` TMEM columns (power of two >= 32) for this CTA; one full warp calls it.

@@ -85,6 +85,7 @@ struct GemvParams {
   uint32_t* g_done;      // CTAs of this launch that finished (local, returns to zero)
   uint32_t x_vec;        // raw activation rows can be read as aligned 16-byte chunks
   uint32_t xw_bytes;     // row-block kernel: fragment bytes of each warp's shared-memory area
+  uint32_t x_res_slots;  // uniform stream-K kernel: resident activation slots per CTA
   int bias_dtype;
   int y_dtype;
 };
@@ -237,6 +238,116 @@ __device__ __forceinline__ void prep_items(const float (&v)[W][4], const bool (&
         *reinterpret_cast<float2*>(slot[w] + batch * 256 * XL + b[w] * 8) =
             make_float2(exp2_int(24 + e[w]), s[w] * exp2_int(e[w] + 1));
   }
+}
+
+// ---- int8 activation limbs (FP16 x, batch <= 2) -------------------------------------
+//
+// The integer tensor-core path multiplies u8 code fragments by s8 activation limbs with
+// m16n8k32 (exact s32 accumulate).  One AND with 0x03030303 << 2m turns a plane code
+// word into an A register whose byte j holds (code+2)·4^m of column 4j+m of the word's
+// 16 columns, so MMA m of a row block reads code position m of every byte, and its
+// B operand carries Y = round(x·2^(30-E-2m)) for those columns: the factor 4^m cancels
+// and every product is (code+2)·x·2^(30-E) up to the rounding of x.  E is the tile's
+// exponent (max|x| < 2^E), so |Y| <= 2^30 and x keeps at least 24 significant bits
+// relative to the tile maximum (an FP16 x is exact down to 2^-13 of it).  Y splits into
+// four balanced signed bytes Y = Σ_l limb_l·2^(24-8l).  The limbs ride in the MMA's N
+// columns: column n = 2·limb + batch row, so one MMA serves batch 1 and 2 alike.  An
+// accumulator that starts from the bits of 1.5·2^23 reads, as FP32, 1.5·2^23 +
+// Σ(code+2)·limb (|Σ| < 2^21), so one FMA with the column's {L, K} =
+// {2^(E-6-8·limb), -(1.5·2^23 + 2·Σlimb)·L} gives the exact limb sum Σcode·limb·L.
+//
+// Slot of one tile (xslot_i8_bytes): entries e = limb·batch + b of 128 bytes, 32 per
+// lane quad position q, word 2m + h of which is the B register b_h of MMA m (bytes j:
+// column 32q + 16h + 4j + m); then 8 columns × {L, K} FP32 ({0, 0} for columns no
+// limb uses).
+constexpr uint32_t kLimbs = 4;
+constexpr uint32_t kAccBiasBits = 0x4B400000u;  // FP32 1.5·2^23
+constexpr float kAccBias = 12582912.0f;
+
+__host__ __device__ inline uint32_t xslot_i8_bytes(uint32_t batch) { return kLimbs * batch * 128u + 64u; }
+
+// Limb preparation of W (tile column, batch row) items, one warp per item; lane L holds
+// columns 4L..4L+3 of the item's tile (v, zero past the last column).  Every path that
+// prepares limbs (prep_x_i8_kernel and the in-kernel builder) goes through this
+// function, so their slots are bit-identical.
+template <int W>
+__device__ __forceinline__ void prep_i8_items(const float (&v)[W][4], const bool (&ok)[W], uint8_t* const (&slot)[W],
+                                              const uint32_t (&b)[W], uint32_t batch, uint32_t lane) {
+  float a[W];
+#pragma unroll
+  for (int w = 0; w < W; ++w)
+    a[w] = fmaxf(fmaxf(fabsf(v[w][0]), fabsf(v[w][1])), fmaxf(fabsf(v[w][2]), fabsf(v[w][3])));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+    for (int w = 0; w < W; ++w) a[w] = fmaxf(a[w], __shfl_xor_sync(0xffffffffu, a[w], o));
+  int E[W], sum[W][kLimbs];
+#pragma unroll
+  for (int w = 0; w < W; ++w) {
+    // a < 2^E: the biased exponent field of a normal float gives floor(log2 a); the
+    // clamp keeps every limb factor 2^(E-6-8l) a normal float
+    E[w] = a[w] > 0.0f ? max(-90, min(100, ((__float_as_int(a[w]) >> 23) & 0xff) - 126)) : 0;
+    // column 4L + t: quad position L/8, half (L%8)/4, byte L%4 of word 2t + half
+    uint8_t* base = slot[w] + (lane >> 3) * 32 + (lane & 7);
+#pragma unroll
+    for (int l = 0; l < static_cast<int>(kLimbs); ++l) sum[w][l] = 0;
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      int y = __float2int_rn(v[w][t] * exp2_int(30 - E[w] - 2 * t));
+      int limb[kLimbs];
+#pragma unroll
+      for (int l = static_cast<int>(kLimbs) - 1; l > 0; --l) {
+        limb[l] = (y << 24) >> 24;  // balanced low byte
+        y = (y - limb[l]) >> 8;
+      }
+      limb[0] = y;  // |limb 0| <= 64
+#pragma unroll
+      for (int l = 0; l < static_cast<int>(kLimbs); ++l) {
+        if (ok[w]) base[(l * batch + b[w]) * 128 + 8 * t] = static_cast<uint8_t>(limb[l] & 0xff);
+        sum[w][l] += limb[l] * (1 << (2 * t));
+      }
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+    for (int w = 0; w < W; ++w)
+#pragma unroll
+      for (int l = 0; l < static_cast<int>(kLimbs); ++l) sum[w][l] += __shfl_xor_sync(0xffffffffu, sum[w][l], o);
+  if (lane == 0) {
+#pragma unroll
+    for (int w = 0; w < W; ++w) {
+      if (!ok[w]) continue;
+      float* cst = reinterpret_cast<float*>(slot[w] + kLimbs * batch * 128);
+#pragma unroll
+      for (int l = 0; l < static_cast<int>(kLimbs); ++l) {
+        const uint32_t n = 2 * l + b[w];
+        const float L = exp2_int(E[w] - 6 - 8 * l);
+        cst[2 * n] = L;
+        cst[2 * n + 1] = -(kAccBias + static_cast<float>(2 * sum[w][l])) * L;
+      }
+      if (b[w] == 0) {
+        for (uint32_t n = 0; n < 8; ++n)
+          if (n >= 2 * kLimbs || (batch == 1 && (n & 1))) cst[2 * n] = cst[2 * n + 1] = 0.0f;
+      }
+    }
+  }
+}
+
+// x [batch][cols] FP16 -> one limb slot per 128-column tile; one warp per (tile column,
+// batch row) item, four items per block.
+__global__ void __launch_bounds__(128) prep_x_i8_kernel(const __half* __restrict__ x, uint32_t cols, uint32_t batch,
+                                                        uint32_t C, uint8_t* __restrict__ xfrag, uint32_t xslot,
+                                                        uint32_t vec) {
+  const uint32_t item = blockIdx.x * 4 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (item >= C * batch) return;  // the whole warp leaves together
+  const uint32_t c = item / batch;
+  float v[1][4];
+  const bool ok[1] = {true};
+  uint8_t* const slot[1] = {xfrag + static_cast<uint64_t>(c) * xslot};
+  const uint32_t b[1] = {item - c * batch};
+  load_x4<__half>(x + static_cast<uint64_t>(b[0]) * cols, c * 128 + 4 * lane, cols, vec != 0, v[0]);
+  prep_i8_items<1>(v, ok, slot, b, batch, lane);
 }
 
 // x [batch][cols] -> one fragment slot per 128-column tile; one warp per (tile column,
@@ -953,7 +1064,9 @@ __global__ void __launch_bounds__(kStreamThreads, (NB == 1 && XL == 1) ? 2 : 1)
 // the depth D a compile-time constant.  The plane is tile-major, so the CTA walks
 // consecutive tile indices (the next tile is always +4352 bytes, also across a tile
 // row) and each tile's D stages become D independent tensor-core chains.  kTilesAhead
-// tiles of records are kept in flight in registers.
+// tiles of records are kept in flight in registers.  With I8 (FP16 x, batch <= 2) the
+// chains are integer m16n8k32 MMAs on int8 activation limbs (4 per tile-stage instead
+// of 8 FP16 MMAs, and 16 ANDs of decode instead of 32 ANDs and 4 shifts).
 
 template <int D>
 struct TilesAhead {
@@ -1138,13 +1251,13 @@ __device__ __forceinline__ void publish_flagged(const GemvParams& p, uint32_t ct
 // words not yet published are read again together (bounded), so waiting costs one
 // round trip to L2 per round, not one per word.  Consumed words are cleared to zero.
 template <int NB, bool B1>
-__device__ __forceinline__ void reduce_split_row(const GemvParams& p, uint32_t r, uint64_t units_per_row,
+__device__ __forceinline__ void reduce_split_row(const GemvParams& p, uint32_t r, uint64_t row_first_unit,
                                                  uint64_t total, uint32_t ctas, uint32_t cta,
                                                  const float (&own)[NB][4], uint32_t rit0, uint32_t q) {
   constexpr int J = B1 ? 1 : 2;                  // batch columns per lane and accumulator block
   constexpr int E = NB * J * 2;                  // elements per lane
   constexpr uint32_t K = E <= 2 ? 8 : (E <= 4 ? 4 : 2);  // contributors per group (16 words)
-  const uint32_t first = unit_owner(static_cast<uint64_t>(r) * units_per_row, total, ctas);
+  const uint32_t first = unit_owner(row_first_unit, total, ctas);
   unsigned long long* part = reinterpret_cast<unsigned long long*>(p.partials);
   uint64_t off[E];
   bool ok[E];
@@ -1321,8 +1434,16 @@ __device__ __forceinline__ ColRanges needed_columns(uint32_t t0, uint32_t t_end,
 // FP32 for XL 2) by the CTA itself through prep_items, so they are bit-identical to a
 // separately prepared buffer.  Each warp reads its items' activations straight from
 // global memory, two items at a time, so their shuffle chains interleave.
+// Resident activation slot of tile column c in a CTA whose first tile is in column
+// c_first: (c - c_first) mod C.  The CTA walks its tiles in descending order, so it visits
+// slots n-1, n-2, ..., 0 (mod C), and holds min(C, n) slots for n tiles.
+__device__ __forceinline__ uint32_t resident_slot(uint32_t c, uint32_t c_first, uint32_t C) {
+  return c >= c_first ? c - c_first : c + C - c_first;
+}
+
 template <int XL>
-__device__ __forceinline__ void build_xfrag_tiles(const GemvParams& p, uint8_t* xres, const ColRanges& cr) {
+__device__ __forceinline__ void build_xfrag_tiles(const GemvParams& p, uint8_t* xres, const ColRanges& cr,
+                                                  uint32_t c_first) {
   using XT = typename std::conditional<XL == 1, __half, float>::type;
   const XT* x = static_cast<const XT*>(p.x_raw);
   const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -1342,31 +1463,272 @@ __device__ __forceinline__ void build_xfrag_tiles(const GemvParams& p, uint8_t* 
       const uint32_t ci = it / p.batch;
       b[w] = it - ci * p.batch;
       const uint32_t c = cr.col(ci);
-      slot[w] = xres + c * p.xslot_bytes;
+      slot[w] = xres + resident_slot(c, c_first, p.C) * p.xslot_bytes;
       load_x4<XT>(x + static_cast<uint64_t>(b[w]) * p.cols, c * 128 + 4 * lane, p.cols, p.x_vec != 0, v[w]);
     }
     prep_items<XL, W>(v, ok, slot, b, p.batch, lane);
   }
 }
 
-template <int NB, int XL, int D, bool B1 = false>
+// The same for the int8 limb slots (FP16 x), through prep_i8_items.
+__device__ __forceinline__ void build_xfrag_tiles_i8(const GemvParams& p, uint8_t* xres, const ColRanges& cr,
+                                                     uint32_t c_first) {
+  const __half* x = static_cast<const __half*>(p.x_raw);
+  const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  constexpr int W = 2;
+  constexpr uint32_t kWarps = kStreamThreads / 32;
+  const uint32_t items = cr.count() * p.batch;
+  for (uint32_t base = warp; base < items; base += W * kWarps) {
+    float v[W][4];
+    bool ok[W];
+    uint8_t* slot[W];
+    uint32_t b[W];
+#pragma unroll
+    for (int w = 0; w < W; ++w) {
+      const uint32_t item = base + w * kWarps;
+      ok[w] = item < items;
+      const uint32_t it = ok[w] ? item : base;
+      const uint32_t ci = it / p.batch;
+      b[w] = it - ci * p.batch;
+      const uint32_t c = cr.col(ci);
+      slot[w] = xres + resident_slot(c, c_first, p.C) * p.xslot_bytes;
+      load_x4<__half>(x + static_cast<uint64_t>(b[w]) * p.cols, c * 128 + 4 * lane, p.cols, p.x_vec != 0, v[w]);
+    }
+    prep_i8_items<W>(v, ok, slot, b, p.batch, lane);
+  }
+}
+
+// This lane's offsets in an int8 limb slot: its B fragment (N column g carries limb g/2
+// of batch row g%2; at batch 1 the odd columns read entry 0, their accumulator columns
+// are never stored) and the {L, K} pairs of its accumulator columns 2q and 2q+1.
+struct XLaneI8 {
+  uint32_t frag, cst;
+  __device__ __forceinline__ XLaneI8(uint32_t batch, uint32_t lane) {
+    const uint32_t g = lane >> 2, q = lane & 3;
+    uint32_t entry = 0;
+    if (g < 2 * kLimbs) entry = batch == 1 ? ((g & 1) ? 0u : g >> 1) : g;
+    frag = entry * 128 + q * 32;
+    cst = kLimbs * batch * 128 + q * 16;
+  }
+};
+
+struct XFragI8 {
+  uint32_t bf[4][2];  // [MMA m][b0, b1]
+  float L[2], K[2];   // accumulator columns 2q, 2q+1
+};
+
+template <bool B1>
+__device__ __forceinline__ void load_xfrag_i8(XFragI8& xf, const XLaneI8& xl, const uint8_t* slot) {
+  const uint4 t0 = lds128(slot + xl.frag), t1 = lds128(slot + xl.frag + 16);
+  xf.bf[0][0] = t0.x;
+  xf.bf[0][1] = t0.y;
+  xf.bf[1][0] = t0.z;
+  xf.bf[1][1] = t0.w;
+  xf.bf[2][0] = t1.x;
+  xf.bf[2][1] = t1.y;
+  xf.bf[3][0] = t1.z;
+  xf.bf[3][1] = t1.w;
+  if (B1) {
+    const float2 c = lds_f2(slot + xl.cst);
+    xf.L[0] = c.x;
+    xf.K[0] = c.y;
+    xf.L[1] = xf.K[1] = 0.0f;
+  } else {
+    const uint4 c = lds128(slot + xl.cst);
+    xf.L[0] = __uint_as_float(c.x);
+    xf.K[0] = __uint_as_float(c.y);
+    xf.L[1] = __uint_as_float(c.z);
+    xf.K[1] = __uint_as_float(c.w);
+  }
+}
+
+// Integer tensor-core part of one tile: per stage 4 MMAs m16n8k32, MMA m fed by the
+// code words ANDed with 0x03030303 << 2m (no shifts).  D independent accumulator chains
+// (two for D == 1, the second starting from zero); every chain of a stage starts from
+// the bits of 1.5·2^23.
+template <int D, bool MX = false>
+__device__ __forceinline__ void tile_mma_i8(const uint4 (&w)[D], const XFragI8& xf,
+                                            uint32_t (&acc)[TileChains<D>::value][4], uint32_t live = ~0u) {
+#pragma unroll
+  for (int m = 0; m < 4; ++m) {
+    const uint32_t mask = 0x03030303u << (2 * m);
+#pragma unroll
+    for (int s = 0; s < D; ++s) {
+      if (MX && !((live >> s) & 1u)) continue;  // warp-uniform: a stage the tile does not select
+      const int c = D == 1 ? (m & 1) : s;
+      const uint32_t a0 = w[s].x & mask, a1 = w[s].y & mask, a2 = w[s].z & mask, a3 = w[s].w & mask;
+      if (D == 1 ? m < 2 : m == 0)
+        mma_u8s8_seed(acc[c], a0, a1, a2, a3, xf.bf[m][0], xf.bf[m][1], (D == 1 && c == 1) ? 0u : kAccBiasBits);
+      else
+        mma_u8s8(acc[c], a0, a1, a2, a3, xf.bf[m][0], xf.bf[m][1]);
+    }
+  }
+}
+
+// y += σ·Σcode·Y·L per stage: one FMA turns the biased accumulator into the exact limb
+// sum, one more applies the row's scale.  Each lane holds its own limb columns; the
+// lane quad is summed when a tile row ends (quad_sum).
+template <int D, bool B1, bool MX = false>
+__device__ __forceinline__ void tile_epilogue_i8(const uint32_t (&sc)[D], const XFragI8& xf,
+                                                 uint32_t (&acc)[TileChains<D>::value][4], float (&y)[1][4],
+                                                 uint32_t live = ~0u) {
+  if (D == 1) {
+    acc[0][0] += acc[1][0];
+    acc[0][2] += acc[1][2];
+    if (!B1) {
+      acc[0][1] += acc[1][1];
+      acc[0][3] += acc[1][3];
+    }
+  }
+#pragma unroll
+  for (int s = 0; s < D; ++s) {
+    if (MX && !((live >> s) & 1u)) continue;
+    const __half2 s2 = *reinterpret_cast<const __half2*>(&sc[s]);
+    const float s_lo = __low2float(s2), s_hi = __high2float(s2);
+    y[0][0] = fmaf(s_lo, fmaf(__uint_as_float(acc[s][0]), xf.L[0], xf.K[0]), y[0][0]);
+    y[0][2] = fmaf(s_hi, fmaf(__uint_as_float(acc[s][2]), xf.L[0], xf.K[0]), y[0][2]);
+    if (!B1) {
+      y[0][1] = fmaf(s_lo, fmaf(__uint_as_float(acc[s][1]), xf.L[1], xf.K[1]), y[0][1]);
+      y[0][3] = fmaf(s_hi, fmaf(__uint_as_float(acc[s][3]), xf.L[1], xf.K[1]), y[0][3]);
+    }
+  }
+}
+
+// Sum of the lane quad's limb columns; every lane of the quad ends with the same bits.
+template <bool B1>
+__device__ __forceinline__ void quad_sum(float (&y)[1][4]) {
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    if (B1 && (e & 1)) continue;
+    y[0][e] += __shfl_xor_sync(0xffffffffu, y[0][e], 1);
+    y[0][e] += __shfl_xor_sync(0xffffffffu, y[0][e], 2);
+  }
+}
+
+// ---- per-tile depth maps in the stream-K kernel ---------------------------------------
+//
+// Units are (tile, stage) pairs in tile order, Σ depth of them in all (plan[R]); CTA i of
+// G takes [⌊iT/G⌋, ⌊(i+1)T/G⌋) as for a uniform prefix.  Each warp finds its CTA's range
+// ends itself through L2 (no CTA barrier): the total and the rows holding the ends by a
+// 32-way search of the plan, the tiles by a warp scan of those rows' depths.
+
+// Largest r < R with plan[r] <= u (plan[0] = 0 <= u < plan[R]), with plan[r] and
+// plan[r + 1]; every lane returns the same values.
+__device__ __forceinline__ uint32_t plan_row_of(const uint32_t* plan, uint32_t R, uint64_t u, uint32_t lane,
+                                                uint64_t& rb, uint64_t& re) {
+  uint32_t lo = 0, hi = R;  // plan[lo] <= u < plan[hi]
+  while (hi - lo > 1) {
+    const uint32_t step = (hi - lo + 31) / 32;
+    const uint32_t idx = lo + lane * step;
+    const bool le = idx < hi && static_cast<uint64_t>(__ldg(plan + idx)) <= u;
+    const uint32_t k = 31 - __clz(__ballot_sync(0xffffffffu, le));  // lane 0 always qualifies
+    lo += k * step;
+    hi = min(hi, lo + step);
+  }
+  rb = __ldg(plan + lo);
+  re = __ldg(plan + lo + 1);
+  return lo;
+}
+
+// Tile column c and stage s of the unit `off` units into tile row r (off < the row's units).
+__device__ __forceinline__ void row_unit_tile(const GemvParams& p, uint32_t r, uint32_t off, uint32_t lane,
+                                              uint32_t& c, uint32_t& s) {
+  const uint8_t* row = p.depth + static_cast<uint64_t>(r) * p.C;
+  uint32_t before = 0;
+  for (uint32_t c0 = 0; c0 < p.C; c0 += 32) {
+    const uint32_t d = c0 + lane < p.C ? clamp_depth(__ldg(row + c0 + lane), p.stage_count) : 0u;
+    uint32_t incl = d;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t t = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= static_cast<uint32_t>(o)) incl += t;
+    }
+    const uint32_t m = __ballot_sync(0xffffffffu, before + incl > off);
+    if (m != 0) {
+      const uint32_t k = __ffs(m) - 1;
+      c = c0 + k;
+      s = off - before - __shfl_sync(0xffffffffu, incl - d, k);
+      return;
+    }
+    before += __shfl_sync(0xffffffffu, incl, 31);
+  }
+  c = p.C - 1;  // not reached for a valid plan
+  s = 0;
+}
+
+struct MixedRange {
+  uint64_t total, u0, u1;
+  uint64_t rb_first, re_last;  // first unit of the range's first row, end of its last row
+  uint32_t ctas, t0, s0, t_end, s_end;
+};
+
+__device__ __forceinline__ MixedRange mixed_range(const GemvParams& p, uint32_t cta, uint32_t lane) {
+  MixedRange m{};
+  m.total = __ldg(p.plan + p.R);
+  m.ctas = static_cast<uint32_t>(m.total < gridDim.x ? m.total : gridDim.x);
+  if (cta >= m.ctas) return m;
+  m.u0 = unit_start(cta, m.total, m.ctas);
+  m.u1 = unit_start(cta + 1, m.total, m.ctas);
+  uint64_t rb0, re0, rb1, re1;
+  const uint32_t r0 = plan_row_of(p.plan, p.R, m.u0, lane, rb0, re0);
+  const uint32_t r1 = plan_row_of(p.plan, p.R, m.u1 - 1, lane, rb1, re1);
+  uint32_t c0, s0, c1, s1;
+  row_unit_tile(p, r0, static_cast<uint32_t>(m.u0 - rb0), lane, c0, s0);
+  row_unit_tile(p, r1, static_cast<uint32_t>(m.u1 - 1 - rb1), lane, c1, s1);
+  m.rb_first = rb0;
+  m.re_last = re1;
+  m.t0 = r0 * p.C + c0;
+  m.s0 = s0;
+  m.t_end = r1 * p.C + c1;
+  m.s_end = s1 + 1;
+  return m;
+}
+
+template <int NB, int XL, int D, bool B1 = false, bool I8 = false, bool MX = false>
 __global__ void __launch_bounds__(kStreamThreads, (NB == 1 && XL == 1) ? 2 : 1)
     gemv_uniform_kernel(const __grid_constant__ GemvParams p) {
+  static_assert(!I8 || (NB == 1 && XL == 1), "the int8 limb path takes FP16 x and batch <= 2");
+  static_assert(!MX || (I8 && D == HQB_MAX_STAGES), "depth maps run on the int8 path at depth 4");
   constexpr int R = TilesAhead<D>::value;
   constexpr uint32_t kFull = (1u << D) - 1u;
-  extern __shared__ __align__(16) uint8_t xres[];  // [C x xslot activation fragments]
-  const uint64_t total = p.total;
-  const uint32_t ctas = static_cast<uint32_t>(total < gridDim.x ? total : gridDim.x), cta = blockIdx.x;
+  extern __shared__ __align__(16) uint8_t xres[];  // [resident activation slots]
+  const uint32_t cta = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, q = lane & 3;
+  // The CTA's units [u0, u1): tiles t0..t_end, the first from stage s0, the last up to
+  // stage s_end; rb_first / re_last: first unit of t0's tile row, end of t_end's.
+  MixedRange rg{};
+  if constexpr (MX) {
+    rg = mixed_range(p, cta, lane);
+  } else {
+    rg.total = p.total;
+    rg.ctas = static_cast<uint32_t>(rg.total < gridDim.x ? rg.total : gridDim.x);
+    if (cta < rg.ctas) {
+      rg.u0 = unit_start(cta, rg.total, rg.ctas);
+      rg.u1 = unit_start(cta + 1, rg.total, rg.ctas);
+      rg.t0 = static_cast<uint32_t>(rg.u0 / D);
+      rg.s0 = static_cast<uint32_t>(rg.u0 % D);
+      rg.t_end = static_cast<uint32_t>((rg.u1 - 1) / D);
+      rg.s_end = static_cast<uint32_t>((rg.u1 - 1) % D) + 1;
+      rg.rb_first = static_cast<uint64_t>(rg.t0 / p.C) * p.C * D;
+      rg.re_last = static_cast<uint64_t>(rg.t_end / p.C + 1) * p.C * D;
+    }
+  }
+  const uint64_t total = rg.total, u0 = rg.u0, u1 = rg.u1;
+  const uint32_t ctas = rg.ctas;
   griddep_launch_dependents();  // a following PDL kernel may be scheduled; it waits for this grid
   if (cta >= ctas) return;
-  const uint64_t u0 = unit_start(cta, total, ctas), u1 = unit_start(cta + 1, total, ctas);
-  const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, q = lane & 3;
   const uint32_t rit0 = warp * 16 + g;
-  // tiles t0..t0+ntiles-1; the first starts at stage s0, the last ends before stage s_end
-  const uint32_t t0 = static_cast<uint32_t>(u0 / D), s0 = static_cast<uint32_t>(u0 % D);
-  const uint32_t t_end = static_cast<uint32_t>((u1 - 1) / D), s_end = static_cast<uint32_t>((u1 - 1) % D) + 1;
+  const uint32_t t0 = rg.t0, s0 = rg.s0, t_end = rg.t_end, s_end = rg.s_end;
   const uint32_t ntiles = t_end - t0 + 1;
   const uint32_t mask_first = kFull & ~((1u << s0) - 1u), mask_last = (1u << s_end) - 1u;
+  // Stages of walk tile k (tile t_end - k) this CTA computes: all D (a depth map: the
+  // tile's depth), cut to the range at its two ends.
+  auto tile_mask = [&](uint32_t k) -> uint32_t {
+    uint32_t m = kFull;
+    if constexpr (MX) m = (1u << clamp_depth(__ldg(p.depth + (t_end - k)), p.stage_count)) - 1u;
+    if (k == 0) m &= mask_last;
+    if (k == ntiles - 1) m &= mask_first;
+    return m;
+  };
   // The CTA walks its tiles in descending order: its last tile row, which goes on in the
   // next CTA, comes first and its part is published early; its first row, which it sums
   // when that row began in an earlier CTA, comes last.
@@ -1386,11 +1748,14 @@ __global__ void __launch_bounds__(kStreamThreads, (NB == 1 && XL == 1) ? 2 : 1)
   }
 
   // Register ring of R tiles x D stages.  A stage outside the CTA's units gets scale 0
-  // (codes 0): its products are finite and its contribution is exactly zero.
+  // (codes 0): its products are finite and its contribution is exactly zero.  With a
+  // depth map such stages are not computed at all (live: the slot's stage mask).
   uint4 w[R][D];
   uint32_t sc[R][D];
+  uint32_t live[R];
   const uint64_t l2_first = policy_evict_first();
   auto load_tile = [&](int slot, uint32_t mask) {
+    live[slot] = mask;
 #pragma unroll
     for (int s = 0; s < D; ++s) {
       if (D == 1 || (mask & (1u << s))) {
@@ -1412,29 +1777,37 @@ __global__ void __launch_bounds__(kStreamThreads, (NB == 1 && XL == 1) ? 2 : 1)
   };
 #pragma unroll
   for (int j = 0; j < R; ++j) {
-    if (static_cast<uint32_t>(j) < ntiles)
-      load_tile(j, (j == 0 ? mask_last : kFull) & (static_cast<uint32_t>(j) == ntiles - 1 ? mask_first : kFull));
+    if (static_cast<uint32_t>(j) < ntiles) load_tile(j, tile_mask(j));
   }
   next_group();
   griddep_wait();
-  {  // activation fragments of the tile columns this CTA touches
-    const uint32_t c_first = t0 % p.C, c_last = t_end % p.C;
-    const bool one_row = t0 / p.C == t_end / p.C;
-    const uint32_t c_lo = one_row ? c_first : 0, c_hi = one_row ? c_last : p.C - 1;
+  const uint32_t c_first = t0 % p.C;
+  if (min(p.C, ntiles) > p.x_res_slots) {  // the launch sized shared memory for fewer slots
+    if (threadIdx.x == 0) atomicOr(p.error, HQB_DEVERR_LAUNCH);
+    return;
+  }
+  {  // activation fragments of the tile columns this CTA touches, at their resident slots
+    const ColRanges cr = needed_columns(t0, t_end, p.C);
     if (p.x_raw != nullptr) {
-      build_xfrag_tiles<XL>(p, xres, needed_columns(t0, t_end, p.C));
+      if constexpr (I8) build_xfrag_tiles_i8(p, xres, cr, c_first);
+      else build_xfrag_tiles<XL>(p, xres, cr, c_first);
     } else {
-      const uint4* src = reinterpret_cast<const uint4*>(p.xfrag + static_cast<uint64_t>(c_lo) * p.xslot_bytes);
-      uint4* dst = reinterpret_cast<uint4*>(xres + c_lo * p.xslot_bytes);
-      const uint32_t chunks = (c_hi - c_lo + 1) * p.xslot_bytes / 16;
-      for (uint32_t t = threadIdx.x; t < chunks; t += kStreamThreads) dst[t] = __ldcg(src + t);
+      const uint32_t per_slot = p.xslot_bytes / 16;
+      const uint32_t chunks = cr.count() * per_slot;
+      for (uint32_t t = threadIdx.x; t < chunks; t += kStreamThreads) {
+        const uint32_t ci = t / per_slot, k = t - ci * per_slot, c = cr.col(ci);
+        const uint4* src = reinterpret_cast<const uint4*>(p.xfrag + static_cast<uint64_t>(c) * p.xslot_bytes) + k;
+        reinterpret_cast<uint4*>(xres + resident_slot(c, c_first, p.C) * p.xslot_bytes)[k] = __ldcg(src);
+      }
     }
   }
   __syncthreads();
   const XLane<NB, XL> xlane(p.batch, lane);
-  const uint64_t units_per_row = static_cast<uint64_t>(p.C) * D;
+  const XLaneI8 xlane8(p.batch, lane);
   uint32_t row = t_end / p.C;
-  const uint8_t* xs = xres + (t_end % p.C) * p.xslot_bytes;  // activation slot of the current tile
+  // activation slot of the current tile; the next tile's is the previous slot (mod C)
+  const uint8_t* xs = xres + resident_slot(t_end % p.C, c_first, p.C) * p.xslot_bytes;
+  const uint8_t* const xs_top = xres + (p.C - 1) * p.xslot_bytes;
   uint32_t left = t_end % p.C + 1;  // tiles of the current row still ahead (may run past ntiles)
   float y[NB][4];
 #pragma unroll
@@ -1449,9 +1822,12 @@ __global__ void __launch_bounds__(kStreamThreads, (NB == 1 && XL == 1) ? 2 : 1)
   // the last tile.
   float kept[NB][4];
   bool keep = false;
+  const uint32_t row_first = t0 / p.C, row_last = t_end / p.C;
   auto advance = [&](uint32_t k) {
     if (--left == 0 || k + 1 == ntiles) {
-      const uint64_t rb = static_cast<uint64_t>(row) * units_per_row, re = rb + units_per_row;
+      if constexpr (I8) quad_sum<B1>(y);
+      // the row's unit range, as far as it matters: inside [u0, u1) unless an end row
+      const uint64_t rb = row == row_first ? rg.rb_first : u0, re = row == row_last ? rg.re_last : u1;
       if (rb >= u0 && re <= u1) {
         store_out<NB>(p, y, row * 128 + rit0, q);
       } else if (re > u1) {
@@ -1468,18 +1844,24 @@ __global__ void __launch_bounds__(kStreamThreads, (NB == 1 && XL == 1) ? 2 : 1)
 #pragma unroll
         for (int e = 0; e < 4; ++e) y[nb][e] = 0.0f;
       --row;
-      xs = xres + (p.C - 1) * p.xslot_bytes;
       left = p.C;
-    } else {
-      xs -= p.xslot_bytes;
     }
+    xs = xs == xres ? xs_top : xs - p.xslot_bytes;
   };
   auto one_tile = [&](int j) {
-    XFrag<NB, XL> xf;
-    load_xfrag<NB, XL>(xf, xlane, xs);
-    float acc[CH][NB][4];
-    tile_mma<NB, XL, D>(w[j], xf, p.shift_mul, acc);
-    tile_epilogue<NB, XL, D, B1>(sc[j], xf, acc, y);
+    if constexpr (I8) {
+      XFragI8 xf;
+      load_xfrag_i8<B1>(xf, xlane8, xs);
+      uint32_t acc[CH][4];
+      tile_mma_i8<D, MX>(w[j], xf, acc, live[j]);
+      tile_epilogue_i8<D, B1, MX>(sc[j], xf, acc, y, live[j]);
+    } else {
+      XFrag<NB, XL> xf;
+      load_xfrag<NB, XL>(xf, xlane, xs);
+      float acc[CH][NB][4];
+      tile_mma<NB, XL, D>(w[j], xf, p.shift_mul, acc);
+      tile_epilogue<NB, XL, D, B1>(sc[j], xf, acc, y);
+    }
   };
 
   uint32_t k0 = 0;
@@ -1489,7 +1871,7 @@ __global__ void __launch_bounds__(kStreamThreads, (NB == 1 && XL == 1) ? 2 : 1)
       const uint32_t k = k0 + j;
       one_tile(j);
       const uint32_t kn = k + R;  // refill slot j with tile kn (group base cb/sb)
-      if (kn < ntiles) load_tile(j, kn == ntiles - 1 ? mask_first : kFull);
+      if (kn < ntiles) load_tile(j, tile_mask(kn));
       advance(k);
     }
     next_group();
@@ -1501,7 +1883,7 @@ __global__ void __launch_bounds__(kStreamThreads, (NB == 1 && XL == 1) ? 2 : 1)
     one_tile(j);
     advance(k);
   }
-  if (keep) reduce_split_row<NB, B1>(p, t0 / p.C, units_per_row, total, ctas, cta, kept, rit0, q);
+  if (keep) reduce_split_row<NB, B1>(p, row_first, rg.rb_first, total, ctas, cta, kept, rit0, q);
   if (p.g_world > 1) gather_signal(p, ctas);
 }
 
@@ -1538,8 +1920,9 @@ __host__ __device__ inline uint32_t rows_unit_start(uint32_t w, uint32_t U) {
   return static_cast<uint32_t>(static_cast<uint64_t>(w) * U / kRowsWarps);
 }
 
-template <int XL, int D, bool B1>
+template <int XL, int D, bool B1, bool I8 = false>
 __global__ void __launch_bounds__(kRowsThreads, 1) gemv_rows_kernel(const __grid_constant__ GemvParams p) {
+  static_assert(!I8 || XL == 1, "the int8 limb path takes FP16 x");
   using XT = typename std::conditional<XL == 1, __half, float>::type;
   constexpr int R = TilesAhead<D>::value;
   constexpr int CH = TileChains<D>::value;
@@ -1627,7 +2010,8 @@ __global__ void __launch_bounds__(kRowsThreads, 1) gemv_rows_kernel(const __grid
           load_x4<XT>(x + static_cast<uint64_t>(b[i]) * p.cols, (ta + t) * 128 + 4 * lane, p.cols, p.x_vec != 0,
                       v[i]);
         }
-        prep_items<XL, 2>(v, ok, slot, b, p.batch, lane);
+        if constexpr (I8) prep_i8_items<2>(v, ok, slot, b, p.batch, lane);
+        else prep_items<XL, 2>(v, ok, slot, b, p.batch, lane);
       }
     } else {
       const uint4* src = reinterpret_cast<const uint4*>(p.xfrag + static_cast<uint64_t>(ta) * p.xslot_bytes);
@@ -1648,6 +2032,7 @@ __global__ void __launch_bounds__(kRowsThreads, 1) gemv_rows_kernel(const __grid
   const bool all_members = U >= kRowsWarps;
 
   const XLane<1, XL> xlane(p.batch, lane);
+  const XLaneI8 xlane8(p.batch, lane);
   float y[1][4] = {{0.0f, 0.0f, 0.0f, 0.0f}};
   uint32_t ct = ta, cj = 0;  // tile being computed: column ct of the CTA's item cj
   const uint8_t* xs = xw;
@@ -1667,6 +2052,7 @@ __global__ void __launch_bounds__(kRowsThreads, 1) gemv_rows_kernel(const __grid
       }
     }
     __syncwarp();
+    if constexpr (I8) quad_sum<B1>(y);  // lanes q hold limb columns: every lane gets the sums
     float* part = red + s * kRedSlotFloats;
     if (B1) {
       if (q == 0) {
@@ -1704,11 +2090,19 @@ __global__ void __launch_bounds__(kRowsThreads, 1) gemv_rows_kernel(const __grid
     }
   };
   auto one_tile = [&](int j) {
-    XFrag<1, XL> xf;
-    load_xfrag<1, XL>(xf, xlane, xs);
-    float acc[CH][1][4];
-    tile_mma<1, XL, D>(w[j], xf, p.shift_mul, acc);
-    tile_epilogue<1, XL, D, B1>(sc[j], xf, acc, y);
+    if constexpr (I8) {
+      XFragI8 xf;
+      load_xfrag_i8<B1>(xf, xlane8, xs);
+      uint32_t acc[CH][4];
+      tile_mma_i8<D>(w[j], xf, acc);
+      tile_epilogue_i8<D, B1>(sc[j], xf, acc, y);
+    } else {
+      XFrag<1, XL> xf;
+      load_xfrag<1, XL>(xf, xlane, xs);
+      float acc[CH][1][4];
+      tile_mma<1, XL, D>(w[j], xf, p.shift_mul, acc);
+      tile_epilogue<1, XL, D, B1>(sc[j], xf, acc, y);
+    }
   };
   for (uint32_t k0 = 0; k0 < total; k0 += R) {
 #pragma unroll
@@ -2236,7 +2630,8 @@ WsLayout ws_layout(uint32_t R, uint32_t C, uint32_t batch, uint32_t xl, int sms)
   L.partials = L.counters + round_up((static_cast<uint64_t>(R) + 1) * 4, 256);  // + launch-done counter
   const uint64_t gmax = static_cast<uint64_t>(sms) * kMaxCtasPerSm;
   L.xfrag = L.partials + round_up(gmax * 2 * batch * 128 * 4, 256);
-  L.xtc = L.xfrag + round_up(static_cast<uint64_t>(C) * xslot_bytes_for(batch, xl), 256);
+  const uint32_t xslot = std::max(xslot_bytes_for(batch, xl), batch <= 2 && xl == 1 ? xslot_i8_bytes(batch) : 0u);
+  L.xtc = L.xfrag + round_up(static_cast<uint64_t>(C) * xslot, 256);
   L.total = L.xtc + round_up(static_cast<uint64_t>(C) * kTcColBytes, 256);
   return L;
 }
@@ -2268,23 +2663,40 @@ GemvKernel pick_uniform_depth(uint32_t d) {
   }
 }
 
-GemvKernel pick_uniform_kernel(uint32_t nb, uint32_t xl, uint32_t d, uint32_t batch) {
+template <bool B1>
+GemvKernel pick_uniform_i8(uint32_t d) {
+  switch (d) {
+    case 1: return gemv_uniform_kernel<1, 1, 1, B1, true>;
+    case 2: return gemv_uniform_kernel<1, 1, 2, B1, true>;
+    case 3: return gemv_uniform_kernel<1, 1, 3, B1, true>;
+    default: return gemv_uniform_kernel<1, 1, 4, B1, true>;
+  }
+}
+
+GemvKernel pick_mixed_i8(uint32_t batch) {
+  return batch == 1 ? gemv_uniform_kernel<1, 1, HQB_MAX_STAGES, true, true, true>
+                    : gemv_uniform_kernel<1, 1, HQB_MAX_STAGES, false, true, true>;
+}
+
+GemvKernel pick_uniform_kernel(uint32_t nb, uint32_t xl, uint32_t d, uint32_t batch, bool i8) {
+  if (i8) return batch == 1 ? pick_uniform_i8<true>(d) : pick_uniform_i8<false>(d);
   if (nb == 1 && xl == 1 && batch == 1) return pick_uniform_depth<1, 1, true>(d);
   if (nb == 1) return xl == 1 ? pick_uniform_depth<1, 1>(d) : pick_uniform_depth<1, 2>(d);
   return xl == 1 ? pick_uniform_depth<2, 1>(d) : pick_uniform_depth<2, 2>(d);
 }
 
-template <int XL, bool B1>
+template <int XL, bool B1, bool I8 = false>
 GemvKernel pick_rows_depth(uint32_t d) {
   switch (d) {
-    case 1: return gemv_rows_kernel<XL, 1, B1>;
-    case 2: return gemv_rows_kernel<XL, 2, B1>;
-    case 3: return gemv_rows_kernel<XL, 3, B1>;
-    default: return gemv_rows_kernel<XL, 4, B1>;
+    case 1: return gemv_rows_kernel<XL, 1, B1, I8>;
+    case 2: return gemv_rows_kernel<XL, 2, B1, I8>;
+    case 3: return gemv_rows_kernel<XL, 3, B1, I8>;
+    default: return gemv_rows_kernel<XL, 4, B1, I8>;
   }
 }
 
-GemvKernel pick_rows_kernel(uint32_t xl, uint32_t d, uint32_t batch) {
+GemvKernel pick_rows_kernel(uint32_t xl, uint32_t d, uint32_t batch, bool i8) {
+  if (i8) return batch == 1 ? pick_rows_depth<1, true, true>(d) : pick_rows_depth<1, false, true>(d);
   if (xl == 1) return batch == 1 ? pick_rows_depth<1, true>(d) : pick_rows_depth<1, false>(d);
   return pick_rows_depth<2, false>(d);
 }
@@ -2329,6 +2741,9 @@ RingShape ring_shape(uint32_t slot_x, uint32_t cap, uint32_t resident) {
 }
 
 constexpr uint32_t kXResidentMax = 64 * 1024;
+// int8 limb slots a stream-K CTA holds (min(C, its tiles) of them): two CTAs per SM up
+// to 104 KB each; more use the FP16-fragment kernels.
+constexpr uint32_t kXResidentMaxI8 = 104 * 1024;
 constexpr uint64_t kFusedTilesMax = 24;
 
 uint32_t gemv_smem_cap() {
@@ -2337,7 +2752,7 @@ uint32_t gemv_smem_cap() {
     m = std::max(m, ring_shape(xslot_bytes_for(HQB_MAX_BATCH, 2), cap, 0).smem);
   for (uint32_t cap = 1; cap <= HQB_MAX_STAGES; ++cap)
     m = std::max(m, ring_shape(0, cap, kXResidentMax).smem);
-  return std::max(std::max(m, kSmemBudget + 1024), kRowsSmemMax);
+  return std::max(std::max(std::max(m, kSmemBudget + 1024), kRowsSmemMax), kXResidentMaxI8 + 256);
 }
 
 // Resident CTAs per SM for a kernel variant at a given shared-memory size (cached).
@@ -2399,6 +2814,15 @@ cudaError_t launch_tc(const GemvParams& p, uint32_t grid, uint32_t smem, bool pd
 // a multiple of 16 bytes.
 bool x_rows_vec(const void* x, uint64_t cols, uint32_t xl) {
   return (reinterpret_cast<uintptr_t>(x) & 15u) == 0 && (cols * (xl == 1 ? 2 : 4)) % 16 == 0;
+}
+
+cudaError_t launch_prep_i8(const void* x, uint64_t cols, uint32_t batch, void* xfrag, cudaStream_t st) {
+  const uint32_t C = static_cast<uint32_t>((cols + 127) / 128);
+  const uint32_t blocks = (C * batch + 3) / 4;  // one warp per (tile column, batch row)
+  prep_x_i8_kernel<<<blocks, 128, 0, st>>>(static_cast<const __half*>(x), static_cast<uint32_t>(cols), batch, C,
+                                           static_cast<uint8_t*>(xfrag), xslot_i8_bytes(batch),
+                                           x_rows_vec(x, cols, 1) ? 1u : 0u);
+  return cudaGetLastError();
 }
 
 cudaError_t launch_prep(const void* x, int x_dtype, uint64_t cols, uint32_t batch, void* xfrag, cudaStream_t st) {
@@ -2612,14 +3036,14 @@ int gemv_impl(const hqb_plane_matrix* m, uint32_t prefix, const uint8_t* depth, 
     return cudaGetLastError();
   }
   const uint8_t* xfrag = static_cast<const uint8_t*>(x);
-  const uint32_t xslot = xslot_bytes_for(batch, xl);
+  const uint32_t xslot16 = xslot_bytes_for(batch, xl);
   // Row-block kernel (uniform prefix, batch <= 8, every warp's activation fragments in its
   // shared memory; it always prepares raw activations itself): the default for small
   // layers, where the stream-K kernel's fixed cost (activation staging, cross-CTA
   // split-row sums) dominates.  Rule, from B200 timings of both kernels: a stream-K CTA
   // would hold u <= kRowsUnitsMax (tile, stage) units, and a row-block warp streams at
   // most u + 2.5 units (its items per CTA times its share of a row block).
-  const uint32_t rows_xw = mixed ? 0u : rows_xw_bytes(m->grid_cols, prefix, xslot);
+  const uint32_t rows_xw = mixed ? 0u : rows_xw_bytes(m->grid_cols, prefix, xslot16);
   const uint64_t all_units = static_cast<uint64_t>(m->grid_rows) * m->grid_cols * prefix;
   const uint64_t warp_units = ((static_cast<uint64_t>(m->grid_rows) * 8 + sms - 1) / sms) *
                               ((static_cast<uint64_t>(m->grid_cols) * prefix + kRowsWarps - 1) / kRowsWarps);
@@ -2629,16 +3053,37 @@ int gemv_impl(const hqb_plane_matrix* m, uint32_t prefix, const uint8_t* depth, 
                          (rows_small || (flags & HQB_FLAG_ROWBLOCK)) &&
                          static_cast<uint64_t>(m->grid_rows) * m->grid_cols * kRecordBytes < (1ull << 32) &&
                          kRowsHeadBytes + static_cast<uint64_t>(kRowsWarps) * rows_xw <= kRowsSmemMax;
+  // Activation slots a uniform stream-K CTA holds: min(C, its tiles), its tiles at most
+  // ceil(units / D) + 1 for units <= ceil(total / G) and any grid G >= min(SMs, total).
+  const uint64_t units_cta = (all_units + sms - 1) / sms;
+  const uint32_t uniform_res_slots = static_cast<uint32_t>(
+      std::min<uint64_t>(m->grid_cols, prefix == 0 ? 1 : (units_cta + prefix - 1) / prefix + 1));
+  // int8 activation limbs: FP16 raw x, batch <= 2, and the limb slots fit (the row-block
+  // kernel's per-warp areas, or the stream-K CTA's resident slots).
+  const bool i8_raw = !simt && !x_prepared && x_dtype == HQB_F16 && batch <= 2 &&
+                      !(flags & (HQB_FLAG_RING | HQB_FLAG_F16MMA));
+  const bool i8_ok = !mixed && i8_raw;
+  // A depth map on the int8 stream-K kernel (depth-4 form, per-tile stage masks): its
+  // CTAs hold at most ceil(R·C·stage_count / SMs) units, so as many tiles plus one.
+  const uint32_t mixed_res_slots = static_cast<uint32_t>(std::min<uint64_t>(
+      m->grid_cols, (static_cast<uint64_t>(m->grid_rows) * m->grid_cols * m->stage_count + sms - 1) / sms + 1));
+  const bool mx = mixed && i8_raw && static_cast<uint64_t>(mixed_res_slots) * xslot_i8_bytes(batch) <= kXResidentMaxI8;
+  const uint32_t rows_xw_i8 = rows_path && i8_ok ? rows_xw_bytes(m->grid_cols, prefix, xslot_i8_bytes(batch)) : 0u;
+  const bool rows_i8 = rows_path && i8_ok && kRowsHeadBytes + static_cast<uint64_t>(kRowsWarps) * rows_xw_i8 <= kRowsSmemMax;
+  const bool i8 = mx || rows_i8 || (!rows_path && i8_ok &&
+                                    static_cast<uint64_t>(uniform_res_slots) * xslot_i8_bytes(batch) <= kXResidentMaxI8);
+  const uint32_t res_slots = mx ? mixed_res_slots : uniform_res_slots;
+  const uint32_t xslot = i8 ? xslot_i8_bytes(batch) : xslot16;
   const uint64_t x_all_bytes = static_cast<uint64_t>(m->grid_cols) * xslot;
   // stream-K kernels: all fragments resident in shared memory (else the ring kernel)
-  const bool streaming = !rows_path && !simt && x_all_bytes <= kXResidentMax && !(flags & HQB_FLAG_RING);
+  const bool streaming = !rows_path && !simt && (i8 || (x_all_bytes <= kXResidentMax && !(flags & HQB_FLAG_RING)));
   // The uniform stream-K kernel builds the fragments of the columns its tiles touch; when
   // CTAs hold more than kFusedTilesMax tiles on average, one preparation launch shared by
   // all is cheaper.
   const uint64_t avg_tiles = static_cast<uint64_t>(m->grid_rows) * m->grid_cols / (static_cast<uint64_t>(sms) * 2);
-  const bool fuse_prep = !x_prepared && (rows_path || (streaming && !mixed && avg_tiles <= kFusedTilesMax));
+  const bool fuse_prep = !x_prepared && (rows_path || (streaming && (!mixed || mx) && avg_tiles <= kFusedTilesMax));
   if (!x_prepared && !fuse_prep) {
-    e = launch_prep(x, x_dtype, m->cols, batch, ws + L.xfrag, st);
+    e = i8 ? launch_prep_i8(x, m->cols, batch, ws + L.xfrag, st) : launch_prep(x, x_dtype, m->cols, batch, ws + L.xfrag, st);
     if (e != cudaSuccess) {
       cudaGetLastError();
       return e;
@@ -2689,22 +3134,26 @@ int gemv_impl(const hqb_plane_matrix* m, uint32_t prefix, const uint8_t* depth, 
   uint32_t smem = 0, threads = 0;
   uint64_t work = p.total;  // upper bound on useful CTAs
   if (rows_path) {
-    p.xw_bytes = rows_xw;
-    k = pick_rows_kernel(xl, prefix, batch);
-    smem = kRowsHeadBytes + kRowsWarps * rows_xw;
+    p.xw_bytes = rows_i8 ? rows_xw_i8 : rows_xw;
+    k = pick_rows_kernel(xl, prefix, batch, rows_i8);
+    smem = kRowsHeadBytes + kRowsWarps * p.xw_bytes;
     threads = kRowsThreads;
     work = static_cast<uint64_t>(m->grid_rows) * 8;  // row-block items
   } else {
     k = !streaming ? pick_kernel(batch > 8 ? 2 : 1, xl, simt)
+        : mx       ? pick_mixed_i8(batch)
         : mixed    ? pick_stream_kernel(batch > 8 ? 2 : 1, xl)
-                   : pick_uniform_kernel(batch > 8 ? 2 : 1, xl, prefix, batch);
-    p.x_resident = x_all_bytes <= kXResidentMax ? 1u : 0u;
+                   : pick_uniform_kernel(batch > 8 ? 2 : 1, xl, prefix, batch, i8);
+    p.x_resident = (i8 || x_all_bytes <= kXResidentMax) ? 1u : 0u;
     p.slot_x_bytes = p.x_resident ? 0u : xslot;
     const RingShape rs = ring_shape(p.slot_x_bytes, mixed ? m->stage_count : prefix,
                                     p.x_resident ? static_cast<uint32_t>(x_all_bytes) : 0u);
     p.ring_slots = rs.slots;
     p.slot_stride = rs.stride;
-    smem = !streaming ? rs.smem : static_cast<uint32_t>(x_all_bytes) + 256;
+    p.x_res_slots = res_slots;
+    smem = !streaming          ? rs.smem
+           : (mixed && !mx)    ? static_cast<uint32_t>(x_all_bytes) + 256
+                               : res_slots * xslot + 256;
     threads = streaming ? kStreamThreads : kGemvThreads;
   }
   const int per_sm = ctas_per_sm(k, smem, device, threads);
@@ -2730,7 +3179,7 @@ int gemv_impl(const hqb_plane_matrix* m, uint32_t prefix, const uint8_t* depth, 
   }
   // Split tile rows exist whenever more than one CTA shares the work; the row-block and
   // uniform stream-K kernels finish them (or have none) themselves.
-  const bool self_finishing = rows_path || (streaming && !mixed);
+  const bool self_finishing = rows_path || (streaming && (!mixed || mx));
   if (!self_finishing && (mixed || std::min<uint64_t>(grid, p.total) > 1)) {
     cudaLaunchConfig_t fc{};
     fc.gridDim = dim3(m->grid_rows);

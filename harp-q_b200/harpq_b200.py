@@ -23,6 +23,9 @@ LIB_PATH = PKG / "lib" / "libharpq_b200.so"
 
 F32, F16 = 0, 1
 FLAG_PDL, FLAG_SIMT, FLAG_RING, FLAG_TCGEN05, FLAG_STREAMK, FLAG_ROWBLOCK = 1, 2, 4, 8, 16, 32
+FLAG_F16MMA = 64  # keep the stream-K kernel on FP16-fragment MMAs (no int8 activation limbs)
+I8_LIMBS = 4
+I8_RESIDENT_MAX = 104 * 1024
 # row-block kernel geometry (mirrors hqb_plane.cu): warps per CTA, shared-memory head
 # (reduction slots), shared-memory limit, and the size rule: the row-block kernel runs by
 # default while a stream-K CTA would hold at most ROWS_UNITS_MAX (tile, stage) units and
@@ -323,8 +326,29 @@ class PlaneMatrix:
         check(status, "hqb_gemv_ex")
         return out
 
+    def uses_int8_limbs(self, batch: int, x_dtype: int, prefix: int, mixed: bool = False, flags: int = 0,
+                        x_prepared: bool = False) -> bool:
+        """Whether the GEMV kernel of one gemv() call (row-block or stream-K, uniform
+        prefix or depth map) multiplies int8 activation limbs (FP16 raw x, batch <= 2, its
+        limb slots fit)."""
+        if x_prepared or x_dtype != F16 or batch > 2 or (flags & (FLAG_SIMT | FLAG_RING | FLAG_F16MMA)):
+            return False
+        xslot = I8_LIMBS * batch * 128 + 64
+        sms = torch.cuda.get_device_properties(self.device).multi_processor_count
+        if mixed:
+            units_cta = -(-(self.grid_rows * self.grid_cols * self.stage_count) // sms)
+            return min(self.grid_cols, units_cta + 1) * xslot <= I8_RESIDENT_MAX
+        if prefix == 0 or (flags & FLAG_TCGEN05):
+            return False
+        if self.gemv_kernel(batch, x_dtype, prefix, mixed, flags) == "gemv_rows_kernel":
+            return ROWS_HEAD_BYTES + ROWS_WARPS * rows_xw_bytes(self.grid_cols, prefix, xslot) <= ROWS_SMEM_MAX
+        units_cta = -(-(self.grid_rows * self.grid_cols * prefix) // sms)
+        slots = min(self.grid_cols, -(-units_cta // prefix) + 1)
+        return slots * xslot <= I8_RESIDENT_MAX
+
     def gemv_kernel(self, batch: int, x_dtype: int, prefix: int, mixed: bool = False, flags: int = 0) -> str:
-        """Name of the GEMV kernel one gemv() call runs, by the library's dispatch rule."""
+        """Name of the GEMV kernel one gemv() call runs, by the library's dispatch rule
+        (the uniform stream-K kernel in both its FP16-fragment and int8-limb forms)."""
         if not mixed and prefix == 0:
             return "fill_kernel"
         if (flags & FLAG_TCGEN05) and not mixed and x_dtype == F16 and batch <= 8 \
@@ -342,7 +366,15 @@ class PlaneMatrix:
                     and ROWS_HEAD_BYTES + ROWS_WARPS * rows_xw_bytes(self.grid_cols, prefix, xslot) <= ROWS_SMEM_MAX \
                     and self.grid_rows * self.grid_cols * 4352 < 2 ** 32:
                 return "gemv_rows_kernel"
+        if mixed and self.uses_int8_limbs(batch, x_dtype, prefix, mixed, flags):
+            return "gemv_uniform_kernel"
         streaming = not (flags & FLAG_SIMT) and self.grid_cols * xslot <= 64 * 1024 and not (flags & FLAG_RING)
+        if not streaming and not mixed and x_dtype == F16 and batch <= 2 \
+                and not (flags & (FLAG_SIMT | FLAG_RING | FLAG_F16MMA)):
+            sms = torch.cuda.get_device_properties(self.device).multi_processor_count
+            units_cta = -(-(self.grid_rows * self.grid_cols * prefix) // sms)
+            slots = min(self.grid_cols, -(-units_cta // prefix) + 1)
+            streaming = slots * (I8_LIMBS * batch * 128 + 64) <= I8_RESIDENT_MAX
         if not streaming:
             return "gemv_kernel"
         return "gemv_stream_kernel" if mixed else "gemv_uniform_kernel"
@@ -364,12 +396,16 @@ class PlaneMatrix:
         if self.gemv_kernel(batch, x_dtype, prefix, mixed, flags) == "gemv_rows_kernel":
             return 1
         sms = torch.cuda.get_device_properties(self.device).multi_processor_count
-        streaming = not (flags & FLAG_SIMT) and self.grid_cols * xslot <= 64 * 1024 and not (flags & FLAG_RING)
+        streaming = self.gemv_kernel(batch, x_dtype, prefix, mixed, flags) in ("gemv_uniform_kernel",
+                                                                              "gemv_stream_kernel")
+        if x_prepared and not mixed and not (self.grid_cols * xslot <= 64 * 1024):
+            streaming = False  # prepared FP16 fragments: the int8-limb form does not apply
         avg_tiles = self.grid_rows * self.grid_cols // (sms * 2)
-        fused = streaming and not mixed and avg_tiles <= 24
+        mx = mixed and self.uses_int8_limbs(batch, x_dtype, prefix, mixed, flags, x_prepared)
+        fused = streaming and (not mixed or mx) and avg_tiles <= 24
         n = 0 if (x_prepared or fused) else 1
         n += 1
-        if not (streaming and not mixed):
+        if not (streaming and (not mixed or mx)):
             n += 1
         return n
 

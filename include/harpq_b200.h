@@ -56,6 +56,11 @@ extern "C" {
  * fragments would not fit shared memory). */
 #define HQB_FLAG_STREAMK 16u
 #define HQB_FLAG_ROWBLOCK 32u
+/* The stream-K kernel at batch <= 2 with FP16 x multiplies int8 activation limbs
+ * (four signed bytes of a 31-bit fixed-point copy of each 128-column tile of x, scaled
+ * to the tile's largest |x|) with integer tensor-core MMAs; this flag keeps it on the
+ * FP16-fragment MMAs instead (comparison/diagnostics). */
+#define HQB_FLAG_F16MMA 64u
 
 /* Fast-path tiling: 128x128 tiles, one scale group per tile row (group 128). */
 #define HQB_TILE 128
@@ -68,6 +73,7 @@ extern "C" {
 #define HQB_DEVERR_SCALE 1        /* a non-finite or negative FP16 scale was repacked   */
 #define HQB_DEVERR_DEPTH 2        /* a depth-map entry outside [1, stage_count]          */
 #define HQB_DEVERR_TIMEOUT 4      /* a pipeline wait exceeded its bound (kernel returned) */
+#define HQB_DEVERR_LAUNCH 8       /* shared memory sized below a CTA's work (kernel returned) */
 
 /* Matrix geometry, same fields and order as ProgressiveGemvGeometry
  * (reference native/include/harpq/progressive_gemv.hpp:15-23). */

@@ -131,7 +131,9 @@ def test_split_rows_deterministic(streamk):
 def test_row_block_kernel_matches_stream_k(rows, cols):
     """The row-block kernel (no tile row split between CTAs; the warps' parts of a row
     block summed in shared memory in warp order) against the FP64 reference and the
-    stream-K kernel at every depth, batch 1/3/8, FP16 and FP32 activations, with bias.
+    stream-K kernel at every depth, batch 1/2/3/8, FP16 and FP32 activations, with bias
+    (FP16 x at batch <= 2: both kernels on int8 activation limbs, also checked against
+    their FP16-fragment forms).
     The shapes cover fewer (tile, stage) units than warps (16x300 at depth 1), a single
     CTA wave, 86 tile columns, and CTAs that take several row blocks in turn (7168x256).
     Repeated calls are bit-identical and leave no device error."""
@@ -144,7 +146,7 @@ def test_row_block_kernel_matches_stream_k(rows, cols):
     bias = rng.standard_normal(rows).astype(np.float32)
     bt = torch.from_numpy(bias).cuda()
     w64 = {p: orc.dequantize_prefix_np(m, p).astype(np.float64) for p in (1, 2, 3, 4)}
-    for batch in (1, 3, 8):
+    for batch in (1, 2, 3, 8):
         x = rng.standard_normal((batch, cols)).astype(np.float16).astype(np.float32)
         for xdt in (torch.float16, torch.float32):
             xt = torch.from_numpy(x).cuda().to(xdt)
@@ -153,6 +155,9 @@ def test_row_block_kernel_matches_stream_k(rows, cols):
                 a = pm.gemv(xt, prefix=p, bias=bt, y_dtype=torch.float32, workspace=ws, flags=rb)
                 a2 = pm.gemv(xt, prefix=p, bias=bt, y_dtype=torch.float32, workspace=ws, flags=rb | hqb.FLAG_PDL)
                 b = pm.gemv(xt, prefix=p, bias=bt, y_dtype=torch.float32, workspace=ws, flags=hqb.FLAG_STREAMK)
+                if xdt == torch.float16 and batch <= 2:  # int8-limb forms against the FP16-fragment forms
+                    c = pm.gemv(xt, prefix=p, bias=bt, y_dtype=torch.float32, workspace=ws, flags=rb | hqb.FLAG_F16MMA)
+                    assert rel_l2(a.cpu().numpy(), c.cpu().numpy()) <= 2e-5, f"row-block int8 vs FP16 b{batch} p{p}"
                 torch.cuda.synchronize()
                 assert torch.equal(a, a2), (batch, xdt, p)
                 e64 = x.astype(np.float64) @ w64[p].T + bias[None, :]
@@ -393,7 +398,8 @@ def test_in_kernel_activation_prep_matches_prepared(cols, xdt, misalign):
         xf = hqb.prepare_x(x)
         for p in (1, 4):
             ya = pm.gemv(x, prefix=p, y_dtype=torch.float32, x_prepared=xf)
-            yb = pm.gemv(x, prefix=p, y_dtype=torch.float32)
+            # raw FP16 x at batch <= 2 defaults to int8 limbs: pin the FP16-fragment form
+            yb = pm.gemv(x, prefix=p, y_dtype=torch.float32, flags=hqb.FLAG_F16MMA)
             assert torch.equal(ya, yb), (batch, p)
 
 
@@ -423,3 +429,134 @@ def test_tcgen05_kernel_ring_wrap_and_pdl(batch):
         torch.cuda.synchronize()
         assert np.array_equal(y_pdl.cpu().numpy(), y), f"PDL p{p}"
     assert ws.error_flags() == 0
+
+
+# ---- stream-K kernel on int8 activation limbs (FP16 x, batch <= 2) -------------------
+
+def _limb_case(rows, cols, batch, seed, outliers):
+    rng = np.random.default_rng(seed)
+    m = random_matrix(rng, rows, cols)
+    x = (rng.standard_normal((batch, cols)) * 2).astype(np.float16)
+    if outliers:
+        x[:, ::97] *= 20  # outlier channels (x20, as the calibration activations of the configs)
+    bias = rng.standard_normal(rows).astype(np.float32)
+    return m, x, bias
+
+
+@pytest.mark.parametrize("rows,cols", [(300, 520), (1000, 3000), (4096, 4096), (200, 11008), (65536, 256)])
+@pytest.mark.parametrize("batch", [1, 2])
+@pytest.mark.parametrize("outliers", [False, True])
+def test_int8_limb_kernel_against_oracle(rows, cols, batch, outliers):
+    """Every prefix, FP32 and FP16 outputs, against the scalar-order oracle (plain x) or
+    the FP64 materialize-then-matvec (x with outlier channels, where the oracle's own FP32
+    running sum drifts by more than the contract), and rel-L2 against FP64 always; the
+    65536x256 case has CTAs whose tiles wrap around the two tile columns more than once."""
+    import harpq_b200 as hqb
+
+    m, x, bias = _limb_case(rows, cols, batch, rows + cols + batch, outliers)
+    pm = plane_matrix(m)
+    xt = torch.from_numpy(x).cuda()
+    xf = x.astype(np.float32)
+    bt = torch.from_numpy(bias).cuda()
+    ws = pm.workspace(batch)
+    fl = hqb.FLAG_STREAMK
+    assert pm.uses_int8_limbs(batch, hqb.F16, 1, flags=fl)
+    for p in (1, 2, 3, 4):
+        y = pm.gemv(xt, prefix=p, bias=bt, y_dtype=torch.float32, workspace=ws, flags=fl).cpu().numpy()
+        e64 = _fp64_reference(m, xf, p, bias)
+        want = e64 if outliers else orc.linear_reference(m, xf, p, bias)
+        assert_close(y, want, 2e-4, 2e-4, f"{rows}x{cols} b{batch} p{p}")
+        assert rel_l2(y, e64) <= 2e-5, f"{rows}x{cols} b{batch} p{p} rel-L2 {rel_l2(y, e64):.2e}"
+        y16 = pm.gemv(xt, prefix=p, bias=bt, y_dtype=torch.float16, workspace=ws, flags=fl).float().cpu().numpy()
+        assert_close(y16, e64, 2e-4, FP16_RTOL, f"{rows}x{cols} b{batch} p{p} f16")
+        # The FP16-fragment form removes the code offset (+2) after FP32 accumulation, so
+        # near-zero outputs next to outlier channels carry cancellation error there; the
+        # int8 form accumulates exactly.  Compare the two as vectors.
+        y_ref16 = pm.gemv(xt, prefix=p, bias=bt, y_dtype=torch.float32, workspace=ws,
+                          flags=fl | hqb.FLAG_F16MMA).cpu().numpy()
+        assert rel_l2(y, y_ref16) <= 1e-4, f"{rows}x{cols} b{batch} p{p} vs FP16-fragment kernel"
+        assert rel_l2(y, e64) <= rel_l2(y_ref16, e64) + 1e-7
+    assert ws.error_flags() == 0
+
+
+def test_int8_limb_kernel_repeatable_and_prepared_launch():
+    """A layer large enough that one limb-preparation launch serves every CTA (more than
+    24 tiles per CTA on average): bit-identical outputs call to call, FP64 parity through
+    the bit-exact device decode."""
+    import harpq_b200 as hqb
+
+    rng = np.random.default_rng(21)
+    rows, cols = 16384, 8192
+    m = random_matrix(rng, rows, cols, stages=2)
+    pm = plane_matrix(m)
+    x = torch.from_numpy((rng.standard_normal((1, cols)) * 3).astype(np.float16)).cuda()
+    ws = pm.workspace(1)
+    assert pm.uses_int8_limbs(1, hqb.F16, 2)
+    assert pm.gemv_launches(1, hqb.F16, 2) == 2  # limb preparation + GEMV
+    a = pm.gemv(x, prefix=2, y_dtype=torch.float32, workspace=ws)
+    b = pm.gemv(x, prefix=2, y_dtype=torch.float32, workspace=ws)
+    assert torch.equal(a, b)
+    e64 = (x.double() @ pm.decode(2).double().T).cpu().numpy()
+    assert_close(a.cpu().numpy(), e64, 2e-4, 2e-4, "16384x8192 p2")
+    assert rel_l2(a.cpu().numpy(), e64) <= 2e-5
+    assert ws.error_flags() == 0
+
+
+def test_int8_limb_kernel_zero_and_extreme_activations():
+    """All-zero tiles, a tile of FP16 subnormals and a tile reaching the FP16 maximum in
+    one activation row (each x keeps at least 24 bits relative to its tile's largest |x|)."""
+    import harpq_b200 as hqb
+
+    rng = np.random.default_rng(33)
+    m = random_matrix(rng, 1024, 1024)
+    pm = plane_matrix(m)
+    x = np.zeros((2, 1024), np.float16)
+    x[0, 128:256] = rng.standard_normal(128).astype(np.float16) * np.float16(2.0 ** -20)  # subnormals
+    x[0, 256:384] = (rng.standard_normal(128) * 8192).astype(np.float16)
+    x[0, 300] = np.float16(65504.0)
+    x[1, 512:] = rng.standard_normal(512).astype(np.float16)
+    xt = torch.from_numpy(x).cuda()
+    xf = x.astype(np.float32)
+    for batch in (1, 2):
+        for p in (1, 4):
+            y = pm.gemv(xt[:batch], prefix=p, y_dtype=torch.float32, flags=hqb.FLAG_STREAMK).cpu().numpy()
+            e64 = _fp64_reference(m, xf[:batch], p)
+            assert_close(y, orc.linear_reference(m, xf[:batch], p), 2e-4, 2e-4, f"b{batch} p{p}")
+            assert rel_l2(y, e64) <= 2e-5
+
+
+@pytest.mark.parametrize("rows,cols", [(300, 520), (11008, 4096), (200, 11008), (65536, 256)])
+@pytest.mark.parametrize("batch", [1, 2])
+def test_int8_limb_kernel_depth_map(rows, cols, batch):
+    """A per-tile depth map on the int8 stream-K kernel (depth-4 form, each tile's stages
+    cut by its depth, units split evenly over the CTAs): the scalar-order oracle for plain
+    x, FP64 for x with outlier channels, repeatable bytes, no device error.  11008x4096 with
+    the map of seed 7 is the mixed-depth configuration."""
+    import harpq_b200 as hqb
+
+    for outliers in (False, True):
+        m, x, bias = _limb_case(rows, cols, batch, rows + 3 * cols + batch, outliers)
+        pm = plane_matrix(m)
+        gr, gc = m.grid
+        depth = np.random.default_rng(7).integers(1, 5, size=(gr, gc)).astype(np.uint8)
+        plan = hqb.DepthPlan(torch.from_numpy(depth).cuda(), pm.stage_count)
+        assert pm.uses_int8_limbs(batch, hqb.F16, 0, mixed=True)
+        xt = torch.from_numpy(x).cuda()
+        xf = x.astype(np.float32)
+        bt = torch.from_numpy(bias).cuda()
+        ws = pm.workspace(batch)
+        y = pm.gemv(xt, depth=plan, bias=bt, y_dtype=torch.float32, workspace=ws)
+        y2 = pm.gemv(xt, depth=plan, bias=bt, y_dtype=torch.float32, workspace=ws)
+        assert torch.equal(y, y2)
+        y = y.cpu().numpy()
+        e64 = _fp64_reference(m, xf, 4, bias, depth=depth)
+        want = e64 if outliers else orc.linear_mixed(m, xf, depth, bias)
+        assert_close(y, want, 2e-4, 2e-4, f"{rows}x{cols} b{batch} outliers={outliers}")
+        assert rel_l2(y, e64) <= 2e-5
+        assert ws.error_flags() == 0
+    # uniform maps against the uniform prefix
+    for p in (1, 3):
+        u = hqb.DepthPlan(torch.full((gr, gc), p, dtype=torch.uint8, device="cuda"), 4)
+        a = pm.gemv(xt, depth=u, y_dtype=torch.float32).cpu().numpy()
+        b = pm.gemv(xt, prefix=p, y_dtype=torch.float32).cpu().numpy()
+        assert rel_l2(a, b) <= 2e-5, f"depth map of {p} vs prefix {p}"
