@@ -346,7 +346,8 @@ class PlaneMatrix:
         slots = min(self.grid_cols, -(-units_cta // prefix) + 1)
         return slots * xslot <= I8_RESIDENT_MAX
 
-    def gemv_kernel(self, batch: int, x_dtype: int, prefix: int, mixed: bool = False, flags: int = 0) -> str:
+    def gemv_kernel(self, batch: int, x_dtype: int, prefix: int, mixed: bool = False, flags: int = 0,
+                    x_prepared: bool = False) -> str:
         """Name of the GEMV kernel one gemv() call runs, by the library's dispatch rule
         (the uniform stream-K kernel in both its FP16-fragment and int8-limb forms)."""
         if not mixed and prefix == 0:
@@ -366,7 +367,7 @@ class PlaneMatrix:
                     and ROWS_HEAD_BYTES + ROWS_WARPS * rows_xw_bytes(self.grid_cols, prefix, xslot) <= ROWS_SMEM_MAX \
                     and self.grid_rows * self.grid_cols * 4352 < 2 ** 32:
                 return "gemv_rows_kernel"
-        if mixed and self.uses_int8_limbs(batch, x_dtype, prefix, mixed, flags):
+        if mixed and self.uses_int8_limbs(batch, x_dtype, prefix, mixed, flags, x_prepared):
             return "gemv_uniform_kernel"
         streaming = not (flags & FLAG_SIMT) and self.grid_cols * xslot <= 64 * 1024 and not (flags & FLAG_RING)
         if not streaming and not mixed and x_dtype == F16 and batch <= 2 \
@@ -396,8 +397,8 @@ class PlaneMatrix:
         if self.gemv_kernel(batch, x_dtype, prefix, mixed, flags) == "gemv_rows_kernel":
             return 1
         sms = torch.cuda.get_device_properties(self.device).multi_processor_count
-        streaming = self.gemv_kernel(batch, x_dtype, prefix, mixed, flags) in ("gemv_uniform_kernel",
-                                                                              "gemv_stream_kernel")
+        streaming = self.gemv_kernel(batch, x_dtype, prefix, mixed, flags, x_prepared) in ("gemv_uniform_kernel",
+                                                                                          "gemv_stream_kernel")
         if x_prepared and not mixed and not (self.grid_cols * xslot <= 64 * 1024):
             streaming = False  # prepared FP16 fragments: the int8-limb form does not apply
         avg_tiles = self.grid_rows * self.grid_cols // (sms * 2)
