@@ -3047,8 +3047,14 @@ int gemv_impl(const hqb_plane_matrix* m, uint32_t prefix, const uint8_t* depth, 
   const uint64_t all_units = static_cast<uint64_t>(m->grid_rows) * m->grid_cols * prefix;
   const uint64_t warp_units = ((static_cast<uint64_t>(m->grid_rows) * 8 + sms - 1) / sms) *
                               ((static_cast<uint64_t>(m->grid_cols) * prefix + kRowsWarps - 1) / kRowsWarps);
+  // With the int8 forms (FP16 raw x, batch <= 2) the stream-K kernel also wins once a
+  // row-block CTA would take more than two row-block items (B200 timings at 2048..12288
+  // rows, prefix 1..4).
+  const bool i8_form = !mixed && !simt && !x_prepared && x_dtype == HQB_F16 && batch <= 2 &&
+                       !(flags & (HQB_FLAG_RING | HQB_FLAG_F16MMA));
+  const uint64_t rows_items_cta = (static_cast<uint64_t>(m->grid_rows) * 8 + sms - 1) / sms;
   const bool rows_small = all_units <= static_cast<uint64_t>(kRowsUnitsMax) * 2 * sms &&
-                          warp_units * 2 * sms <= all_units + 5ull * sms;
+                          warp_units * 2 * sms <= all_units + 5ull * sms && (!i8_form || rows_items_cta <= 2);
   const bool rows_path = !mixed && !simt && batch <= 8 && !(flags & (HQB_FLAG_RING | HQB_FLAG_STREAMK)) &&
                          (rows_small || (flags & HQB_FLAG_ROWBLOCK)) &&
                          static_cast<uint64_t>(m->grid_rows) * m->grid_cols * kRecordBytes < (1ull << 32) &&

@@ -362,6 +362,8 @@ class PlaneMatrix:
             all_units = self.grid_rows * self.grid_cols * prefix
             warp_units = -(-self.grid_rows * 8 // sms) * -(-self.grid_cols * prefix // ROWS_WARPS)
             small = all_units <= ROWS_UNITS_MAX * 2 * sms and warp_units * 2 * sms <= all_units + 5 * sms
+            if x_dtype == F16 and batch <= 2 and not x_prepared and not (flags & (FLAG_SIMT | FLAG_RING | FLAG_F16MMA)):
+                small = small and -(-self.grid_rows * 8 // sms) <= 2  # int8 forms: see the library's rule
             if not (flags & (FLAG_SIMT | FLAG_RING | FLAG_STREAMK)) and batch <= 8 \
                     and (small or (flags & FLAG_ROWBLOCK)) \
                     and ROWS_HEAD_BYTES + ROWS_WARPS * rows_xw_bytes(self.grid_cols, prefix, xslot) <= ROWS_SMEM_MAX \
