@@ -1,12 +1,18 @@
 // Plane-layout kernels of the progressive int2 GEMV for sm_100a.
 //
-//   repack_kernel     reference row-major stage -> plane records (one per tile)
-//   prep_x_kernel     activations -> per-tile tensor-core B fragments + correction sums
-//   gemv_kernel       warp-specialised, bulk-copy pipelined GEMV (tensor-core or CUDA-core
-//                     consumer), stream-K partition with deterministic split-row fix-up
-//   decode_kernel     planes -> dense FP32 weights, bit-identical to DequantizePrefix
-//   depth_plan_kernel per-tile depth map -> row-cost prefix sums (the mixed-depth schedule)
-//   fill_kernel       prefix 0: bias or exact zeros
+//   repack_kernel        reference row-major stage -> plane records (one per tile)
+//   prep_x_kernel        activations -> per-tile FP16 tensor-core B fragments + correction sums
+//   prep_x_i8_kernel     FP16 activations -> per-tile int8 limbs + {L, K} epilogue constants
+//   gemv_uniform_kernel  stream-K GEMV with a per-warp register ring (uniform prefix, or a
+//                        depth map on the int8 form); split tile rows finished in-kernel
+//   gemv_rows_kernel     row-block GEMV for small layers (no tile row split between CTAs)
+//   gemv_stream_kernel   depth maps where the int8 form does not apply
+//   gemv_kernel          warp-specialised, bulk-copy pipelined GEMV (tensor-core or CUDA-core
+//                        consumer) for wide activations and comparisons, with fixup_kernel
+//   gemv_tc_kernel       tcgen05 (UMMA, TMEM accumulators) comparison GEMV
+//   decode_kernel        planes -> dense FP32 weights, bit-identical to DequantizePrefix
+//   depth_plan_kernel    per-tile depth map -> row-cost prefix sums (the mixed-depth schedule)
+//   fill_kernel          prefix 0: bias or exact zeros
 //
 // Plane record of one (tile, stage), HQB_TILE_RECORD_BYTES = 8 x 544:
 //   row block rb (tile rows 16rb..16rb+15) at rb*544:
