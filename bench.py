@@ -721,6 +721,10 @@ def main(argv=None) -> int:
     if world > 1:
         import datetime
 
+        # NCCL's version banner goes to stdout, where the one JSON line of this run belongs;
+        # keep warnings, drop the banner (an explicit INFO/TRACE request is left alone).
+        if os.environ.get("NCCL_DEBUG", "VERSION").upper() == "VERSION":
+            os.environ["NCCL_DEBUG"] = "WARN"
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                              device_id=device)
     import harpq_b200  # noqa: F401  (fails loudly when the library is missing)
