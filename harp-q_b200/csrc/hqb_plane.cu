@@ -2,7 +2,7 @@
 //
 //   repack_kernel        reference row-major stage -> plane records (one per tile)
 //   prep_x_kernel        activations -> per-tile FP16 tensor-core B fragments + correction sums
-//   prep_x_i8_kernel     FP16 activations -> per-tile int8 limbs + {L, K} epilogue constants
+//   prep_x_i8_kernel     FP16/FP32 activations -> per-tile int8 limbs + {L, K} epilogue constants
 //   gemv_uniform_kernel  stream-K GEMV with a per-warp register ring (uniform prefix, or a
 //                        depth map on the int8 form); split tile rows finished in-kernel
 //   gemv_rows_kernel     row-block GEMV for small layers (no tile row split between CTAs)
@@ -246,7 +246,7 @@ __device__ __forceinline__ void prep_items(const float (&v)[W][4], const bool (&
   }
 }
 
-// ---- int8 activation limbs (FP16 x, batch <= 2) -------------------------------------
+// ---- int8 activation limbs (FP16 or FP32 x, batch <= 2) ------------------------------
 //
 // The integer tensor-core path multiplies u8 code fragments by s8 activation limbs with
 // m16n8k32 (exact s32 accumulate).  One AND with 0x03030303 << 2m turns a plane code
@@ -340,9 +340,10 @@ __device__ __forceinline__ void prep_i8_items(const float (&v)[W][4], const bool
   }
 }
 
-// x [batch][cols] FP16 -> one limb slot per 128-column tile; one warp per (tile column,
-// batch row) item, four items per block.
-__global__ void __launch_bounds__(128) prep_x_i8_kernel(const __half* __restrict__ x, uint32_t cols, uint32_t batch,
+// x [batch][cols] (FP16 or FP32) -> one limb slot per 128-column tile; one warp per
+// (tile column, batch row) item, four items per block.
+template <typename XT>
+__global__ void __launch_bounds__(128) prep_x_i8_kernel(const XT* __restrict__ x, uint32_t cols, uint32_t batch,
                                                         uint32_t C, uint8_t* __restrict__ xfrag, uint32_t xslot,
                                                         uint32_t vec) {
   const uint32_t item = blockIdx.x * 4 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
@@ -352,7 +353,7 @@ __global__ void __launch_bounds__(128) prep_x_i8_kernel(const __half* __restrict
   const bool ok[1] = {true};
   uint8_t* const slot[1] = {xfrag + static_cast<uint64_t>(c) * xslot};
   const uint32_t b[1] = {item - c * batch};
-  load_x4<__half>(x + static_cast<uint64_t>(b[0]) * cols, c * 128 + 4 * lane, cols, vec != 0, v[0]);
+  load_x4<XT>(x + static_cast<uint64_t>(b[0]) * cols, c * 128 + 4 * lane, cols, vec != 0, v[0]);
   prep_i8_items<1>(v, ok, slot, b, batch, lane);
 }
 
@@ -1070,7 +1071,7 @@ __global__ void __launch_bounds__(kStreamThreads, (NB == 1 && XL == 1) ? 2 : 1)
 // the depth D a compile-time constant.  The plane is tile-major, so the CTA walks
 // consecutive tile indices (the next tile is always +4352 bytes, also across a tile
 // row) and each tile's D stages become D independent tensor-core chains.  kTilesAhead
-// tiles of records are kept in flight in registers.  With I8 (FP16 x, batch <= 2) the
+// tiles of records are kept in flight in registers.  With I8 (batch <= 2) the
 // chains are integer m16n8k32 MMAs on int8 activation limbs (4 per tile-stage instead
 // of 8 FP16 MMAs, and 16 ANDs of decode instead of 32 ANDs and 4 shifts).
 
@@ -1476,10 +1477,12 @@ __device__ __forceinline__ void build_xfrag_tiles(const GemvParams& p, uint8_t* 
   }
 }
 
-// The same for the int8 limb slots (FP16 x), through prep_i8_items.
+// The same for the int8 limb slots (XL 1: FP16 x, 2: FP32 x), through prep_i8_items.
+template <int XL>
 __device__ __forceinline__ void build_xfrag_tiles_i8(const GemvParams& p, uint8_t* xres, const ColRanges& cr,
                                                      uint32_t c_first) {
-  const __half* x = static_cast<const __half*>(p.x_raw);
+  using XT = typename std::conditional<XL == 1, __half, float>::type;
+  const XT* x = static_cast<const XT*>(p.x_raw);
   const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   constexpr int W = 2;
   constexpr uint32_t kWarps = kStreamThreads / 32;
@@ -1498,7 +1501,7 @@ __device__ __forceinline__ void build_xfrag_tiles_i8(const GemvParams& p, uint8_
       b[w] = it - ci * p.batch;
       const uint32_t c = cr.col(ci);
       slot[w] = xres + resident_slot(c, c_first, p.C) * p.xslot_bytes;
-      load_x4<__half>(x + static_cast<uint64_t>(b[w]) * p.cols, c * 128 + 4 * lane, p.cols, p.x_vec != 0, v[w]);
+      load_x4<XT>(x + static_cast<uint64_t>(b[w]) * p.cols, c * 128 + 4 * lane, p.cols, p.x_vec != 0, v[w]);
     }
     prep_i8_items<W>(v, ok, slot, b, p.batch, lane);
   }
@@ -1691,9 +1694,9 @@ __device__ __forceinline__ MixedRange mixed_range(const GemvParams& p, uint32_t 
 }
 
 template <int NB, int XL, int D, bool B1 = false, bool I8 = false, bool MX = false>
-__global__ void __launch_bounds__(kStreamThreads, (NB == 1 && XL == 1) ? 2 : 1)
+__global__ void __launch_bounds__(kStreamThreads, (NB == 1 && (XL == 1 || I8)) ? 2 : 1)
     gemv_uniform_kernel(const __grid_constant__ GemvParams p) {
-  static_assert(!I8 || (NB == 1 && XL == 1), "the int8 limb path takes FP16 x and batch <= 2");
+  static_assert(!I8 || NB == 1, "the int8 limb path takes batch <= 2");
   static_assert(!MX || (I8 && D == HQB_MAX_STAGES), "depth maps run on the int8 path at depth 4");
   constexpr int R = TilesAhead<D>::value;
   constexpr uint32_t kFull = (1u << D) - 1u;
@@ -1795,7 +1798,7 @@ __global__ void __launch_bounds__(kStreamThreads, (NB == 1 && XL == 1) ? 2 : 1)
   {  // activation fragments of the tile columns this CTA touches, at their resident slots
     const ColRanges cr = needed_columns(t0, t_end, p.C);
     if (p.x_raw != nullptr) {
-      if constexpr (I8) build_xfrag_tiles_i8(p, xres, cr, c_first);
+      if constexpr (I8) build_xfrag_tiles_i8<XL>(p, xres, cr, c_first);
       else build_xfrag_tiles<XL>(p, xres, cr, c_first);
     } else {
       const uint32_t per_slot = p.xslot_bytes / 16;
@@ -1928,7 +1931,6 @@ __host__ __device__ inline uint32_t rows_unit_start(uint32_t w, uint32_t U) {
 
 template <int XL, int D, bool B1, bool I8 = false>
 __global__ void __launch_bounds__(kRowsThreads, 1) gemv_rows_kernel(const __grid_constant__ GemvParams p) {
-  static_assert(!I8 || XL == 1, "the int8 limb path takes FP16 x");
   using XT = typename std::conditional<XL == 1, __half, float>::type;
   constexpr int R = TilesAhead<D>::value;
   constexpr int CH = TileChains<D>::value;
@@ -2636,7 +2638,7 @@ WsLayout ws_layout(uint32_t R, uint32_t C, uint32_t batch, uint32_t xl, int sms)
   L.partials = L.counters + round_up((static_cast<uint64_t>(R) + 1) * 4, 256);  // + launch-done counter
   const uint64_t gmax = static_cast<uint64_t>(sms) * kMaxCtasPerSm;
   L.xfrag = L.partials + round_up(gmax * 2 * batch * 128 * 4, 256);
-  const uint32_t xslot = std::max(xslot_bytes_for(batch, xl), batch <= 2 && xl == 1 ? xslot_i8_bytes(batch) : 0u);
+  const uint32_t xslot = std::max(xslot_bytes_for(batch, xl), batch <= 2 ? xslot_i8_bytes(batch) : 0u);
   L.xtc = L.xfrag + round_up(static_cast<uint64_t>(C) * xslot, 256);
   L.total = L.xtc + round_up(static_cast<uint64_t>(C) * kTcColBytes, 256);
   return L;
@@ -2669,23 +2671,27 @@ GemvKernel pick_uniform_depth(uint32_t d) {
   }
 }
 
-template <bool B1>
+template <int XL, bool B1>
 GemvKernel pick_uniform_i8(uint32_t d) {
   switch (d) {
-    case 1: return gemv_uniform_kernel<1, 1, 1, B1, true>;
-    case 2: return gemv_uniform_kernel<1, 1, 2, B1, true>;
-    case 3: return gemv_uniform_kernel<1, 1, 3, B1, true>;
-    default: return gemv_uniform_kernel<1, 1, 4, B1, true>;
+    case 1: return gemv_uniform_kernel<1, XL, 1, B1, true>;
+    case 2: return gemv_uniform_kernel<1, XL, 2, B1, true>;
+    case 3: return gemv_uniform_kernel<1, XL, 3, B1, true>;
+    default: return gemv_uniform_kernel<1, XL, 4, B1, true>;
   }
 }
 
-GemvKernel pick_mixed_i8(uint32_t batch) {
-  return batch == 1 ? gemv_uniform_kernel<1, 1, HQB_MAX_STAGES, true, true, true>
-                    : gemv_uniform_kernel<1, 1, HQB_MAX_STAGES, false, true, true>;
+GemvKernel pick_mixed_i8(uint32_t batch, uint32_t xl) {
+  if (xl == 1)
+    return batch == 1 ? gemv_uniform_kernel<1, 1, HQB_MAX_STAGES, true, true, true>
+                      : gemv_uniform_kernel<1, 1, HQB_MAX_STAGES, false, true, true>;
+  return batch == 1 ? gemv_uniform_kernel<1, 2, HQB_MAX_STAGES, true, true, true>
+                    : gemv_uniform_kernel<1, 2, HQB_MAX_STAGES, false, true, true>;
 }
 
 GemvKernel pick_uniform_kernel(uint32_t nb, uint32_t xl, uint32_t d, uint32_t batch, bool i8) {
-  if (i8) return batch == 1 ? pick_uniform_i8<true>(d) : pick_uniform_i8<false>(d);
+  if (i8 && xl == 1) return batch == 1 ? pick_uniform_i8<1, true>(d) : pick_uniform_i8<1, false>(d);
+  if (i8) return batch == 1 ? pick_uniform_i8<2, true>(d) : pick_uniform_i8<2, false>(d);
   if (nb == 1 && xl == 1 && batch == 1) return pick_uniform_depth<1, 1, true>(d);
   if (nb == 1) return xl == 1 ? pick_uniform_depth<1, 1>(d) : pick_uniform_depth<1, 2>(d);
   return xl == 1 ? pick_uniform_depth<2, 1>(d) : pick_uniform_depth<2, 2>(d);
@@ -2702,7 +2708,8 @@ GemvKernel pick_rows_depth(uint32_t d) {
 }
 
 GemvKernel pick_rows_kernel(uint32_t xl, uint32_t d, uint32_t batch, bool i8) {
-  if (i8) return batch == 1 ? pick_rows_depth<1, true, true>(d) : pick_rows_depth<1, false, true>(d);
+  if (i8 && xl == 1) return batch == 1 ? pick_rows_depth<1, true, true>(d) : pick_rows_depth<1, false, true>(d);
+  if (i8) return batch == 1 ? pick_rows_depth<2, true, true>(d) : pick_rows_depth<2, false, true>(d);
   if (xl == 1) return batch == 1 ? pick_rows_depth<1, true>(d) : pick_rows_depth<1, false>(d);
   return pick_rows_depth<2, false>(d);
 }
@@ -2822,12 +2829,18 @@ bool x_rows_vec(const void* x, uint64_t cols, uint32_t xl) {
   return (reinterpret_cast<uintptr_t>(x) & 15u) == 0 && (cols * (xl == 1 ? 2 : 4)) % 16 == 0;
 }
 
-cudaError_t launch_prep_i8(const void* x, uint64_t cols, uint32_t batch, void* xfrag, cudaStream_t st) {
+cudaError_t launch_prep_i8(const void* x, int x_dtype, uint64_t cols, uint32_t batch, void* xfrag, cudaStream_t st) {
   const uint32_t C = static_cast<uint32_t>((cols + 127) / 128);
   const uint32_t blocks = (C * batch + 3) / 4;  // one warp per (tile column, batch row)
-  prep_x_i8_kernel<<<blocks, 128, 0, st>>>(static_cast<const __half*>(x), static_cast<uint32_t>(cols), batch, C,
-                                           static_cast<uint8_t*>(xfrag), xslot_i8_bytes(batch),
-                                           x_rows_vec(x, cols, 1) ? 1u : 0u);
+  const uint32_t xl = x_dtype == HQB_F32 ? 2 : 1;
+  const uint32_t vec = x_rows_vec(x, cols, xl) ? 1u : 0u;
+  if (x_dtype == HQB_F32)
+    prep_x_i8_kernel<float><<<blocks, 128, 0, st>>>(static_cast<const float*>(x), static_cast<uint32_t>(cols), batch,
+                                                    C, static_cast<uint8_t*>(xfrag), xslot_i8_bytes(batch), vec);
+  else
+    prep_x_i8_kernel<__half><<<blocks, 128, 0, st>>>(static_cast<const __half*>(x), static_cast<uint32_t>(cols),
+                                                     batch, C, static_cast<uint8_t*>(xfrag), xslot_i8_bytes(batch),
+                                                     vec);
   return cudaGetLastError();
 }
 
@@ -3053,10 +3066,10 @@ int gemv_impl(const hqb_plane_matrix* m, uint32_t prefix, const uint8_t* depth, 
   const uint64_t all_units = static_cast<uint64_t>(m->grid_rows) * m->grid_cols * prefix;
   const uint64_t warp_units = ((static_cast<uint64_t>(m->grid_rows) * 8 + sms - 1) / sms) *
                               ((static_cast<uint64_t>(m->grid_cols) * prefix + kRowsWarps - 1) / kRowsWarps);
-  // With the int8 forms (FP16 raw x, batch <= 2) the stream-K kernel also wins once a
+  // With the int8 forms (raw x, batch <= 2) the stream-K kernel also wins once a
   // row-block CTA would take more than two row-block items (B200 timings at 2048..12288
   // rows, prefix 1..4).
-  const bool i8_form = !mixed && !simt && !x_prepared && x_dtype == HQB_F16 && batch <= 2 &&
+  const bool i8_form = !mixed && !simt && !x_prepared && batch <= 2 &&
                        !(flags & (HQB_FLAG_RING | HQB_FLAG_F16MMA));
   const uint64_t rows_items_cta = (static_cast<uint64_t>(m->grid_rows) * 8 + sms - 1) / sms;
   const bool rows_small = all_units <= static_cast<uint64_t>(kRowsUnitsMax) * 2 * sms &&
@@ -3070,9 +3083,9 @@ int gemv_impl(const hqb_plane_matrix* m, uint32_t prefix, const uint8_t* depth, 
   const uint64_t units_cta = (all_units + sms - 1) / sms;
   const uint32_t uniform_res_slots = static_cast<uint32_t>(
       std::min<uint64_t>(m->grid_cols, prefix == 0 ? 1 : (units_cta + prefix - 1) / prefix + 1));
-  // int8 activation limbs: FP16 raw x, batch <= 2, and the limb slots fit (the row-block
+  // int8 activation limbs: raw FP16 or FP32 x, batch <= 2, and the limb slots fit (the row-block
   // kernel's per-warp areas, or the stream-K CTA's resident slots).
-  const bool i8_raw = !simt && !x_prepared && x_dtype == HQB_F16 && batch <= 2 &&
+  const bool i8_raw = !simt && !x_prepared && batch <= 2 &&
                       !(flags & (HQB_FLAG_RING | HQB_FLAG_F16MMA));
   const bool i8_ok = !mixed && i8_raw;
   // A depth map on the int8 stream-K kernel (depth-4 form, per-tile stage masks): its
@@ -3095,7 +3108,8 @@ int gemv_impl(const hqb_plane_matrix* m, uint32_t prefix, const uint8_t* depth, 
   const uint64_t avg_tiles = static_cast<uint64_t>(m->grid_rows) * m->grid_cols / (static_cast<uint64_t>(sms) * 2);
   const bool fuse_prep = !x_prepared && (rows_path || (streaming && (!mixed || mx) && avg_tiles <= kFusedTilesMax));
   if (!x_prepared && !fuse_prep) {
-    e = i8 ? launch_prep_i8(x, m->cols, batch, ws + L.xfrag, st) : launch_prep(x, x_dtype, m->cols, batch, ws + L.xfrag, st);
+    e = i8 ? launch_prep_i8(x, x_dtype, m->cols, batch, ws + L.xfrag, st)
+           : launch_prep(x, x_dtype, m->cols, batch, ws + L.xfrag, st);
     if (e != cudaSuccess) {
       cudaGetLastError();
       return e;
@@ -3153,7 +3167,7 @@ int gemv_impl(const hqb_plane_matrix* m, uint32_t prefix, const uint8_t* depth, 
     work = static_cast<uint64_t>(m->grid_rows) * 8;  // row-block items
   } else {
     k = !streaming ? pick_kernel(batch > 8 ? 2 : 1, xl, simt)
-        : mx       ? pick_mixed_i8(batch)
+        : mx       ? pick_mixed_i8(batch, xl)
         : mixed    ? pick_stream_kernel(batch > 8 ? 2 : 1, xl)
                    : pick_uniform_kernel(batch > 8 ? 2 : 1, xl, prefix, batch, i8);
     p.x_resident = (i8 || x_all_bytes <= kXResidentMax) ? 1u : 0u;

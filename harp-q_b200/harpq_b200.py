@@ -23,7 +23,7 @@ LIB_PATH = PKG / "lib" / "libharpq_b200.so"
 
 F32, F16 = 0, 1
 FLAG_PDL, FLAG_SIMT, FLAG_RING, FLAG_TCGEN05, FLAG_STREAMK, FLAG_ROWBLOCK = 1, 2, 4, 8, 16, 32
-FLAG_F16MMA = 64  # keep the stream-K kernel on FP16-fragment MMAs (no int8 activation limbs)
+FLAG_F16MMA = 64  # keep the GEMV kernels on FP16-fragment MMAs (no int8 activation limbs)
 I8_LIMBS = 4
 I8_RESIDENT_MAX = 104 * 1024
 # row-block kernel geometry (mirrors hqb_plane.cu): warps per CTA, shared-memory head
@@ -331,7 +331,7 @@ class PlaneMatrix:
         """Whether the GEMV kernel of one gemv() call (row-block or stream-K, uniform
         prefix or depth map) multiplies int8 activation limbs (FP16 raw x, batch <= 2, its
         limb slots fit)."""
-        if x_prepared or x_dtype != F16 or batch > 2 or (flags & (FLAG_SIMT | FLAG_RING | FLAG_F16MMA)):
+        if x_prepared or batch > 2 or (flags & (FLAG_SIMT | FLAG_RING | FLAG_F16MMA)):
             return False
         xslot = I8_LIMBS * batch * 128 + 64
         sms = torch.cuda.get_device_properties(self.device).multi_processor_count
@@ -362,7 +362,7 @@ class PlaneMatrix:
             all_units = self.grid_rows * self.grid_cols * prefix
             warp_units = -(-self.grid_rows * 8 // sms) * -(-self.grid_cols * prefix // ROWS_WARPS)
             small = all_units <= ROWS_UNITS_MAX * 2 * sms and warp_units * 2 * sms <= all_units + 5 * sms
-            if x_dtype == F16 and batch <= 2 and not x_prepared and not (flags & (FLAG_SIMT | FLAG_RING | FLAG_F16MMA)):
+            if batch <= 2 and not x_prepared and not (flags & (FLAG_SIMT | FLAG_RING | FLAG_F16MMA)):
                 small = small and -(-self.grid_rows * 8 // sms) <= 2  # int8 forms: see the library's rule
             if not (flags & (FLAG_SIMT | FLAG_RING | FLAG_STREAMK)) and batch <= 8 \
                     and (small or (flags & FLAG_ROWBLOCK)) \
@@ -372,7 +372,7 @@ class PlaneMatrix:
         if mixed and self.uses_int8_limbs(batch, x_dtype, prefix, mixed, flags, x_prepared):
             return "gemv_uniform_kernel"
         streaming = not (flags & FLAG_SIMT) and self.grid_cols * xslot <= 64 * 1024 and not (flags & FLAG_RING)
-        if not streaming and not mixed and x_dtype == F16 and batch <= 2 \
+        if not streaming and not mixed and batch <= 2 \
                 and not (flags & (FLAG_SIMT | FLAG_RING | FLAG_F16MMA)):
             sms = torch.cuda.get_device_properties(self.device).multi_processor_count
             units_cta = -(-(self.grid_rows * self.grid_cols * prefix) // sms)

@@ -56,7 +56,7 @@ extern "C" {
  * fragments would not fit shared memory). */
 #define HQB_FLAG_STREAMK 16u
 #define HQB_FLAG_ROWBLOCK 32u
-/* The stream-K kernel at batch <= 2 with FP16 x multiplies int8 activation limbs
+/* The GEMV kernels at batch <= 2 with raw FP16 or FP32 x multiply int8 activation limbs
  * (four signed bytes of a 31-bit fixed-point copy of each 128-column tile of x, scaled
  * to the tile's largest |x|) with integer tensor-core MMAs; this flag keeps it on the
  * FP16-fragment MMAs instead (comparison/diagnostics). */

@@ -85,7 +85,8 @@ def test_gemv_batches_and_dtypes(batch, x_dtype):
 
 
 def test_fp32_activations_wide_dynamic_range():
-    """FP32 x spanning 1e-6..1e6 goes through the hi/lo split with a per-tile exponent."""
+    """FP32 x spanning 1e-6..1e6 in every tile (int8 limbs at batch 2: each x keeps at least
+    24 bits relative to its tile's largest |x|)."""
     rng = np.random.default_rng(7)
     m = random_matrix(rng, 256, 384)
     pm = plane_matrix(m)
