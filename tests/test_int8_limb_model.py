@@ -141,9 +141,9 @@ def _row_block(codes, sigma, x):
 
 
 @pytest.mark.parametrize("batch", [1, 2])
-@pytest.mark.parametrize("case", ["plain", "outliers", "extremes"])
+@pytest.mark.parametrize("case", ["plain", "outliers", "extremes", "fp32_wide"])
 def test_int8_limb_row_block_model(batch, case):
-    rng = np.random.default_rng({"plain": 1, "outliers": 2, "extremes": 3}[case] + 10 * batch)
+    rng = np.random.default_rng({"plain": 1, "outliers": 2, "extremes": 3, "fp32_wide": 4}[case] + 10 * batch)
     codes = rng.integers(-2, 2, size=(16, 128))
     sigma = rng.uniform(0.002, 0.05, size=16).astype(np.float16).astype(np.float32)
     x = rng.standard_normal((batch, 128)).astype(np.float16).astype(np.float32)
@@ -152,6 +152,9 @@ def test_int8_limb_row_block_model(batch, case):
     elif case == "extremes":
         x[0, :64] = (rng.standard_normal(64) * 2.0 ** -20).astype(np.float16)  # FP16 subnormals
         x[0, 70] = 65504.0
+    elif case == "fp32_wide":  # FP32 activations spanning 1e-6..1e6 in the tile
+        x = (np.sign(rng.standard_normal((batch, 128))) * 10.0 ** rng.uniform(-6, 6, size=(batch, 128)))
+        x = x.astype(np.float32)
     y = _row_block(codes, sigma, x)
     w = (codes * sigma[:, None]).astype(np.float64)
     ref = w @ x.T.astype(np.float64)  # [16][batch]
