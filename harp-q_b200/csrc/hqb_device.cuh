@@ -91,6 +91,14 @@ __device__ __forceinline__ void bulk_load(void* smem_dst, const void* gmem_src, 
       : "memory");
 }
 
+// 1-D bulk prefetch of global memory into L2 (bytes and address 16-byte aligned); no data
+// moves into the SM.
+__device__ __forceinline__ void bulk_prefetch_l2(const void* gmem_src, uint32_t bytes, uint64_t policy) {
+  asm volatile("cp.async.bulk.prefetch.L2.global.L2::cache_hint [%0], %1, %2;" ::"l"(gmem_src), "r"(bytes),
+               "l"(policy)
+               : "memory");
+}
+
 // Acquire-release fetch-add at GPU scope: the release orders this thread's earlier
 // memory operations (and, after a CTA barrier, those of its CTA) before the add; the
 // acquire orders what follows after it.
@@ -241,6 +249,24 @@ __device__ __forceinline__ uint32_t lds32(const void* p) {
 __device__ __forceinline__ float2 lds_f2(const void* p) {
   float2 v;
   asm volatile("ld.shared.v2.f32 {%0,%1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(smem_u32(p)));
+  return v;
+}
+
+// Shared-memory loads from 32-bit shared-window addresses (no generic-to-shared conversion
+// per access; constant offsets fold into the instruction).
+__device__ __forceinline__ uint4 lds128a(uint32_t a) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
+  return v;
+}
+__device__ __forceinline__ uint2 lds64a(uint32_t a) {
+  uint2 v;
+  asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(a));
+  return v;
+}
+__device__ __forceinline__ uint32_t lds32a(uint32_t a) {
+  uint32_t v;
+  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a));
   return v;
 }
 

@@ -24,25 +24,8 @@ LIB_PATH = PKG / "lib" / "libharpq_b200.so"
 F32, F16 = 0, 1
 FLAG_PDL, FLAG_SIMT, FLAG_RING, FLAG_TCGEN05, FLAG_STREAMK, FLAG_ROWBLOCK = 1, 2, 4, 8, 16, 32
 FLAG_F16MMA = 64  # keep the GEMV kernels on FP16-fragment MMAs (no int8 activation limbs)
+FLAG_BULK = 128  # bulk-copy kernel (batch <= 2, raw x): default for large layers, forced by this flag
 I8_LIMBS = 4
-I8_RESIDENT_MAX = 104 * 1024
-# row-block kernel geometry (mirrors hqb_plane.cu): warps per CTA, shared-memory head
-# (reduction slots), shared-memory limit, and the size rule: the row-block kernel runs by
-# default while a stream-K CTA would hold at most ROWS_UNITS_MAX (tile, stage) units and
-# a row-block warp would stream at most 2.5 units more than that
-ROWS_WARPS, ROWS_HEAD_BYTES, ROWS_SMEM_MAX, ROWS_UNITS_MAX = 16, 2 * 16 * 16 * 8 * 4 + 256, 200 * 1024, 16
-
-
-def rows_xw_bytes(grid_cols: int, depth: int, xslot: int) -> int:
-    """Fragment bytes of one warp's area in the row-block kernel: the most tile columns
-    any warp's contiguous range of the C*depth (tile, stage) units touches."""
-    units = grid_cols * depth
-    nt = 0
-    for w in range(ROWS_WARPS):
-        ua, ub = w * units // ROWS_WARPS, (w + 1) * units // ROWS_WARPS
-        if ua < ub:
-            nt = max(nt, (ub - 1) // depth - ua // depth + 1)
-    return nt * xslot
 TILE = 128
 RECORD_BYTES = 4352
 MAX_STAGES = 4
@@ -72,6 +55,11 @@ class PlaneMatrixC(ctypes.Structure):
                 ("reserved", u32), ("planes", vp * MAX_STAGES)]
 
 
+class LaunchInfo(ctypes.Structure):
+    _fields_ = [("launches", u32), ("int8_limbs", u32), ("grid", u32), ("block", u32), ("smem_bytes", u32),
+                ("reserved", u32), ("kernel", ctypes.c_char * 40)]
+
+
 MAX_PEERS = 8
 
 
@@ -97,6 +85,7 @@ EXPORTS = {
     "hqb_gemv_ex": (i32, [ctypes.POINTER(PlaneMatrixC), u32, vp, vp, vp, i32, u32, i32, vp, i32, vp, i32, vp, u64,
                           u32, vp]),
     "hqb_gemv_noalloc": (i32, [ctypes.POINTER(PlaneMatrixC), u32, vp, i32, u32, vp, i32, vp, i32, vp]),
+    "hqb_gemv_query": (i32, [ctypes.POINTER(PlaneMatrixC), u32, i32, i32, u32, i32, u32, ctypes.POINTER(LaunchInfo)]),
     "hqb_peer_alloc": (i32, [u64, ctypes.POINTER(vp), vp]),
     "hqb_peer_open": (i32, [vp, ctypes.POINTER(vp)]),
     "hqb_peer_close": (i32, [vp]),
@@ -326,91 +315,29 @@ class PlaneMatrix:
         check(status, "hqb_gemv_ex")
         return out
 
+    def launch_info(self, batch: int, x_dtype: int, prefix: int, mixed: bool = False, flags: int = 0,
+                    x_prepared: bool = False) -> LaunchInfo:
+        """What one gemv() call enqueues on this device (the library's own choice, hqb_gemv_query)."""
+        info = LaunchInfo()
+        with torch.cuda.device(self.device):
+            check(lib().hqb_gemv_query(ctypes.byref(self.c_struct()), prefix, 1 if mixed else 0, x_dtype, batch,
+                                       1 if x_prepared else 0, flags, ctypes.byref(info)), "hqb_gemv_query")
+        return info
+
     def uses_int8_limbs(self, batch: int, x_dtype: int, prefix: int, mixed: bool = False, flags: int = 0,
                         x_prepared: bool = False) -> bool:
-        """Whether the GEMV kernel of one gemv() call (row-block or stream-K, uniform
-        prefix or depth map) multiplies int8 activation limbs (FP16 raw x, batch <= 2, its
-        limb slots fit)."""
-        if x_prepared or batch > 2 or (flags & (FLAG_SIMT | FLAG_RING | FLAG_F16MMA)):
-            return False
-        xslot = I8_LIMBS * batch * 128 + 64
-        sms = torch.cuda.get_device_properties(self.device).multi_processor_count
-        if mixed:
-            units_cta = -(-(self.grid_rows * self.grid_cols * self.stage_count) // sms)
-            return min(self.grid_cols, units_cta + 1) * xslot <= I8_RESIDENT_MAX
-        if prefix == 0 or (flags & FLAG_TCGEN05):
-            return False
-        if self.gemv_kernel(batch, x_dtype, prefix, mixed, flags) == "gemv_rows_kernel":
-            return ROWS_HEAD_BYTES + ROWS_WARPS * rows_xw_bytes(self.grid_cols, prefix, xslot) <= ROWS_SMEM_MAX
-        units_cta = -(-(self.grid_rows * self.grid_cols * prefix) // sms)
-        slots = min(self.grid_cols, -(-units_cta // prefix) + 1)
-        return slots * xslot <= I8_RESIDENT_MAX
+        """Whether the GEMV kernel of one gemv() call multiplies int8 activation limbs."""
+        return bool(self.launch_info(batch, x_dtype, prefix, mixed, flags, x_prepared).int8_limbs)
 
     def gemv_kernel(self, batch: int, x_dtype: int, prefix: int, mixed: bool = False, flags: int = 0,
                     x_prepared: bool = False) -> str:
-        """Name of the GEMV kernel one gemv() call runs, by the library's dispatch rule
-        (the uniform stream-K kernel in both its FP16-fragment and int8-limb forms)."""
-        if not mixed and prefix == 0:
-            return "fill_kernel"
-        if (flags & FLAG_TCGEN05) and not mixed and x_dtype == F16 and batch <= 8 \
-                and not (flags & (FLAG_SIMT | FLAG_RING)):
-            return "gemv_tc_kernel"
-        xl = 2 if x_dtype == F32 else 1
-        xslot = -(-(batch * (256 * xl + 8)) // 16) * 16
-        sms = torch.cuda.get_device_properties(self.device).multi_processor_count
-        if not mixed:
-            all_units = self.grid_rows * self.grid_cols * prefix
-            warp_units = -(-self.grid_rows * 8 // sms) * -(-self.grid_cols * prefix // ROWS_WARPS)
-            small = all_units <= ROWS_UNITS_MAX * 2 * sms and warp_units * 2 * sms <= all_units + 5 * sms
-            if batch <= 2 and not x_prepared and not (flags & (FLAG_SIMT | FLAG_RING | FLAG_F16MMA)):
-                small = small and -(-self.grid_rows * 8 // sms) <= 2  # int8 forms: see the library's rule
-            if not (flags & (FLAG_SIMT | FLAG_RING | FLAG_STREAMK)) and batch <= 8 \
-                    and (small or (flags & FLAG_ROWBLOCK)) \
-                    and ROWS_HEAD_BYTES + ROWS_WARPS * rows_xw_bytes(self.grid_cols, prefix, xslot) <= ROWS_SMEM_MAX \
-                    and self.grid_rows * self.grid_cols * 4352 < 2 ** 32:
-                return "gemv_rows_kernel"
-        if mixed and self.uses_int8_limbs(batch, x_dtype, prefix, mixed, flags, x_prepared):
-            return "gemv_uniform_kernel"
-        streaming = not (flags & FLAG_SIMT) and self.grid_cols * xslot <= 64 * 1024 and not (flags & FLAG_RING)
-        if not streaming and not mixed and batch <= 2 \
-                and not (flags & (FLAG_SIMT | FLAG_RING | FLAG_F16MMA)):
-            sms = torch.cuda.get_device_properties(self.device).multi_processor_count
-            units_cta = -(-(self.grid_rows * self.grid_cols * prefix) // sms)
-            slots = min(self.grid_cols, -(-units_cta // prefix) + 1)
-            streaming = slots * (I8_LIMBS * batch * 128 + 64) <= I8_RESIDENT_MAX
-        if not streaming:
-            return "gemv_kernel"
-        return "gemv_stream_kernel" if mixed else "gemv_uniform_kernel"
+        """Name of the GEMV kernel one gemv() call runs."""
+        return self.launch_info(batch, x_dtype, prefix, mixed, flags, x_prepared).kernel.decode()
 
     def gemv_launches(self, batch: int, x_dtype: int, prefix: int, mixed: bool = False, flags: int = 0,
                       x_prepared: bool = False) -> int:
-        """Kernels one gemv() call launches, by the library's dispatch rule: the row-block
-        kernel alone (uniform prefix, batch <= 8: it prepares raw activations itself and
-        has no split tile rows); otherwise activation preparation unless x is prepared or
-        the uniform stream-K kernel prepares it, the GEMV and, unless that kernel runs
-        (it reduces split tile rows itself), the split-row fix-up."""
-        if not mixed and prefix == 0:
-            return 1  # bias / zero fill only
-        if (flags & FLAG_TCGEN05) and not mixed and not x_prepared and x_dtype == F16 and batch <= 8 \
-                and not (flags & (FLAG_SIMT | FLAG_RING)):
-            return 2  # activation blocks, then the tcgen05 kernel
-        xl = 2 if x_dtype == F32 else 1
-        xslot = -(-(batch * (256 * xl + 8)) // 16) * 16
-        if self.gemv_kernel(batch, x_dtype, prefix, mixed, flags) == "gemv_rows_kernel":
-            return 1
-        sms = torch.cuda.get_device_properties(self.device).multi_processor_count
-        streaming = self.gemv_kernel(batch, x_dtype, prefix, mixed, flags, x_prepared) in ("gemv_uniform_kernel",
-                                                                                          "gemv_stream_kernel")
-        if x_prepared and not mixed and not (self.grid_cols * xslot <= 64 * 1024):
-            streaming = False  # prepared FP16 fragments: the int8-limb form does not apply
-        avg_tiles = self.grid_rows * self.grid_cols // (sms * 2)
-        mx = mixed and self.uses_int8_limbs(batch, x_dtype, prefix, mixed, flags, x_prepared)
-        fused = streaming and (not mixed or mx) and avg_tiles <= 24
-        n = 0 if (x_prepared or fused) else 1
-        n += 1
-        if not (streaming and (not mixed or mx)):
-            n += 1
-        return n
+        """Kernels one gemv() call launches (activation preparation, GEMV, split-row fix-up)."""
+        return int(self.launch_info(batch, x_dtype, prefix, mixed, flags, x_prepared).launches)
 
     def gemv_gather(self, x: torch.Tensor, gather: "Gather", prefix: int | None = None,
                     bias: torch.Tensor | None = None, workspace: Workspace | None = None, flags: int = 0,

@@ -61,6 +61,12 @@ extern "C" {
  * to the tile's largest |x|) with integer tensor-core MMAs; this flag keeps it on the
  * FP16-fragment MMAs instead (comparison/diagnostics). */
 #define HQB_FLAG_F16MMA 64u
+/* Batch <= 2 with raw FP16 or FP32 x, uniform prefix or depth map: the bulk-copy kernel
+ * (plane chunks of ~40-52 KB moved into shared memory by 1-D bulk copies issued ahead of
+ * the programmatic-dependent-launch wait, int8 activation limbs).  It is the default for
+ * uniform layers of >= 96 MB of selected planes at prefix >= 2; this flag selects it for
+ * any layer. */
+#define HQB_FLAG_BULK 128u
 
 /* Fast-path tiling: 128x128 tiles, one scale group per tile row (group 128). */
 #define HQB_TILE 128
@@ -208,6 +214,24 @@ HQB_API int hqb_gemv_ex(const hqb_plane_matrix* m, uint32_t prefix, const uint8_
                         uint32_t batch, int x_prepared, const void* bias, int bias_dtype,
                         void* y, int y_dtype, void* workspace, uint64_t workspace_bytes,
                         uint32_t flags, void* stream);
+
+/* What one GEMV call would enqueue on the current device, without enqueueing anything:
+ * the library's own kernel choice for (m, prefix or depth map, x dtype, batch, prepared x,
+ * flags).  No reference counterpart (the reference has one kernel). */
+typedef struct hqb_launch_info {
+  uint32_t launches;   /* kernels the call enqueues (activation preparation, GEMV, fix-up) */
+  uint32_t int8_limbs; /* 1 when the GEMV multiplies int8 activation limbs */
+  uint32_t grid;       /* the GEMV kernel's CTAs */
+  uint32_t block;      /* its threads per CTA */
+  uint32_t smem_bytes; /* its dynamic shared memory per CTA */
+  uint32_t reserved;
+  char kernel[40];     /* GEMV kernel family, e.g. "gemv_bulk_kernel" (NUL-terminated) */
+} hqb_launch_info;
+
+/* mixed != 0: a per-tile depth map (prefix ignored).  Returns the status hqb_gemv_ex would
+ * return for invalid arguments, else 0 with *info filled. */
+HQB_API int hqb_gemv_query(const hqb_plane_matrix* m, uint32_t prefix, int mixed, int x_dtype, uint32_t batch,
+                           int x_prepared, uint32_t flags, hqb_launch_info* info);
 
 /* ---- GEMV with a fixed scratch (no reference counterpart) --------------------------- */
 
