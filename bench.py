@@ -273,8 +273,19 @@ def run_ours(args, rank, world, device):
     srcs = {g["src"]: g["cols"] for g in groups}
     gen = torch.Generator(device=device)
     gen.manual_seed(7)
-    x_dev = {s: torch.randn(1, k, generator=gen, device=device).half() for s, k in srcs.items()}
-    y_loc = {g["name"]: torch.empty(1, g["nrows"], dtype=torch.float16, device=device) for g in groups}
+    # every input of a step in one device buffer and every output in another (views per
+    # group), so a step moves its inputs and outputs with one copy each way
+    x_all = torch.empty(sum(srcs.values()), dtype=torch.float16, device=device)
+    x_dev, off = {}, 0
+    for s_, k in srcs.items():
+        x_dev[s_] = x_all[off:off + k].view(1, k)
+        x_dev[s_].copy_(torch.randn(1, k, generator=gen, device=device).half())
+        off += k
+    y_all = torch.empty(sum(g["nrows"] for g in groups), dtype=torch.float16, device=device)
+    y_loc, off = {}, 0
+    for g in groups:
+        y_loc[g["name"]] = y_all[off:off + g["nrows"]].view(1, g["nrows"])
+        off += g["nrows"]
     y_full = {g["name"]: torch.empty(world, g["slot_rows"], dtype=torch.float16, device=device) for g in groups}
     # N > 1: NCCL all_gather_into_tensor of each group's output slices; --fused-gather uses
     # the fused all-gather instead (outputs stored into every rank's buffer over NVLink by
@@ -339,26 +350,33 @@ def run_ours(args, rank, world, device):
             torch.distributed.barrier()
         torch.cuda.synchronize()
 
-    # ---- timed region: K steps
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    barrier()
-    t_timed0 = time.monotonic()
-    start.record()
-    for i in range(args.steps):
-        if use_graph:
-            graphs[i % ncopies].replay()
-        else:
-            step(i % ncopies)
-    end.record()
-    barrier()
+    # ---- timed region: K steps, repeated; each repeat bracketed by a barrier and a
+    # synchronize on both sides and timed with CUDA events, the max over ranks taken per
+    # repeat; the headline is the median repeat
+    repeats = max(1, args.repeats)
+    rep_ms = []
+    t_timed0 = None
+    for _ in range(repeats):
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier()
+        if t_timed0 is None:
+            t_timed0 = time.monotonic()
+        start.record()
+        for i in range(args.steps):
+            if use_graph:
+                graphs[i % ncopies].replay()
+            else:
+                step(i % ncopies)
+        end.record()
+        barrier()
+        ms = start.elapsed_time(end)
+        if world > 1:
+            t = torch.tensor([ms], device=device)
+            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+            ms = float(t.item())
+        rep_ms.append(ms / args.steps)
     t_timed1 = time.monotonic()
-    ms = start.elapsed_time(end)
-    ms_max = ms
-    if world > 1:
-        t = torch.tensor([ms], device=device)
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        ms_max = float(t.item())
-    ms_per_step = ms_max / args.steps
+    ms_per_step = statistics.median(rep_ms)
     # whole-job bytes: the full (unsharded) layers, each input once per group
     total_bytes = sum(group_bytes([{"nrows": m["rows"]} for m in g["members"]], g["cols"], prefix) for g in groups)
     value = total_bytes / (ms_per_step * 1e-3) / 1e9
@@ -408,22 +426,68 @@ def run_ours(args, rank, world, device):
     dom_b, dom_ms = by_kernel[dominant]
     achieved = dom_b / (dom_ms * 1e-3) / 1e9
 
-    # ---- e2e through the public API: pinned host x -> device, GEMVs, device -> host y
-    host_x = {s: x_dev[s].cpu().pin_memory() for s in srcs}
+    # ---- N > 1: the step's collective alone (the NCCL all-gathers of every group, in one
+    # graph), so that the step splits into per-rank GEMV time and gather time
+    gather_us = None
+    if world > 1 and not fused:
+        gg = torch.cuda.CUDAGraph()
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            for G in groups:
+                gather(G)
+        torch.cuda.current_stream().wait_stream(side)
+        with torch.cuda.graph(gg):
+            for _ in range(8):
+                for G in groups:
+                    gather(G)
+        for _ in range(2):
+            gg.replay()
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(5):
+            gg.replay()
+        e1.record()
+        barrier()
+        t = torch.tensor([e0.elapsed_time(e1) / 40.0], device=device)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        gather_us = round(float(t.item()) * 1e3, 3)
+        del gg
+    gemv_us = sum(v["us"] for v in kern.values())
+    if world > 1:
+        t = torch.tensor([gemv_us], device=device)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        gemv_us = float(t.item())
+
+    # ---- e2e through the public API: pinned host x -> device, GEMVs, device -> host y.
+    # One host->device copy of the step's inputs and one device->host copy of its outputs;
+    # at N = 1 the step's GEMVs go to the library in one call (hqb.Step: hqb_gemv_batch), at
+    # N > 1 call by call with the all-gathers between them.
+    host_x_all = x_all.cpu().pin_memory()
+
     def gathered(g, copy):
         if fused:
             return gathers[g["name"]][copy % 2].out
         return y_full[g["name"]] if world > 1 else y_loc[g["name"]]
 
-    host_y = {g["name"]: torch.empty_like(gathered(g, 0), device="cpu").pin_memory() for g in groups}
-    x_stage = {s: torch.empty_like(x_dev[s]) for s in srcs}
+    if world == 1:
+        host_y_all = torch.empty_like(y_all, device="cpu").pin_memory()
+        steps_api = [hqb.Step([(G["copies"][c], x_dev[G["src"]], prefix, y_loc[G["name"]], hqb.FLAG_PDL)
+                               for G in groups], ws) for c in range(ncopies)]
+        host_y = {"all": host_y_all}
+    else:
+        host_y = {g["name"]: torch.empty_like(gathered(g, 0), device="cpu").pin_memory() for g in groups}
 
     def e2e_step(copy):
-        for s in srcs:
-            x_stage[s].copy_(host_x[s], non_blocking=True)
-        step(copy, x_src=x_stage)
-        for g in groups:
-            host_y[g["name"]].copy_(gathered(g, copy), non_blocking=True)
+        x_all.copy_(host_x_all, non_blocking=True)
+        if world == 1:
+            steps_api[copy].run()
+            host_y_all.copy_(y_all, non_blocking=True)
+        else:
+            step(copy)
+            for g in groups:
+                host_y[g["name"]].copy_(gathered(g, copy), non_blocking=True)
 
     for i in range(3):
         e2e_step(i % ncopies)
@@ -440,7 +504,7 @@ def run_ours(args, rank, world, device):
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
         e2e_ms = float(t.item())
     e2e_ms /= args.steps
-    h2d = sum(x.numel() * 2 for x in host_x.values())
+    h2d = host_x_all.numel() * 2
     d2h = sum(y.numel() * 2 for y in host_y.values())
 
     clk.__exit__(None, None, None)
@@ -483,10 +547,19 @@ def run_ours(args, rank, world, device):
         "kernels": kern,
         "e2e": {"value": round(total_bytes / (e2e_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
                 "us_per_step": round(e2e_ms * 1e3, 2), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
-        "gpu_launches": launches_per_step * args.steps,
+        "gpu_launches": launches_per_step * args.steps * repeats,
+        "timing": {"repeats": repeats, "steps_per_repeat": args.steps,
+                   "ms_per_step": [round(v, 5) for v in rep_ms], "median_ms": round(ms_per_step, 5),
+                   "min_ms": round(min(rep_ms), 5), "max_ms": round(max(rep_ms), 5)},
         "clocks": clk.summary(t_timed0, t_timed1),
         "device_error_flags": flags | gather_flags,
     }
+    if world > 1:
+        # per rank (max over ranks): the GEMV launches of a step timed alone, the step's
+        # gather alone (NCCL; the fused gather stores inside the GEMV), and the whole step
+        result["per_rank"] = {"gemv_us": round(gemv_us, 3), "gather_us": gather_us,
+                              "step_us": round(ms_per_step * 1e3, 3),
+                              "gather": "fused-p2p" if fused else "nccl-all_gather_into_tensor"}
     peaks = {}
     try:
         peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
@@ -607,7 +680,95 @@ def supplementary(device):
     out["small_batch_p4"] = sb
     del copies
     torch.cuda.empty_cache()
+    out["prefix_sweep"] = prefix_sweep(device, gen)
+    out["reference_gpu_kernel"] = reference_gpu_kernel(device, gen)
     return out
+
+
+def prefix_sweep(device, gen):
+    """The metric at every prefix depth: config 1 (4096x4096) and the 7B MLP shapes
+    (11008x4096, 4096x11008), batch 1, FP16 x/y, the library's default kernel per shape;
+    weights rotate over > 3x L2."""
+    import harpq_b200 as hqb
+
+    res = {}
+    for rows, cols in ((4096, 4096), (11008, 4096), (4096, 11008)):
+        per_copy = 4 * 17 * rows * cols // 64
+        n = max(2, -(-3 * L2_BYTES // per_copy))
+        mats = [_random_plane_matrix(rows, cols, gen, device) for _ in range(n)]
+        x = torch.randn(1, cols, device=device, generator=gen).half()
+        y = torch.empty(1, rows, device=device, dtype=torch.float16)
+        ws = hqb.Workspace(mats[0].workspace_bytes(1, hqb.F16), device)
+        for p in (1, 2, 3, 4):
+            us = _graph_us(lambda i: mats[i % n].gemv(x, prefix=p, out=y, workspace=ws, flags=hqb.FLAG_PDL), 32)
+            b = algorithmic_bytes(rows, cols, p)
+            res[f"{rows}x{cols}_p{p}"] = {"us": round(us, 3), "gbs": round(b / (us * 1e-6) / 1e9, 1),
+                                          "kernel": mats[0].gemv_kernel(1, hqb.F16, p)}
+        del mats
+        torch.cuda.empty_cache()
+    return res
+
+
+def reference_gpu_kernel(device, gen):
+    """The reference's own ProgressiveGemvKernel (native/src/progressive_gemv.cu:348-411),
+    compiled for sm_100a from its sources into oracle/_ref/libharpq_ref_gpu.so and launched
+    through its LaunchProgressiveGemv, timed on this GPU next to this library's drop-in
+    reference-layout kernel (hqb_raw_gemv) and its plane kernel, on the same codes and scales
+    (reference layout: row-major codes, FP16 scales), FP32 x/y as the reference takes them,
+    weights rotating over > 3x L2."""
+    import ctypes
+
+    import harpq_b200 as hqb
+
+    path = ROOT / "oracle" / "_ref" / "libharpq_ref_gpu.so"
+    if not path.exists():
+        return {"unavailable": "oracle/_ref/libharpq_ref_gpu.so not built"}
+    R = ctypes.CDLL(str(path))
+    R.hqr_gpu_launch.restype = ctypes.c_int
+    R.hqr_gpu_launch.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_uint32,
+                                 ctypes.c_uint32, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
+    res = {}
+    for rows, cols, p in ((4096, 4096, 2), (11008, 4096, 2)):
+        g = hqb.geometry(rows, cols)
+        per_copy = p * 17 * rows * cols // 64
+        n = max(2, -(-3 * L2_BYTES // per_copy))
+        raw = []
+        for _ in range(n):
+            codes = [torch.randint(0, 256, (g.padded_rows * g.padded_columns // 4,), dtype=torch.uint8, device=device,
+                                   generator=gen) for _ in range(p)]
+            bits = [(torch.rand(g.padded_rows // 128 * (g.padded_columns // 128) * 128, device=device, generator=gen)
+                     * 0.01 + 1e-3).half().view(torch.int16) for _ in range(p)]
+            raw.append((codes, bits))
+        x = torch.randn(cols, device=device, generator=gen)
+        y = torch.empty(rows, device=device)
+        geo = (ctypes.c_uint64 * 7)(g.original_rows, g.original_columns, g.padded_rows, g.padded_columns,
+                                    g.tile_rows, g.tile_columns, g.group_size)
+        ptrs = [((ctypes.c_void_p * p)(*[c.data_ptr() for c in codes]), (ctypes.c_void_p * p)(*[b.data_ptr() for b in bits]))
+                for codes, bits in raw]
+        stream = lambda: torch.cuda.current_stream().cuda_stream
+
+        def ref(i):
+            rc = R.hqr_gpu_launch(geo, ptrs[i % n][0], ptrs[i % n][1], p, p, x.data_ptr(), None, y.data_ptr(), stream())
+            if rc != 0:
+                raise RuntimeError(f"reference LaunchProgressiveGemv: {rc}")
+
+        mats = [hqb.RawMatrix(g, codes, bits) for codes, bits in raw]
+        planes = [hqb.PlaneMatrix.from_stages(rows, cols, codes, bits) for codes, bits in raw]
+        ws = hqb.Workspace(planes[0].workspace_bytes(1, hqb.F32), device)
+        b = p * (rows * cols // 4 + rows * (cols // 128) * 2) + 4 * cols + 4 * rows  # FP32 x and y
+        t_ref = _graph_us(ref, 16)
+        t_raw = _graph_us(lambda i: mats[i % n].gemv(x, p), 16)
+        xr = x.view(1, -1)
+        t_plane = _graph_us(lambda i: planes[i % n].gemv(xr, prefix=p, out=y.view(1, -1), workspace=ws,
+                                                          flags=hqb.FLAG_PDL), 16)
+        res[f"{rows}x{cols}_p{p}"] = {
+            "reference_kernel_us": round(t_ref, 3), "reference_kernel_gbs": round(b / (t_ref * 1e-6) / 1e9, 1),
+            "hqb_raw_gemv_us": round(t_raw, 3), "hqb_raw_gemv_gbs": round(b / (t_raw * 1e-6) / 1e9, 1),
+            "plane_us": round(t_plane, 3), "plane_gbs": round(b / (t_plane * 1e-6) / 1e9, 1),
+            "plane_speedup_vs_reference_kernel": round(t_ref / t_plane, 2)}
+        del raw, mats, planes, ptrs
+        torch.cuda.empty_cache()
+    return res
 
 
 # ---------------------------------------------------------------------------------------
@@ -671,6 +832,32 @@ def time_reference(name, steps, warmup, device, threads=None, budget_s=None):
                       f"{mean * 1e3:.1f} ms/step", "ms_per_step": mean * 1e3, "steps_timed": len(times)}
 
 
+def time_numpy_reference(name, device, budget_s=12.0):
+    """The reference's NumPy progressive_matmul (src/harpq/quantization.py:352-406, restated
+    in oracle/oracle.py: progressive_matmul_np) on the host: per layer, each selected stage
+    decoded to dense FP32 and multiplied through BLAS with every host core.  Steps run until
+    the budget is spent (at least one)."""
+    from oracle import oracle as orc
+
+    prefix, mats, xs = reference_inputs(name, device)
+    by_src: dict = {}
+    for _, src, m in mats:
+        by_src.setdefault(src, (m.cols, []))[1].append({"nrows": m.rows})
+    step_bytes = sum(group_bytes(members, cols, prefix) for cols, members in by_src.values())
+    times = []
+    t_all = time.perf_counter()
+    while not times or (time.perf_counter() - t_all < budget_s and len(times) < 20):
+        t0 = time.perf_counter()
+        for _, src, m in mats:
+            orc.progressive_matmul_np(m, xs[src], prefix)
+        times.append(time.perf_counter() - t0)
+    mean = sum(times) / len(times)
+    blas = {k: os.environ[k] for k in ("OMP_NUM_THREADS", "OPENBLAS_NUM_THREADS", "MKL_NUM_THREADS") if k in os.environ}
+    return {"value": round(step_bytes / mean / 1e9, 4), "unit": "GB/s", "cores": os.cpu_count() or 1, "kind": "port",
+            "sample": f"{len(times)} full {name} step(s) of the NumPy progressive_matmul restatement, BLAS threads "
+                      f"{blas or 'default (all cores)'}, {mean * 1e3:.1f} ms/step"}
+
+
 def run_reference_arm(args, device):
     name = args.workload
     # each step is one full pass of the workload on the host cores; the run stops
@@ -699,6 +886,7 @@ def main(argv=None) -> int:
     ap.add_argument("--no-graph", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extras", action="store_true", help="skip the supplementary single-GPU measurements")
+    ap.add_argument("--repeats", type=int, default=5, help="timed regions of --steps steps (median reported)")
     ap.add_argument("--fused-gather", action="store_true",
                     help="N > 1: gather outputs with the fused P2P gather instead of NCCL all_gather_into_tensor")
     args = ap.parse_args(argv)
@@ -721,10 +909,8 @@ def main(argv=None) -> int:
     if world > 1:
         import datetime
 
-        # NCCL's version banner goes to stdout, where the one JSON line of this run belongs;
-        # keep warnings, drop the banner (an explicit INFO/TRACE request is left alone).
-        if os.environ.get("NCCL_DEBUG", "VERSION").upper() == "VERSION":
-            os.environ["NCCL_DEBUG"] = "WARN"
+        # NCCL's own lines (banner, NCCL_DEBUG=INFO communicator lines) go to stdout before
+        # the one JSON line, which rank 0 prints last
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                              device_id=device)
     import harpq_b200  # noqa: F401  (fails loudly when the library is missing)
@@ -740,6 +926,7 @@ def main(argv=None) -> int:
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cb = time_reference(args.workload, 3, 1, device, budget_s=20.0)
         result["cpu_baseline"] = {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")}
+        result["cpu_baseline"]["numpy"] = time_numpy_reference(args.workload, device)
     if world > 1:
         torch.distributed.barrier()
         torch.distributed.destroy_process_group()

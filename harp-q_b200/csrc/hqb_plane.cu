@@ -39,6 +39,7 @@
 #include <cstdint>
 #include <cstring>
 #include <mutex>
+#include <new>
 #include <type_traits>
 
 #include "harpq_b200.h"
@@ -1707,13 +1708,14 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemv_tc_kernel(const __grid_con
 
 // Waits (one thread, bounded) until every rank's counter in `flags` reached *epoch + 1,
 // then advances the epoch.
-__global__ void gather_wait_kernel(const uint32_t* flags, uint32_t world, uint32_t* epoch, int* device_flags) {
+__global__ void gather_wait_kernel(const uint32_t* flags, uint32_t world, uint32_t* epoch, int* device_flags,
+                                   unsigned long long limit_ns) {
   if (threadIdx.x != 0) return;
   const uint32_t target = *epoch + 1u;
   const unsigned long long start = global_timer_ns();
   for (uint32_t r = 0; r < world; ++r) {
     while (static_cast<int32_t>(ld_acquire_sys(flags + r) - target) < 0) {
-      if (global_timer_ns() - start > kWaitLimitNs) {
+      if (global_timer_ns() - start > limit_ns) {
         if (device_flags != nullptr) atomicOr(device_flags, HQB_DEVERR_TIMEOUT);
         *epoch = target;
         return;
@@ -2340,13 +2342,14 @@ int gemv_impl(const hqb_plane_matrix* m, uint32_t prefix, const uint8_t* depth, 
   // Bulk-copy kernel (hqb_bulk.cu): raw FP16 or FP32 x at batch <= 2, uniform prefix or a
   // depth map -- the default there.  Plane bytes reach shared memory through large 1-D
   // bulk copies issued ahead of griddepcontrol.wait; activations become int8 limbs.
-  // Default for large uniform-prefix layers (>= 96 MB of selected planes, prefix >= 2), where
-  // its steady streaming rate wins; smaller layers keep the register-ring kernels, whose
-  // fixed cost per launch is lower (B200 timings of both).  HQB_FLAG_BULK forces it.
+  // Default for wide layers (>= 128 tile columns, i.e. K >= 16384) of >= 96 MB of selected
+  // planes at prefix >= 2, where its streaming rate wins (8192x28672 at prefix 3: 35.0 us
+  // against 39.2 us); elsewhere the register-ring kernels keep the lower fixed cost per
+  // launch (B200 timings of both).  HQB_FLAG_BULK forces it.
   const bool bulk_form = !simt && !x_prepared && batch <= 2 &&
                          !(flags & (HQB_FLAG_RING | HQB_FLAG_F16MMA | HQB_FLAG_STREAMK | HQB_FLAG_ROWBLOCK));
   const uint64_t sel_plane_bytes = static_cast<uint64_t>(m->grid_rows) * m->grid_cols * kRecordBytes * prefix;
-  const bool bulk_default = !mixed && prefix >= 2 && sel_plane_bytes >= (96ull << 20);
+  const bool bulk_default = !mixed && prefix >= 2 && m->grid_cols >= 128 && sel_plane_bytes >= (96ull << 20);
   if (bulk_form && ((flags & HQB_FLAG_BULK) || bulk_default)) {
     const uint32_t kd = mixed ? HQB_MAX_STAGES : prefix;
     // units: exact for a uniform prefix; a depth map's total lives on the device, so the
@@ -2617,13 +2620,20 @@ HQB_API int hqb_gemv_gather(const hqb_plane_matrix* m, uint32_t prefix, const vo
                    workspace_bytes, flags, stream, gather);
 }
 
-HQB_API int hqb_gather_wait(const uint32_t* flags, uint32_t world, uint32_t* epoch, int* device_flags,
-                            void* stream) {
-  if (flags == nullptr || epoch == nullptr || world == 0 || world > HQB_MAX_PEERS) return HQB_ERR_INVALID;
+HQB_API int hqb_gather_wait_ex(const uint32_t* flags, uint32_t world, uint32_t* epoch, int* device_flags,
+                               uint64_t limit_ns, void* stream) {
+  if (flags == nullptr || epoch == nullptr || world == 0 || world > HQB_MAX_PEERS || limit_ns == 0)
+    return HQB_ERR_INVALID;
   const cudaError_t prior = take_prior_error();
   if (prior != cudaSuccess) return prior;
-  gather_wait_kernel<<<1, 32, 0, as_stream(stream)>>>(flags, world, epoch, device_flags);
+  gather_wait_kernel<<<1, 32, 0, as_stream(stream)>>>(flags, world, epoch, device_flags,
+                                                      std::min<uint64_t>(limit_ns, kWaitLimitNs));
   return cudaGetLastError();
+}
+
+HQB_API int hqb_gather_wait(const uint32_t* flags, uint32_t world, uint32_t* epoch, int* device_flags,
+                            void* stream) {
+  return hqb_gather_wait_ex(flags, world, epoch, device_flags, kWaitLimitNs, stream);
 }
 
 HQB_API int hqb_peer_alloc(uint64_t bytes, void** ptr, void* ipc_handle) {
@@ -2657,6 +2667,78 @@ HQB_API int hqb_peer_close(void* ptr) {
 HQB_API int hqb_peer_free(void* ptr) {
   if (ptr == nullptr) return HQB_ERR_INVALID;
   return cudaFree(ptr);
+}
+
+HQB_API int hqb_gemv_batch(const hqb_gemv_call* calls, uint32_t count, void* workspace, uint64_t workspace_bytes,
+                           void* stream) {
+  if (calls == nullptr || count == 0) return HQB_ERR_INVALID;
+  for (uint32_t i = 0; i < count; ++i) {
+    const hqb_gemv_call& c = calls[i];
+    const int st = gemv_impl(c.m, c.prefix, c.depth, c.depth_plan, c.x, c.x_dtype, c.batch, c.x_prepared, c.bias,
+                             c.bias_dtype, c.y, c.y_dtype, workspace, workspace_bytes, c.flags, stream, nullptr);
+    if (st != HQB_OK) return st;
+  }
+  return HQB_OK;
+}
+
+}  // extern "C"
+
+// A captured decode step: the CUDA graph of a batch of GEMV calls.
+struct hqb_step {
+  cudaGraph_t graph = nullptr;
+  cudaGraphExec_t exec = nullptr;
+};
+
+extern "C" {
+
+HQB_API int hqb_step_create(const hqb_gemv_call* calls, uint32_t count, void* workspace, uint64_t workspace_bytes,
+                            hqb_step** step) {
+  if (step == nullptr || calls == nullptr || count == 0) return HQB_ERR_INVALID;
+  *step = nullptr;
+  const cudaError_t prior = take_prior_error();
+  if (prior != cudaSuccess) return prior;
+  cudaStream_t s = nullptr;
+  cudaError_t e = cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking);
+  if (e != cudaSuccess) return e;
+  hqb_step* st = new (std::nothrow) hqb_step();
+  if (st == nullptr) {
+    cudaStreamDestroy(s);
+    return cudaErrorMemoryAllocation;
+  }
+  int status = cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal);
+  if (status == cudaSuccess) {
+    status = hqb_gemv_batch(calls, count, workspace, workspace_bytes, s);
+    cudaGraph_t g = nullptr;
+    const cudaError_t end = cudaStreamEndCapture(s, &g);  // always end the capture
+    if (status == HQB_OK) status = end;
+    st->graph = g;
+    if (status == HQB_OK) status = cudaGraphInstantiate(&st->exec, g, 0);
+  }
+  cudaStreamDestroy(s);
+  if (status != HQB_OK) {
+    if (st->exec != nullptr) cudaGraphExecDestroy(st->exec);
+    if (st->graph != nullptr) cudaGraphDestroy(st->graph);
+    delete st;
+    cudaGetLastError();
+    return status;
+  }
+  *step = st;
+  return HQB_OK;
+}
+
+HQB_API int hqb_step_launch(hqb_step* step, void* stream) {
+  if (step == nullptr || step->exec == nullptr) return HQB_ERR_INVALID;
+  const cudaError_t prior = take_prior_error();
+  if (prior != cudaSuccess) return prior;
+  return cudaGraphLaunch(step->exec, as_stream(stream));
+}
+
+HQB_API int hqb_step_destroy(hqb_step* step) {
+  if (step == nullptr) return HQB_ERR_INVALID;
+  if (step->exec != nullptr) cudaGraphExecDestroy(step->exec);
+  if (step->graph != nullptr) cudaGraphDestroy(step->graph);
+  delete step;
+  return HQB_OK;
 }
 
 HQB_API int hqb_gemv(const hqb_plane_matrix* m, uint32_t prefix, const void* x, int x_dtype, uint32_t batch,

@@ -14,9 +14,13 @@
 //   prepared activations: each call writes them before it reads them, so they need no
 //       initial value.
 //
-// Set-up: the first call on a device, with that device current, resolves the array's
-// address on that device with cudaGetSymbolAddress and enqueues a clear of the whole
-// array on the caller's stream.  Later calls reuse the cached address.
+// Set-up: every call, with the device current, resolves the array's address on that
+// device with cudaGetSymbolAddress; the first call (and a call that finds the address
+// changed, after cudaDeviceReset) enqueues a clear of the whole array on the caller's
+// stream.  Make the first call before any stream capture.
+//
+// Recovery: hqb_gemv_noalloc_flags reads (and optionally clears) the error word;
+// hqb_gemv_noalloc_reset clears the whole array again, for use after a non-zero word.
 //
 // Concurrency: there is ONE scratch per device.  Calls whose GPU work overlaps (on
 // different streams, or from several host threads without ordering between their
@@ -37,22 +41,30 @@ __device__ __align__(256) unsigned char g_gemv_scratch[HQB_NOALLOC_SCRATCH_BYTES
 
 constexpr int kMaxDevices = 64;
 std::mutex g_setup_mutex;
-void* g_scratch_on_device[kMaxDevices];  // resolved once per device, never released
+void* g_scratch_on_device[kMaxDevices];  // last address seen per device (cleared there)
 
-// Address of this device's scratch; the first call per device resolves it and clears
-// the array on `st`.
+// Address of this device's scratch.  It is resolved on every call (cudaGetSymbolAddress
+// allocates nothing): the first call per device, and any call that finds the address
+// changed (the module loaded again after cudaDeviceReset), clears the array on `st`.
 cudaError_t device_scratch(int device, cudaStream_t st, void** out) {
+  void* p = nullptr;
+  cudaError_t e = cudaGetSymbolAddress(&p, g_gemv_scratch);
+  if (e != cudaSuccess) return e;
+  if (p == nullptr || (reinterpret_cast<uintptr_t>(p) & 255u) != 0) return cudaErrorInvalidDevicePointer;
   std::lock_guard<std::mutex> lock(g_setup_mutex);
-  if (g_scratch_on_device[device] == nullptr) {
-    void* p = nullptr;
-    cudaError_t e = cudaGetSymbolAddress(&p, g_gemv_scratch);
-    if (e != cudaSuccess) return e;
-    if (p == nullptr || (reinterpret_cast<uintptr_t>(p) & 255u) != 0) return cudaErrorInvalidDevicePointer;
+  if (g_scratch_on_device[device] != p) {
     e = cudaMemsetAsync(p, 0, HQB_NOALLOC_SCRATCH_BYTES, st);
     if (e != cudaSuccess) return e;
     g_scratch_on_device[device] = p;
   }
-  *out = g_scratch_on_device[device];
+  *out = p;
+  return cudaSuccess;
+}
+
+cudaError_t current_device(int* device) {
+  cudaError_t e = cudaGetDevice(device);
+  if (e != cudaSuccess) return e;
+  if (*device < 0 || *device >= kMaxDevices) return cudaErrorInvalidDevice;
   return cudaSuccess;
 }
 
@@ -63,9 +75,8 @@ extern "C" HQB_API int hqb_gemv_noalloc(const hqb_plane_matrix* m, uint32_t pref
                                         void* stream) {
   if (m == nullptr || x == nullptr || y == nullptr) return HQB_ERR_INVALID;
   int device = 0;
-  cudaError_t e = cudaGetDevice(&device);
+  cudaError_t e = current_device(&device);
   if (e != cudaSuccess) return e;
-  if (device < 0 || device >= kMaxDevices) return cudaErrorInvalidDevice;
   // Same size rule as a caller workspace; 0 means the matrix, batch or dtype is invalid.
   const uint64_t need = hqb_workspace_bytes(m, batch, x_dtype, device);
   if (need == 0) return HQB_ERR_INVALID;
@@ -77,4 +88,37 @@ extern "C" HQB_API int hqb_gemv_noalloc(const hqb_plane_matrix* m, uint32_t pref
   if (e != cudaSuccess) return e;
   return hqb_gemv(m, prefix, x, x_dtype, batch, bias, bias_dtype, y, y_dtype, scratch, HQB_NOALLOC_SCRATCH_BYTES,
                   stream);
+}
+
+// The error word is the scratch's first 4 bytes (the workspace layout of hqb_gemv).
+extern "C" HQB_API int hqb_gemv_noalloc_flags(int* host_flags, int clear, void* stream) {
+  if (host_flags == nullptr) return HQB_ERR_INVALID;
+  int device = 0;
+  cudaError_t e = current_device(&device);
+  if (e != cudaSuccess) return e;
+  void* scratch = nullptr;
+  e = device_scratch(device, hqb::as_stream(stream), &scratch);
+  if (e != cudaSuccess) return e;
+  e = cudaMemcpyAsync(host_flags, scratch, sizeof(int), cudaMemcpyDeviceToHost, hqb::as_stream(stream));
+  if (e == cudaSuccess && clear) e = cudaMemsetAsync(scratch, 0, sizeof(int), hqb::as_stream(stream));
+  if (e != cudaSuccess) return e;
+  return cudaStreamSynchronize(hqb::as_stream(stream));
+}
+
+extern "C" HQB_API int hqb_gemv_noalloc_reset(void* stream) {
+  int device = 0;
+  cudaError_t e = current_device(&device);
+  if (e != cudaSuccess) return e;
+  void* scratch = nullptr;
+  e = device_scratch(device, hqb::as_stream(stream), &scratch);
+  if (e != cudaSuccess) return e;
+  return cudaMemsetAsync(scratch, 0, HQB_NOALLOC_SCRATCH_BYTES, hqb::as_stream(stream));
+}
+
+extern "C" HQB_API int hqb_gemv_noalloc_scratch(void** ptr) {
+  if (ptr == nullptr) return HQB_ERR_INVALID;
+  int device = 0;
+  cudaError_t e = current_device(&device);
+  if (e != cudaSuccess) return e;
+  return device_scratch(device, nullptr, ptr);
 }

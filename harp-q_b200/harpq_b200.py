@@ -30,7 +30,8 @@ TILE = 128
 RECORD_BYTES = 4352
 MAX_STAGES = 4
 MAX_BATCH = 16
-DEVERR_SCALE, DEVERR_DEPTH, DEVERR_TIMEOUT = 1, 2, 4
+DEVERR_SCALE, DEVERR_DEPTH, DEVERR_TIMEOUT, DEVERR_LAUNCH = 1, 2, 4, 8
+HQB_OK, HQB_ERR_INVALID, HQB_ERR_UNSUPPORTED = 0, 1, 801
 NOALLOC_SCRATCH_BYTES = 4 << 20
 ERR_SCRATCH_LIMIT = 20001
 
@@ -53,6 +54,12 @@ class RawStageF32(ctypes.Structure):
 class PlaneMatrixC(ctypes.Structure):
     _fields_ = [("rows", u64), ("cols", u64), ("grid_rows", u32), ("grid_cols", u32), ("stage_count", u32),
                 ("reserved", u32), ("planes", vp * MAX_STAGES)]
+
+
+class GemvCallC(ctypes.Structure):
+    _fields_ = [("m", vp), ("prefix", u32), ("x_dtype", i32), ("depth", vp), ("depth_plan", vp), ("x", vp),
+                ("batch", u32), ("x_prepared", i32), ("bias", vp), ("bias_dtype", i32), ("y_dtype", i32), ("y", vp),
+                ("flags", u32), ("reserved", u32)]
 
 
 class LaunchInfo(ctypes.Structure):
@@ -85,6 +92,10 @@ EXPORTS = {
     "hqb_gemv_ex": (i32, [ctypes.POINTER(PlaneMatrixC), u32, vp, vp, vp, i32, u32, i32, vp, i32, vp, i32, vp, u64,
                           u32, vp]),
     "hqb_gemv_noalloc": (i32, [ctypes.POINTER(PlaneMatrixC), u32, vp, i32, u32, vp, i32, vp, i32, vp]),
+    "hqb_gemv_batch": (i32, [ctypes.POINTER(GemvCallC), u32, vp, u64, vp]),
+    "hqb_step_create": (i32, [ctypes.POINTER(GemvCallC), u32, vp, u64, ctypes.POINTER(vp)]),
+    "hqb_step_launch": (i32, [vp, vp]),
+    "hqb_step_destroy": (i32, [vp]),
     "hqb_gemv_query": (i32, [ctypes.POINTER(PlaneMatrixC), u32, i32, i32, u32, i32, u32, ctypes.POINTER(LaunchInfo)]),
     "hqb_peer_alloc": (i32, [u64, ctypes.POINTER(vp), vp]),
     "hqb_peer_open": (i32, [vp, ctypes.POINTER(vp)]),
@@ -93,6 +104,10 @@ EXPORTS = {
     "hqb_gemv_gather": (i32, [ctypes.POINTER(PlaneMatrixC), u32, vp, i32, u32, vp, i32, i32, ctypes.POINTER(GatherC),
                               vp, u64, u32, vp]),
     "hqb_gather_wait": (i32, [vp, u32, vp, vp, vp]),
+    "hqb_gather_wait_ex": (i32, [vp, u32, vp, vp, u64, vp]),
+    "hqb_gemv_noalloc_flags": (i32, [ctypes.POINTER(i32), i32, vp]),
+    "hqb_gemv_noalloc_reset": (i32, [vp]),
+    "hqb_gemv_noalloc_scratch": (i32, [ctypes.POINTER(vp)]),
     "hqb_decode_planes": (i32, [ctypes.POINTER(PlaneMatrixC), u32, vp, vp, u64, vp]),
     "hqb_raw_gemv": (i32, [ctypes.POINTER(Geometry), ctypes.POINTER(RawStage), u32, u32, vp, u64, vp, u64, vp, u64,
                            vp]),
@@ -277,8 +292,14 @@ class PlaneMatrix:
         return m
 
     def c_struct(self) -> PlaneMatrixC:
-        arr = (vp * MAX_STAGES)(*[p.data_ptr() for p in self.planes], *([None] * (MAX_STAGES - len(self.planes))))
-        return PlaneMatrixC(self.rows, self.cols, self.grid_rows, self.grid_cols, self.stage_count, 0, arr)
+        """The C view of this matrix, built once per set of planes (kept while they are)."""
+        key = tuple(p.data_ptr() for p in self.planes)
+        cached = getattr(self, "_c", None)
+        if cached is None or cached[0] != key:
+            arr = (vp * MAX_STAGES)(*key, *([None] * (MAX_STAGES - len(key))))
+            cached = (key, PlaneMatrixC(self.rows, self.cols, self.grid_rows, self.grid_cols, len(key), 0, arr))
+            self._c = cached
+        return cached[1]
 
     def workspace_bytes(self, batch: int, x_dtype: int = F16) -> int:
         dev = self.device.index if self.device.index is not None else torch.cuda.current_device()
@@ -362,6 +383,53 @@ class PlaneMatrix:
         check(lib().hqb_decode_planes(ctypes.byref(self.c_struct()), prefix, _ptr(depth), _ptr(out), out.numel(),
                                       _stream(stream)), "hqb_decode_planes")
         return out
+
+
+class Step:
+    """A fixed list of GEMV calls (plane matrix, x, prefix, out, flags) on one stream with one
+    workspace: the decode step's GEMVs for one host call.  graph=True (default) captures them
+    once into a CUDA graph (hqb_step_create) and run() launches it; graph=False runs them
+    through hqb_gemv_batch.  Buffers are bound at construction; refill x and read out in
+    place."""
+
+    def __init__(self, calls, workspace: Workspace, graph: bool = True):
+        self.calls = list(calls)
+        self.handle = None
+        self.ws = workspace
+        arr = (GemvCallC * len(self.calls))()
+        self._keep = []
+        for i, (pm, x, prefix, out, flags) in enumerate(self.calls):
+            x = x if x.dim() == 2 else x.unsqueeze(0)
+            if not x.is_contiguous() or not out.is_contiguous():
+                raise ValueError("Step buffers must be contiguous")
+            ms = pm.c_struct()
+            self._keep.append(ms)
+            arr[i] = GemvCallC(ctypes.addressof(ms), prefix, _dtype_code(x), None, None, x.data_ptr(), x.shape[0], 0,
+                               None, F32, _dtype_code(out), out.data_ptr(), flags, 0)
+        self.arr = arr
+        if graph:
+            h = vp()
+            check(lib().hqb_step_create(arr, len(self.calls), self.ws.ptr(), self.ws.nbytes, ctypes.byref(h)),
+                  "hqb_step_create")
+            self.handle = h.value
+
+    def run(self, stream=None) -> None:
+        if self.handle is not None:
+            check(lib().hqb_step_launch(self.handle, _stream(stream)), "hqb_step_launch")
+        else:
+            check(lib().hqb_gemv_batch(self.arr, len(self.calls), self.ws.ptr(), self.ws.nbytes, _stream(stream)),
+                  "hqb_gemv_batch")
+
+    def close(self) -> None:
+        if self.handle is not None:
+            lib().hqb_step_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 class RawMatrix:

@@ -64,8 +64,8 @@ extern "C" {
 /* Batch <= 2 with raw FP16 or FP32 x, uniform prefix or depth map: the bulk-copy kernel
  * (plane chunks of ~40-52 KB moved into shared memory by 1-D bulk copies issued ahead of
  * the programmatic-dependent-launch wait, int8 activation limbs).  It is the default for
- * uniform layers of >= 96 MB of selected planes at prefix >= 2; this flag selects it for
- * any layer. */
+ * uniform layers of >= 128 tile columns and >= 96 MB of selected planes at prefix >= 2;
+ * this flag selects it for any layer. */
 #define HQB_FLAG_BULK 128u
 
 /* Fast-path tiling: 128x128 tiles, one scale group per tile row (group 128). */
@@ -233,6 +233,41 @@ typedef struct hqb_launch_info {
 HQB_API int hqb_gemv_query(const hqb_plane_matrix* m, uint32_t prefix, int mixed, int x_dtype, uint32_t batch,
                            int x_prepared, uint32_t flags, hqb_launch_info* info);
 
+/* One GEMV of a batch of calls: the arguments of hqb_gemv_ex. */
+typedef struct hqb_gemv_call {
+  const hqb_plane_matrix* m;
+  uint32_t prefix;
+  int x_dtype;
+  const uint8_t* depth;       /* NULL: uniform prefix */
+  const uint32_t* depth_plan; /* NULL: uniform prefix */
+  const void* x;
+  uint32_t batch;
+  int x_prepared;
+  const void* bias;
+  int bias_dtype;
+  int y_dtype;
+  void* y;
+  uint32_t flags;
+  uint32_t reserved;
+} hqb_gemv_call;
+
+/* The calls in order on one stream with one workspace (large enough for every call), one
+ * host call for a whole decode step: stops at the first call that fails and returns its
+ * status (the calls before it are enqueued).  No reference counterpart. */
+HQB_API int hqb_gemv_batch(const hqb_gemv_call* calls, uint32_t count, void* workspace, uint64_t workspace_bytes,
+                           void* stream);
+
+/* A decode step captured once: the calls of hqb_gemv_batch recorded into a CUDA graph
+ * (their programmatic-dependent launches kept as graph edges) and instantiated.  Launching
+ * it costs one graph launch on the host, whatever the number of GEMVs.  The buffers the
+ * calls name are bound into the graph: refill x and read y in place.  No reference
+ * counterpart. */
+typedef struct hqb_step hqb_step;
+HQB_API int hqb_step_create(const hqb_gemv_call* calls, uint32_t count, void* workspace, uint64_t workspace_bytes,
+                            hqb_step** step);
+HQB_API int hqb_step_launch(hqb_step* step, void* stream);
+HQB_API int hqb_step_destroy(hqb_step* step);
+
 /* ---- GEMV with a fixed scratch (no reference counterpart) --------------------------- */
 
 /* Size of the per-device scratch array built into the library for hqb_gemv_noalloc:
@@ -258,11 +293,25 @@ HQB_API int hqb_gemv_query(const hqb_plane_matrix* m, uint32_t prefix, int mixed
  *   read.
  * - One scratch per device: calls whose GPU work overlaps (other streams, other host
  *   threads) race on it.  Order them on one stream or with events.
- * - Device error bits land in the scratch's error word, which is not exposed; the
- *   status returned is that of the launches. */
+ * - Device error bits land in the scratch's error word: read them with
+ *   hqb_gemv_noalloc_flags.  After a non-zero word (a bounded wait that ran out, for
+ *   instance) the split-row counters and partial sums may not have returned to zero:
+ *   call hqb_gemv_noalloc_reset before the next call.
+ * - Every call checks the array's address on the current device (cudaGetSymbolAddress,
+ *   which allocates nothing); when it differs from the cached one (the module was loaded
+ *   again after cudaDeviceReset) the array is cleared again before use. */
 HQB_API int hqb_gemv_noalloc(const hqb_plane_matrix* m, uint32_t prefix, const void* x,
                              int x_dtype, uint32_t batch, const void* bias, int bias_dtype,
                              void* y, int y_dtype, void* stream);
+/* The scratch's device error word (HQB_DEVERR_* bits) of the current device copied to
+ * *host_flags after the work on `stream` (synchronises the stream); clear != 0 also sets
+ * the word back to zero.  Allocates nothing. */
+HQB_API int hqb_gemv_noalloc_flags(int* host_flags, int clear, void* stream);
+/* Enqueues a clear of the whole scratch array of the current device on `stream` (the state
+ * of the first call).  Allocates nothing. */
+HQB_API int hqb_gemv_noalloc_reset(void* stream);
+/* Device address of the current device's scratch array (*ptr), for inspection. */
+HQB_API int hqb_gemv_noalloc_scratch(void** ptr);
 
 /* ---- output-row shards across GPUs: fused all-gather over peer memory --------------- */
 
@@ -309,6 +358,11 @@ HQB_API int hqb_gemv_gather(const hqb_plane_matrix* m, uint32_t prefix, const vo
  * buffer. */
 HQB_API int hqb_gather_wait(const uint32_t* flags, uint32_t world, uint32_t* epoch, int* device_flags,
                             void* stream);
+/* The same with a caller-chosen bound in nanoseconds (at most the 2 s of hqb_gather_wait):
+ * a rank that has not signalled within it ends the wait with HQB_DEVERR_TIMEOUT set and the
+ * epoch advanced, and the stream goes on, so a host-side failure detector can act. */
+HQB_API int hqb_gather_wait_ex(const uint32_t* flags, uint32_t world, uint32_t* epoch, int* device_flags,
+                               uint64_t limit_ns, void* stream);
 
 /* Dense FP32 weights [rows][cols] decoded from planes, Σ_{s<d} code·scale summed in
  * stage order from 0.0f — bit-identical to DequantizePrefix

@@ -225,6 +225,21 @@ def stage_dense_np(m: Matrix, s: int) -> np.ndarray:
     return (codes * full)[:rows, :cols]
 
 
+def progressive_matmul_np(m: Matrix, x: np.ndarray, prefix: int, bias: np.ndarray | None = None) -> np.ndarray:
+    """NumPy restatement of the reference's ``progressive_matmul``
+    (src/harpq/quantization.py:352-406): each selected stage is decoded to dense FP32
+    (``dequantize_stage``) and multiplied on its own (BLAS), the stage outputs accumulated in
+    stage order into FP32 zeros, then the bias.  Test infrastructure and the NumPy CPU
+    baseline; not a product path."""
+    xs = np.asarray(x, np.float32).reshape(-1, m.cols)
+    out = np.zeros((xs.shape[0], m.rows), np.float32)
+    for s in range(prefix):
+        out += xs @ stage_dense_np(m, s).T
+    if bias is not None:
+        out += np.asarray(bias, np.float32)
+    return out
+
+
 def dequantize_prefix_np(m: Matrix, prefix: int, depth: np.ndarray | None = None) -> np.ndarray:
     """Vectorised twin of hqo_dequantize_prefix / hqo_dequantize_mixed."""
     g = m.geometry

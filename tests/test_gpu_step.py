@@ -1,0 +1,61 @@
+"""GPU: a decode step as one library call -- hqb_gemv_batch (eager) and hqb_step_* (the calls
+captured once into a CUDA graph) -- gives the bytes of the same GEMVs called one by one, and
+a captured step keeps working as its inputs are refilled in place."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+from conftest import plane_matrix, random_matrix  # noqa: E402
+
+
+def test_step_batch_and_graph_match_single_calls():
+    import harpq_b200 as hqb
+
+    rng = np.random.default_rng(2024)
+    shapes = [(768, 512), (300, 512), (1024, 1000), (200, 11008)]
+    pms = [plane_matrix(random_matrix(rng, r, c)) for r, c in shapes]
+    xs = [torch.from_numpy(rng.standard_normal((1, c)).astype(np.float16)).cuda() for _, c in shapes]
+    ys = [torch.empty(1, r, dtype=torch.float16, device="cuda") for r, _ in shapes]
+    ws = hqb.Workspace(max(pm.workspace_bytes(1, hqb.F16) for pm in pms))
+    prefixes = [1, 2, 3, 4]
+    ref = [pm.gemv(x, prefix=p, y_dtype=torch.float16, workspace=ws) for pm, x, p in zip(pms, xs, prefixes)]
+    calls = [(pm, x, p, y, hqb.FLAG_PDL) for pm, x, p, y in zip(pms, xs, prefixes, ys)]
+    for graph in (False, True):
+        step = hqb.Step(calls, ws, graph=graph)
+        for y in ys:
+            y.fill_(float("nan"))
+        step.run()
+        torch.cuda.synchronize()
+        for a, b in zip(ys, ref):
+            assert torch.equal(a, b), f"graph={graph}"
+        # inputs refilled in place: the captured step reads the new values
+        for x in xs:
+            x.mul_(-1)
+        step.run()
+        torch.cuda.synchronize()
+        for a, pm, x, p in zip(ys, pms, xs, prefixes):
+            assert torch.equal(a, pm.gemv(x, prefix=p, y_dtype=torch.float16, workspace=ws))
+        for x in xs:
+            x.mul_(-1)
+        step.close()
+    assert ws.error_flags() == 0
+
+
+def test_step_rejects_an_invalid_call_and_enqueues_nothing_after_it():
+    import harpq_b200 as hqb
+
+    rng = np.random.default_rng(3)
+    pm = plane_matrix(random_matrix(rng, 256, 256, stages=2))
+    x = torch.randn(1, 256, device="cuda").half()
+    y = torch.empty(1, 256, dtype=torch.float16, device="cuda")
+    ws = pm.workspace(1)
+    with pytest.raises(hqb.HQBError) as e:
+        hqb.Step([(pm, x, 3, y, 0)], ws)  # prefix 3 > stage count 2
+    assert e.value.status == hqb.HQB_ERR_INVALID
+    with pytest.raises(hqb.HQBError):
+        hqb.Step([(pm, x, 3, y, 0)], ws, graph=False).run()

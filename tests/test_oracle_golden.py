@@ -125,6 +125,16 @@ def test_seeded_fixture_linear_matches_reference_numpy(name):
 
 
 @pytest.mark.parametrize("name", SEEDED_NAMES)
+def test_numpy_matmul_restatement_matches_reference_outputs(name):
+    """progressive_matmul_np (the NumPy CPU baseline) against the reference's own
+    progressive_matmul outputs stored in the fixture (same decode, BLAS matmul per stage)."""
+    m, _, z = load_seeded(name)
+    for p in range(5):
+        y = orc.progressive_matmul_np(m, z["x"], p, z["bias"])
+        np.testing.assert_allclose(y, z["prefix_outputs"][p], rtol=1e-6, atol=1e-6)
+
+
+@pytest.mark.parametrize("name", SEEDED_NAMES)
 def test_numpy_encoder_restatement_is_byte_identical(name):
     _, payloads, z = load_seeded(name)
     q = qz.quantize(z["weights"])

@@ -120,3 +120,40 @@ def test_noalloc_invalid_arguments():
     assert L.hqb_gemv_noalloc(ctypes.byref(m), 3, _ptr(x), hqb.F16, 1, None, hqb.F32, _ptr(y), hqb.F32, s) == 1
     assert L.hqb_gemv_noalloc(ctypes.byref(m), 1, _ptr(x), hqb.F16, 0, None, hqb.F32, _ptr(y), hqb.F32, s) == 1
     assert L.hqb_gemv_noalloc(ctypes.byref(m), 1, _ptr(x), 7, 1, None, hqb.F32, _ptr(y), hqb.F32, s) == 1
+
+
+@pytest.mark.gpu
+def test_noalloc_error_word_read_clear_and_reset():
+    """The scratch's error word through the C ABI: a set bit is read back by
+    hqb_gemv_noalloc_flags (and cleared on request); hqb_gemv_noalloc_reset returns the whole
+    array to its first-call state, after which the GEMV matches hqb_gemv again."""
+    hqb, L = _lib()
+    rng = np.random.default_rng(404)
+    m = random_matrix(rng, 700, 900)
+    pm = plane_matrix(m)
+    x = torch.from_numpy(rng.standard_normal((1, m.cols)).astype(np.float16)).cuda()
+    stream = torch.cuda.current_stream().cuda_stream
+    ref, a, b = _both(pm, x, 3, None, torch.float32)
+    flags = ctypes.c_int(-1)
+    assert L.hqb_gemv_noalloc_flags(ctypes.byref(flags), 0, stream) == 0
+    assert flags.value == 0
+    # set the error word as a kernel would after a bounded wait ran out
+    addr = ctypes.c_void_p()
+    assert L.hqb_gemv_noalloc_scratch(ctypes.byref(addr)) == 0
+    word = torch.as_tensor(hqb._DeviceView(addr.value, (1,), "<i4"), device="cuda")
+    word.fill_(hqb.DEVERR_TIMEOUT)
+    torch.cuda.synchronize()
+    assert L.hqb_gemv_noalloc_flags(ctypes.byref(flags), 0, stream) == 0
+    assert flags.value == hqb.DEVERR_TIMEOUT
+    assert L.hqb_gemv_noalloc_flags(ctypes.byref(flags), 1, stream) == 0  # read and clear
+    assert flags.value == hqb.DEVERR_TIMEOUT
+    assert L.hqb_gemv_noalloc_flags(ctypes.byref(flags), 0, stream) == 0
+    assert flags.value == 0
+    # a damaged scratch (non-zero split-row words) is repaired by the reset
+    word.fill_(hqb.DEVERR_TIMEOUT)
+    assert L.hqb_gemv_noalloc_reset(stream) == 0
+    assert L.hqb_gemv_noalloc_flags(ctypes.byref(flags), 0, stream) == 0
+    assert flags.value == 0
+    ref2, a2, b2 = _both(pm, x, 3, None, torch.float32)
+    for got in (a, b, a2, b2):
+        _check(ref, got, torch.float32, "noalloc after reset")
