@@ -298,6 +298,8 @@ def run_ours(args, rank, world, device):
     # per step: the launches of each group's GEMV by the library's own dispatch rule (the
     # uniform kernel prepares its raw activations itself where they fit)
     launches_per_step = sum(g["copies"][0].gemv_launches(1, hqb.F16, prefix) + (1 if fused else 0) for g in groups)
+    if world == 1 and args.step_mode == "grouped":
+        launches_per_step = 1
 
     def gather(g):
         if world == 1:
@@ -354,28 +356,41 @@ def run_ours(args, rank, world, device):
     # synchronize on both sides and timed with CUDA events, the max over ranks taken per
     # repeat; the headline is the median repeat
     repeats = max(1, args.repeats)
-    rep_ms = []
-    t_timed0 = None
-    for _ in range(repeats):
-        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        barrier()
-        if t_timed0 is None:
-            t_timed0 = time.monotonic()
-        start.record()
-        for i in range(args.steps):
-            if use_graph:
-                graphs[i % ncopies].replay()
-            else:
-                step(i % ncopies)
-        end.record()
-        barrier()
-        ms = start.elapsed_time(end)
-        if world > 1:
-            t = torch.tensor([ms], device=device)
-            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-            ms = float(t.item())
-        rep_ms.append(ms / args.steps)
+
+    def time_steps(run_one):
+        out = []
+        for _ in range(repeats):
+            start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            barrier()
+            start.record()
+            for i in range(args.steps):
+                run_one(i)
+            end.record()
+            barrier()
+            ms = start.elapsed_time(end)
+            if world > 1:
+                t = torch.tensor([ms], device=device)
+                torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+                ms = float(t.item())
+            out.append(ms / args.steps)
+        return out
+
+    # the step's GEMVs as one grouped launch (hqb_gemv_grouped: the workload's layers take
+    # inputs of their own, so they are independent) -- N = 1 only, the all-gathers of N > 1
+    # sit between the launches
+    grouped = world == 1 and args.step_mode == "grouped"
+    gsteps = []
+    if grouped:
+        gsteps = [hqb.Step([(G["copies"][c], x_dev[G["src"]], prefix, y_loc[G["name"]], hqb.FLAG_PDL)
+                            for G in groups], ws, graph=True, independent=True) for c in range(ncopies)]
+        for i in range(3):
+            gsteps[i % ncopies].run()
+        torch.cuda.synchronize()
+    t_timed0 = time.monotonic()
+    chained_ms = time_steps(lambda i: graphs[i % ncopies].replay() if use_graph else step(i % ncopies))
+    grouped_ms = time_steps(lambda i: gsteps[i % ncopies].run()) if grouped else None
     t_timed1 = time.monotonic()
+    rep_ms = grouped_ms if grouped else chained_ms
     ms_per_step = statistics.median(rep_ms)
     # whole-job bytes: the full (unsharded) layers, each input once per group
     total_bytes = sum(group_bytes([{"nrows": m["rows"]} for m in g["members"]], g["cols"], prefix) for g in groups)
@@ -421,6 +436,10 @@ def run_ours(args, rank, world, device):
         by_kernel[kname][1] += per_launch_ms
         tot_b += b
         tot_ms += per_launch_ms
+    if grouped:
+        # one kernel per step: its launches back to back (the grouped step graph) are the step
+        by_kernel = {"gemv_grouped_kernel": [sum(G["bytes"] for G in groups), ms_per_step]}
+        tot_ms = ms_per_step
     # the roofline line is the kernel with the most device time; every kernel's share is listed
     dominant = max(by_kernel, key=lambda k: by_kernel[k][1])
     dom_b, dom_ms = by_kernel[dominant]
@@ -473,8 +492,9 @@ def run_ours(args, rank, world, device):
 
     if world == 1:
         host_y_all = torch.empty_like(y_all, device="cpu").pin_memory()
-        steps_api = [hqb.Step([(G["copies"][c], x_dev[G["src"]], prefix, y_loc[G["name"]], hqb.FLAG_PDL)
-                               for G in groups], ws) for c in range(ncopies)]
+        steps_api = gsteps if grouped else [
+            hqb.Step([(G["copies"][c], x_dev[G["src"]], prefix, y_loc[G["name"]], hqb.FLAG_PDL) for G in groups], ws)
+            for c in range(ncopies)]
         host_y = {"all": host_y_all}
     else:
         host_y = {g["name"]: torch.empty_like(gathered(g, 0), device="cpu").pin_memory() for g in groups}
@@ -538,7 +558,8 @@ def run_ours(args, rank, world, device):
         "config": {"workload": name, "prefix": prefix, "batch": 1,
                    "layers": [[m["name"], m["rows"], g["cols"]] for g in groups for m in g["members"]],
                    "launches": [[g["name"], g["nrows"], g["cols"]] for g in groups],
-                   "grouping": "layers sharing an input run as one row-stacked launch",
+                   "grouping": "layers sharing an input run as one row-stacked launch; step_mode grouped: "
+                               "the launch groups (independent inputs) run as one grouped kernel launch",
                    "parallelism": (f"row-shard{world}+" + ("fused-p2p-allgather" if fused else "nccl-allgather"))
                                   if world > 1 else "single",
                    "l2": f"{ncopies} rotating weight copies, {ncopies * step_bytes / 2**20:.0f} MiB > 3x L2",
@@ -551,6 +572,12 @@ def run_ours(args, rank, world, device):
         "timing": {"repeats": repeats, "steps_per_repeat": args.steps,
                    "ms_per_step": [round(v, 5) for v in rep_ms], "median_ms": round(ms_per_step, 5),
                    "min_ms": round(min(rep_ms), 5), "max_ms": round(max(rep_ms), 5)},
+        "step_mode": "grouped" if grouped else "chained",
+        # the same step as dependent launches (one launch per layer group, PDL between them,
+        # as a decoder block whose layers wait for each other runs)
+        "chained": {"value": round(total_bytes / (statistics.median(chained_ms) * 1e-3) / 1e9, 1),
+                    "ms_per_step": round(statistics.median(chained_ms), 5),
+                    "launches_per_step": sum(g["copies"][0].gemv_launches(1, hqb.F16, prefix) for g in groups)},
         "clocks": clk.summary(t_timed0, t_timed1),
         "device_error_flags": flags | gather_flags,
     }
@@ -570,8 +597,8 @@ def run_ours(args, rank, world, device):
     result["roofline"] = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                           "frac": round(achieved / peak, 4),
                           "peak_source": "measured" if "hbm_gbs" in peaks else "fallback",
-                          "traffic": None if traffic is None else round(traffic * dom_b / len(
-                              [g for g in kern.values() if g["kernel"] == dominant])),
+                          "traffic": None if traffic is None else round(traffic * dom_b / max(1, len(
+                              [g for g in kern.values() if g["kernel"] == dominant]))),
                           "kernel": f"hqb::{dominant} (activation preparation and split-row sums inside)",
                           "achieved_note": "algorithmic bytes of one launch per group run by this kernel / sum of "
                                            "those groups' average launch durations (CUDA events around graphs of "
@@ -887,6 +914,8 @@ def main(argv=None) -> int:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extras", action="store_true", help="skip the supplementary single-GPU measurements")
     ap.add_argument("--repeats", type=int, default=5, help="timed regions of --steps steps (median reported)")
+    ap.add_argument("--step-mode", choices=["grouped", "chained"], default="grouped",
+                    help="N = 1: the step's independent GEMVs as one grouped launch, or one launch per group")
     ap.add_argument("--fused-gather", action="store_true",
                     help="N > 1: gather outputs with the fused P2P gather instead of NCCL all_gather_into_tensor")
     args = ap.parse_args(argv)

@@ -1,7 +1,8 @@
 // C++17 API of the reference (harpq::native_runtime) implemented over this library's
 // C ABI.  Validation order, messages' meaning and exception types follow the
 // reference so its callers and tests behave the same; the arithmetic runs on the
-// device through the sm_100a kernels.
+// device through the sm_100a kernels (the reference's three host functions fall back
+// to host loops of the same operations when no device is usable).
 //
 //   stage codec    reference native/src/stage_codec.cpp:80-339
 //   fused GEMV     reference native/src/progressive_gemv.cu:73-541
@@ -192,6 +193,80 @@ std::vector<float> Download(const DeviceArray<float>& d, std::size_t n, cudaStre
   return out;
 }
 
+// ---- host forms of the reference's host functions ----------------------------------------
+//
+// DequantizeStage, DequantizePrefix and ProgressiveLinearReference are host functions in
+// the reference (stage_codec.cpp:225-339), callable without a GPU.  With a usable device
+// they run as raw_dequantize_kernel / raw_linear_ordered_kernel; without one, as the loops
+// below, which take the same FP32 operations in the same order (each product and sum
+// rounded on its own; this file is compiled with -ffp-contract=off), so both give the
+// same bits.  The GEMV entry points have no host form.
+
+bool DeviceUsable() {
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess) {
+    static_cast<void>(cudaGetLastError());
+    return false;
+  }
+  return n > 0;
+}
+
+int HostCode(const std::vector<std::uint8_t>& codes, std::size_t index) {
+  const unsigned raw = (codes[index >> 2] >> (2 * (index & 3))) & 3u;
+  return raw >= 2 ? static_cast<int>(raw) - 4 : static_cast<int>(raw);
+}
+
+std::size_t HostScaleIndex(const MatrixGeometry& g, std::size_t row, std::size_t col) {
+  const std::size_t grid_cols = g.padded_columns / g.tile_columns;
+  const std::size_t tr = row / g.tile_rows, rit = row % g.tile_rows;
+  const std::size_t tc = col / g.tile_columns, cit = col % g.tile_columns;
+  return ((tr * grid_cols + tc) * g.tile_rows + rit) * (g.tile_columns / g.group_size) + cit / g.group_size;
+}
+
+// Stages [first, last): the bare product for one stage, else the products added in
+// stage order into 0.0f.
+std::vector<float> HostDequantize(const ProgressiveMatrix& m, std::size_t first, std::size_t last, bool from_zero) {
+  const MatrixGeometry& g = m.geometry;
+  std::vector<float> out(g.original_rows * g.original_columns);
+  for (std::size_t row = 0; row < g.original_rows; ++row)
+    for (std::size_t col = 0; col < g.original_columns; ++col) {
+      const std::size_t ci = row * g.padded_columns + col, si = HostScaleIndex(g, row, col);
+      float w = 0.0f;
+      for (std::size_t s = first; s < last; ++s) {
+        const float prod = static_cast<float>(HostCode(m.stages[s].packed_codes, ci)) * m.stages[s].scales[si];
+        w = (s == first && !from_zero) ? prod : w + prod;
+      }
+      out[row * g.original_columns + col] = w;
+    }
+  return out;
+}
+
+// Per (batch, row): per stage a fresh dot summed column by column, added into the
+// output; bias last.
+std::vector<float> HostLinearOrdered(const ProgressiveMatrix& m, std::size_t prefix, const std::vector<float>& x,
+                                     std::size_t batch, const std::vector<float>& bias) {
+  const MatrixGeometry& g = m.geometry;
+  std::vector<float> y(batch * g.original_rows);
+  for (std::size_t b = 0; b < batch; ++b)
+    for (std::size_t row = 0; row < g.original_rows; ++row) {
+      const float* xb = x.data() + b * g.original_columns;
+      float out = 0.0f;
+      for (std::size_t s = 0; s < prefix; ++s) {
+        float dot = 0.0f;
+        for (std::size_t col = 0; col < g.original_columns; ++col) {
+          const float w = static_cast<float>(HostCode(m.stages[s].packed_codes, row * g.padded_columns + col)) *
+                          m.stages[s].scales[HostScaleIndex(g, row, col)];
+          const float p = xb[col] * w;
+          dot = dot + p;
+        }
+        out = out + dot;
+      }
+      if (!bias.empty()) out = out + bias[row];
+      y[b * g.original_rows + row] = out;
+    }
+  return y;
+}
+
 // ---- fused GEMV host validation (reference progressive_gemv.cu:73-183) ------------------
 
 struct HostGeometry {
@@ -342,6 +417,7 @@ std::vector<float> DequantizeStage(const ProgressiveMatrix& matrix, std::size_t 
   ValidateCodecMatrix(matrix);
   if (stage_index >= matrix.stages.size()) throw StageCodecError("stage_index is outside the available prefix");
   const std::size_t n = Mul<StageCodecError>(matrix.geometry.original_rows, matrix.geometry.original_columns, "output element count");
+  if (!DeviceUsable()) return HostDequantize(matrix, stage_index, stage_index + 1, false);
   DeviceArray<float> out(n);
   Stream s;
   DeviceStagesF32 st(matrix, stage_index + 1, s.get());
@@ -356,6 +432,7 @@ std::vector<float> DequantizePrefix(const ProgressiveMatrix& matrix, std::size_t
   ValidateCodecMatrix(matrix);
   if (prefix > matrix.stages.size()) throw StageCodecError("prefix exceeds the available stage count");
   const std::size_t n = Mul<StageCodecError>(matrix.geometry.original_rows, matrix.geometry.original_columns, "output element count");
+  if (!DeviceUsable()) return HostDequantize(matrix, 0, prefix, true);
   DeviceArray<float> out(n);
   Stream s;
   DeviceStagesF32 st(matrix, prefix, s.get());
@@ -381,6 +458,7 @@ std::vector<float> ProgressiveLinearReference(const std::vector<float>& inputs, 
     if (!std::isfinite(v)) throw StageCodecError("inputs and bias must be finite");
   const std::size_t n = Mul<StageCodecError>(batch_size, g.original_rows, "linear output element count");
   if (n == 0) return {};
+  if (!DeviceUsable()) return HostLinearOrdered(matrix, prefix, inputs, batch_size, bias);
   Stream s;
   DeviceArray<float> x(inputs.size()), b(bias.size()), y(n);
   Upload(x, inputs, s.get(), "cudaMemcpyAsync(inputs H2D)");

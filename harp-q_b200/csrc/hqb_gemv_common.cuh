@@ -216,12 +216,22 @@ __device__ __forceinline__ void prep_i8_items(const float (&v)[W][4], const bool
   for (int o = 16; o > 0; o >>= 1)
 #pragma unroll
     for (int w = 0; w < W; ++w) a[w] = fmaxf(a[w], __shfl_xor_sync(0xffffffffu, a[w], o));
+  // A tile holding a NaN or an Inf, or a value of 2^100 or more (beyond this form's limb
+  // factors), gets NaN constants: every output of its batch row is NaN rather than wrong.
+  // (The bulk kernel's limb_item keeps such finite values exact.)
+  bool bad[W];
+#pragma unroll
+  for (int w = 0; w < W; ++w) {
+    const bool lane_bad = !(isfinite(v[w][0]) && isfinite(v[w][1]) && isfinite(v[w][2]) && isfinite(v[w][3])) ||
+                          a[w] >= 1.2676506e30f;  // 2^100
+    bad[w] = __any_sync(0xffffffffu, lane_bad);
+  }
   int E[W], sum[W][kLimbs];
 #pragma unroll
   for (int w = 0; w < W; ++w) {
     // a < 2^E: the biased exponent field of a normal float gives floor(log2 a); the
     // clamp keeps every limb factor 2^(E-6-8l) a normal float
-    E[w] = a[w] > 0.0f ? max(-90, min(100, ((__float_as_int(a[w]) >> 23) & 0xff) - 126)) : 0;
+    E[w] = a[w] > 0.0f && !bad[w] ? max(-90, min(100, ((__float_as_int(a[w]) >> 23) & 0xff) - 126)) : 0;
     // column 4L + t: quad position L/8, half (L%8)/4, byte L%4 of word 2t + half
     uint8_t* base = slot[w] + (lane >> 3) * 32 + (lane & 7);
 #pragma unroll
@@ -258,8 +268,8 @@ __device__ __forceinline__ void prep_i8_items(const float (&v)[W][4], const bool
       for (int l = 0; l < static_cast<int>(kLimbs); ++l) {
         const uint32_t n = 2 * l + b[w];
         const float L = exp2_int(E[w] - 6 - 8 * l);
-        cst[2 * n] = L;
-        cst[2 * n + 1] = -(kAccBias + static_cast<float>(2 * sum[w][l])) * L;
+        cst[2 * n] = bad[w] ? __uint_as_float(0x7fc00000u) : L;
+        cst[2 * n + 1] = bad[w] ? __uint_as_float(0x7fc00000u) : -(kAccBias + static_cast<float>(2 * sum[w][l])) * L;
       }
       if (b[w] == 0) {
         for (uint32_t n = 0; n < 8; ++n)
@@ -852,6 +862,161 @@ __device__ __forceinline__ MixedRange mixed_range(const GemvParams& p, uint32_t 
   m.t_end = r1 * p.C + c1;
   m.s_end = s1 + 1;
   return m;
+}
+
+// ---- int8-limb tile step from zero-started chains (bulk and lean stream-K kernels) ----
+
+// D = A·B, m16n8k32 u8 x s8 -> s32, accumulator from zero.
+__device__ __forceinline__ void mma_u8s8_z(uint32_t (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                           uint32_t b0, uint32_t b1) {
+  asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%10,%10,%10,%10};"
+      : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0u));
+}
+
+// Integer tensor-core part of one tile: per stage 4 MMAs m16n8k32, MMA m fed by the code
+// words ANDed with 0x03030303 << 2m.  D independent chains from zero (two for D == 1).
+template <int D, bool MX>
+__device__ __forceinline__ void bulk_tile_mma(const uint4 (&w)[D], const XFragI8& xf,
+                                              uint32_t (&acc)[TileChains<D>::value][4], uint32_t live) {
+#pragma unroll
+  for (int m = 0; m < 4; ++m) {
+    const uint32_t mask = 0x03030303u << (2 * m);
+#pragma unroll
+    for (int s = 0; s < D; ++s) {
+      if (MX && !((live >> s) & 1u)) continue;  // warp-uniform: a stage the tile does not select
+      const int c = D == 1 ? (m & 1) : s;
+      const uint32_t a0 = w[s].x & mask, a1 = w[s].y & mask, a2 = w[s].z & mask, a3 = w[s].w & mask;
+      if (D == 1 ? m < 2 : m == 0)
+        mma_u8s8_z(acc[c], a0, a1, a2, a3, xf.bf[m][0], xf.bf[m][1]);
+      else
+        mma_u8s8(acc[c], a0, a1, a2, a3, xf.bf[m][0], xf.bf[m][1]);
+    }
+  }
+}
+
+// y += σ·Σcode·Y·L per stage.  The integer sum S reads as the FP32 1.5·2^23 + S once the
+// bits of 1.5·2^23 are added (|S| < 2^21), so one FMA with the slot's {L, K} gives the
+// exact limb sum and one more applies the row's scale -- the arithmetic of the seeded
+// chains of the register-ring kernels, bit for bit.
+template <int D, bool B1, bool MX>
+__device__ __forceinline__ void bulk_tile_epilogue(const uint32_t (&sc)[D], const XFragI8& xf,
+                                                   uint32_t (&acc)[TileChains<D>::value][4], float (&y)[1][4],
+                                                   uint32_t live) {
+  if (D == 1) {
+    acc[0][0] += acc[1][0];
+    acc[0][2] += acc[1][2];
+    if (!B1) {
+      acc[0][1] += acc[1][1];
+      acc[0][3] += acc[1][3];
+    }
+  }
+#pragma unroll
+  for (int s = 0; s < D; ++s) {
+    if (MX && !((live >> s) & 1u)) continue;
+    const __half2 s2 = *reinterpret_cast<const __half2*>(&sc[s]);
+    const float s_lo = __low2float(s2), s_hi = __high2float(s2);
+    y[0][0] = fmaf(s_lo, fmaf(__uint_as_float(acc[s][0] + kAccBiasBits), xf.L[0], xf.K[0]), y[0][0]);
+    y[0][2] = fmaf(s_hi, fmaf(__uint_as_float(acc[s][2] + kAccBiasBits), xf.L[0], xf.K[0]), y[0][2]);
+    if (!B1) {
+      y[0][1] = fmaf(s_lo, fmaf(__uint_as_float(acc[s][1] + kAccBiasBits), xf.L[1], xf.K[1]), y[0][1]);
+      y[0][3] = fmaf(s_hi, fmaf(__uint_as_float(acc[s][3] + kAccBiasBits), xf.L[1], xf.K[1]), y[0][3]);
+    }
+  }
+}
+
+// Limb slots of the tile columns a CTA touches, built from raw x by WARPS warps.  Every
+// CTA reads the same few KB of x at once, so the reads are L2-slice bound: each lane loads
+// four consecutive activations (one 8- or 16-byte load, no sector read twice), a per-warp
+// 512-byte shared-memory area turns them into limb_item's column order, and up to four
+// items per warp are loaded before any is transformed.
+template <int XL, uint32_t WARPS>
+__device__ __forceinline__ void build_limb_slots(const GemvParams& p, uint8_t* xres, float* scratch,
+                                                 const ColRanges& cr, uint32_t c_first, uint32_t warp, uint32_t lane) {
+  using XT = typename std::conditional<XL == 1, __half, float>::type;
+  const XT* x = static_cast<const XT*>(p.x_raw);
+  const uint32_t items = cr.count() * p.batch;
+  const uint32_t q = lane >> 3, m = (lane >> 1) & 3u, h = lane & 1u;
+  const uint32_t col_lane = 32u * q + 16u * h + m;  // limb_item's columns: col_lane + 4j
+  constexpr uint32_t W = 4;
+  for (uint32_t base = warp; base < items; base += W * WARPS) {
+    float v4[W][4];
+    uint32_t c[W], b[W];
+#pragma unroll
+    for (uint32_t w = 0; w < W; ++w) {
+      const uint32_t it = base + w * WARPS;
+      const uint32_t ci = it < items ? it / p.batch : 0u;
+      b[w] = it < items ? it - ci * p.batch : 0u;
+      c[w] = cr.col(ci);
+      if (it < items)
+        load_x4<XT>(x + static_cast<uint64_t>(b[w]) * p.cols, c[w] * 128 + 4 * lane, p.cols, p.x_vec != 0, v4[w]);
+    }
+#pragma unroll
+    for (uint32_t w = 0; w < W; ++w) {
+      if (base + w * WARPS >= items) break;
+      *reinterpret_cast<float4*>(scratch + 4 * lane) = make_float4(v4[w][0], v4[w][1], v4[w][2], v4[w][3]);
+      __syncwarp();
+      float v[4];
+#pragma unroll
+      for (int jj = 0; jj < 4; ++jj) v[jj] = scratch[col_lane + 4 * jj];
+      __syncwarp();
+      limb_item(v, xres + resident_slot(c[w], c_first, p.C) * p.xslot_bytes, b[w], p.batch, lane);
+    }
+  }
+}
+
+// The same for a tile with a batch row whose limb slot is marked wide (K >= 0, see
+// limb_item): such a row's K holds -K and its stage sums are multiplied by its wide factor
+// (1.0 for the other row); NaN constants (a non-finite activation) give NaN.
+template <int D, bool B1, bool MX>
+__device__ __forceinline__ void bulk_tile_epilogue_wide(const uint32_t (&sc)[D], const XFragI8& xf,
+                                                        uint32_t (&acc)[TileChains<D>::value][4], float (&y)[1][4],
+                                                        uint32_t live, float f0, float f1) {
+  if (D == 1) {
+#pragma unroll
+    for (int e = 0; e < 4; ++e) acc[0][e] += acc[1][e];
+  }
+  // a wide row's K is stored negated (>= 0); NaN stays NaN
+  const float k0 = xf.K[0] >= 0.0f ? -xf.K[0] : xf.K[0], k1 = xf.K[1] >= 0.0f ? -xf.K[1] : xf.K[1];
+#pragma unroll
+  for (int s = 0; s < D; ++s) {
+    if (MX && !((live >> s) & 1u)) continue;
+    const __half2 s2 = *reinterpret_cast<const __half2*>(&sc[s]);
+    const float s_lo = __low2float(s2), s_hi = __high2float(s2);
+    y[0][0] = fmaf(s_lo * f0, fmaf(__uint_as_float(acc[s][0] + kAccBiasBits), xf.L[0], k0), y[0][0]);
+    y[0][2] = fmaf(s_hi * f0, fmaf(__uint_as_float(acc[s][2] + kAccBiasBits), xf.L[0], k0), y[0][2]);
+    if (!B1) {
+      y[0][1] = fmaf(s_lo * f1, fmaf(__uint_as_float(acc[s][1] + kAccBiasBits), xf.L[1], k1), y[0][1]);
+      y[0][3] = fmaf(s_hi * f1, fmaf(__uint_as_float(acc[s][3] + kAccBiasBits), xf.L[1], k1), y[0][3]);
+    }
+  }
+}
+
+// This lane's limb fragments and {L, K} from a slot at shared address `a` (XLaneI8 offsets).
+template <bool B1>
+__device__ __forceinline__ void load_limbs(XFragI8& xf, uint32_t frag_a, uint32_t cst_a) {
+  const uint4 t0 = lds128a(frag_a), t1 = lds128a(frag_a + 16);
+  xf.bf[0][0] = t0.x;
+  xf.bf[0][1] = t0.y;
+  xf.bf[1][0] = t0.z;
+  xf.bf[1][1] = t0.w;
+  xf.bf[2][0] = t1.x;
+  xf.bf[2][1] = t1.y;
+  xf.bf[3][0] = t1.z;
+  xf.bf[3][1] = t1.w;
+  if (B1) {
+    const uint2 c = lds64a(cst_a);
+    xf.L[0] = __uint_as_float(c.x);
+    xf.K[0] = __uint_as_float(c.y);
+    xf.L[1] = xf.K[1] = 0.0f;
+  } else {
+    const uint4 c = lds128a(cst_a);
+    xf.L[0] = __uint_as_float(c.x);
+    xf.K[0] = __uint_as_float(c.y);
+    xf.L[1] = __uint_as_float(c.z);
+    xf.K[1] = __uint_as_float(c.w);
+  }
 }
 
 using GemvKernel = void (*)(GemvParams);

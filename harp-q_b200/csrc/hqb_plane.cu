@@ -955,15 +955,16 @@ __device__ __forceinline__ void build_xfrag_tiles_i8(const GemvParams& p, uint8_
 }
 
 
+// The stream-K kernel's work as CTA `cta` of a grid of `grid` CTAs on problem p (the kernel
+// below, and one problem of a grouped launch).
 template <int NB, int XL, int D, bool B1 = false, bool I8 = false, bool MX = false>
-__global__ void __launch_bounds__(kStreamThreads, (NB == 1 && (XL == 1 || I8)) ? 2 : 1)
-    gemv_uniform_kernel(const __grid_constant__ GemvParams p) {
+__device__ __forceinline__ void uniform_body(const GemvParams& p, const uint32_t cta, const uint32_t grid) {
   static_assert(!I8 || NB == 1, "the int8 limb path takes batch <= 2");
   static_assert(!MX || (I8 && D == HQB_MAX_STAGES), "depth maps run on the int8 path at depth 4");
   constexpr int R = TilesAhead<D>::value;
   constexpr uint32_t kFull = (1u << D) - 1u;
   extern __shared__ __align__(16) uint8_t xres[];  // [resident activation slots]
-  const uint32_t cta = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, q = lane & 3;
+  const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, q = lane & 3;
   // The CTA's units [u0, u1): tiles t0..t_end, the first from stage s0, the last up to
   // stage s_end; rb_first / re_last: first unit of t0's tile row, end of t_end's.
   MixedRange rg{};
@@ -971,7 +972,7 @@ __global__ void __launch_bounds__(kStreamThreads, (NB == 1 && (XL == 1 || I8)) ?
     rg = mixed_range(p, cta, lane);
   } else {
     rg.total = p.total;
-    rg.ctas = static_cast<uint32_t>(rg.total < gridDim.x ? rg.total : gridDim.x);
+    rg.ctas = static_cast<uint32_t>(rg.total < grid ? rg.total : grid);
     if (cta < rg.ctas) {
       rg.u0 = unit_start(cta, rg.total, rg.ctas);
       rg.u1 = unit_start(cta + 1, rg.total, rg.ctas);
@@ -1156,6 +1157,244 @@ __global__ void __launch_bounds__(kStreamThreads, (NB == 1 && (XL == 1 || I8)) ?
   }
   if (keep) reduce_split_row<NB, B1>(p, row_first, rg.rb_first, total, ctas, cta, kept, rit0, q);
   if (p.g_world > 1) gather_signal(p, ctas);
+}
+
+// The stream-K kernel's int8-limb form at a uniform prefix, written for the fewest
+// instructions per (row block, stage) task: the same partition, descending walk, register
+// ring, split-row scheme and arithmetic as uniform_body, with
+//   * the steady-state loop over whole groups of R tiles whose refills are interior tiles:
+//     every refill loads all D stage records with no mask and no bound test;
+//   * the CTA's two edge tiles (partial stage ranges) loaded with masks, outside that loop;
+//   * MMA chains from zero (the 1.5·2^23 bias added in the epilogue), limb slots at 32-bit
+//     shared addresses, and limb slots built by limb_item (so activations up to the FP32
+//     maximum keep the contract, and a NaN or Inf gives NaN outputs).
+// Shared memory: the resident limb slots, then a 512-byte transpose area per warp.
+template <int XL, int D, bool B1>
+__device__ __forceinline__ void lean_body(const GemvParams& p, const uint32_t cta, const uint32_t grid) {
+  constexpr int R = TilesAhead<D>::value;
+  constexpr uint32_t kFull = (1u << D) - 1u;
+  constexpr int CH = TileChains<D>::value;
+  constexpr uint32_t XS = kLimbs * (B1 ? 1u : 2u) * 128u + 80u;  // xslot_i8_bytes(batch)
+  constexpr uint32_t kWideOff = kLimbs * (B1 ? 1u : 2u) * 128u + 64u;
+  extern __shared__ __align__(16) uint8_t xres[];
+  const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, q = lane & 3;
+  const uint64_t total = p.total;
+  const uint32_t ctas = static_cast<uint32_t>(total < grid ? total : grid);
+  griddep_launch_dependents();  // a following PDL kernel may be scheduled; it waits for this grid
+  if (cta >= ctas) return;
+  uint64_t u0, u1;
+  if (total * (ctas + 1ull) <= 0xffffffffull) {  // 32-bit divisions (the usual case)
+    const uint32_t T = static_cast<uint32_t>(total);
+    u0 = (cta * T) / ctas;
+    u1 = ((cta + 1) * T) / ctas;
+  } else {
+    u0 = unit_start(cta, total, ctas);
+    u1 = unit_start(cta + 1, total, ctas);
+  }
+  const uint32_t C = p.C;
+  const uint32_t t0 = static_cast<uint32_t>(u0 / D), s0 = static_cast<uint32_t>(u0 % D);
+  const uint32_t t_end = static_cast<uint32_t>((u1 - 1) / D), s_end = static_cast<uint32_t>((u1 - 1) % D) + 1;
+  const uint32_t row_first = t0 / C, row_last = t_end / C;
+  const uint64_t rb_first = static_cast<uint64_t>(row_first) * C * D;
+  const uint64_t re_last = static_cast<uint64_t>(row_last + 1) * C * D;
+  const uint32_t ntiles = t_end - t0 + 1;
+  const uint32_t mask_first = kFull & ~((1u << s0) - 1u), mask_last = (1u << s_end) - 1u;
+  const uint32_t rit0 = warp * 16 + g;
+
+  // Records of walk tile k (tile t_end - k) for this lane: cb[s] - k * 4352 (codes), the
+  // scale pair scale_rel bytes further.  cur[s] points at the first tile the next group's
+  // refills load (walk tile k0 + R), so refill j of a group is cur[s] - j * 4352.
+  const uint32_t lane_off = warp * kRowBlockBytes + lane * 16;
+  const uint32_t scale_rel = 512 + g * 4 - lane * 16;
+  const uint64_t l2_first = policy_evict_first();
+  const uint8_t* base[D];
+#pragma unroll
+  for (int s = 0; s < D; ++s) base[s] = p.planes[s] + static_cast<uint64_t>(t_end) * kRecordBytes + lane_off;
+  uint4 w[R][D];
+  uint32_t sc[R][D];
+  // walk tile k into ring slot `slot`; stages outside `mask` are not loaded and read as
+  // scale 0 with codes 0 (their products are exactly zero)
+  auto load_masked = [&](int slot, uint32_t k, uint32_t mask) {
+#pragma unroll
+    for (int s = 0; s < D; ++s) {
+      if (mask & (1u << s)) {
+        const uint8_t* a = base[s] - static_cast<uint64_t>(k) * kRecordBytes;
+        ld_plane(w[slot][s], sc[slot][s], a, a + scale_rel, l2_first);
+      } else {
+        w[slot][s] = make_uint4(0u, 0u, 0u, 0u);
+        sc[slot][s] = 0u;
+      }
+    }
+  };
+  auto edge_mask = [&](uint32_t k) -> uint32_t {
+    uint32_t m = kFull;
+    if (k == 0) m &= mask_last;
+    if (k == ntiles - 1) m &= mask_first;
+    return m;
+  };
+#pragma unroll
+  for (int j = 0; j < R; ++j)
+    if (static_cast<uint32_t>(j) < ntiles) load_masked(j, j, edge_mask(j));
+  griddep_wait();
+  const uint32_t c_first = t0 % C;
+  if (min(C, ntiles) > p.x_res_slots) {  // the launch sized shared memory for fewer slots
+    if (threadIdx.x == 0) atomicOr(p.error, HQB_DEVERR_LAUNCH);
+    return;
+  }
+  {
+    const ColRanges cr = needed_columns(t0, t_end, C);
+    if (p.x_raw != nullptr) {
+      build_limb_slots<XL, kStreamThreads / 32>(p, xres,
+                                                reinterpret_cast<float*>(xres + p.x_res_slots * XS) + warp * 128, cr,
+                                                c_first, warp, lane);
+    } else {  // slots prepared by one launch for all CTAs (prep_limbs_kernel)
+      constexpr uint32_t per_slot = XS / 16;
+      const uint32_t chunks = cr.count() * per_slot;
+      for (uint32_t t = threadIdx.x; t < chunks; t += kStreamThreads) {
+        const uint32_t ci = t / per_slot, k = t - ci * per_slot, c = cr.col(ci);
+        const uint4* src = reinterpret_cast<const uint4*>(p.xfrag + static_cast<uint64_t>(c) * XS) + k;
+        reinterpret_cast<uint4*>(xres + resident_slot(c, c_first, C) * XS)[k] = __ldcg(src);
+      }
+    }
+  }
+  __syncthreads();
+
+  const XLaneI8 xl8(B1 ? 1u : 2u, lane);
+  const uint32_t xres_a = smem_u32(xres);
+  const uint32_t x_top = (C - 1) * XS;
+  uint32_t xoff = resident_slot(t_end % C, c_first, C) * XS;  // limb slot of the current tile
+  uint32_t row = t_end / C;
+  uint32_t left = t_end % C + 1;  // tiles of the current row still ahead (may run past ntiles)
+  float y[1][4] = {{0.0f, 0.0f, 0.0f, 0.0f}};
+  float kept[1][4];
+  bool keep = false;
+
+  // Tiles whose limb slot is wide or non-finite (limb_item marks them with K >= 0 or NaN)
+  // need the slower epilogue; a CTA without any runs the hot loop without that branch.
+  bool any_wide = false;
+  {
+    const ColRanges cr = needed_columns(t0, t_end, C);
+    for (uint32_t i = lane; i < cr.count() * (B1 ? 1u : 2u); i += 32) {
+      const uint32_t c = cr.col(B1 ? i : i >> 1), b = B1 ? 0u : (i & 1u);
+      const float k = __uint_as_float(lds32a(xres_a + resident_slot(c, c_first, C) * XS + kLimbs * (B1 ? 1u : 2u) * 128u +
+                                              (2u * b + 1u) * 4u));
+      any_wide = any_wide || !(k < 0.0f);
+    }
+    any_wide = __any_sync(0xffffffffu, any_wide);
+  }
+
+  // The math of the tile in ring slot j (limbs at xres_a + xoff), then the next limb slot.
+  // WIDE: the slot may be wide or non-finite (checked per tile).
+  auto tile_math = [&](int j, auto wide_tag) {
+    constexpr bool WIDE = decltype(wide_tag)::value;
+    XFragI8 xf;
+    load_limbs<B1>(xf, xres_a + xoff + xl8.frag, xres_a + xoff + xl8.cst);
+    uint32_t acc[CH][4];
+    bulk_tile_mma<D, false>(w[j], xf, acc, kFull);
+    if (!WIDE || (xf.K[0] < 0.0f && (B1 || xf.K[1] < 0.0f))) {
+      bulk_tile_epilogue<D, B1, false>(sc[j], xf, acc, y, kFull);
+    } else {
+      const float f0 = __uint_as_float(lds32a(xres_a + xoff + kWideOff));
+      const float f1 = B1 ? 1.0f : __uint_as_float(lds32a(xres_a + xoff + kWideOff + 4));
+      bulk_tile_epilogue_wide<D, B1, false>(sc[j], xf, acc, y, kFull, f0, f1);
+    }
+    xoff = xoff == 0 ? x_top : xoff - XS;
+  };
+  // End of a tile row (its column 0) or of the CTA's range: the row's sums are stored,
+  // published for a later CTA, or kept to be finished last.
+  auto flush_row = [&]() {
+    quad_sum<B1>(y);
+    const uint64_t rb = row == row_first ? rb_first : u0, re = row == row_last ? re_last : u1;
+    if (rb >= u0 && re <= u1) {
+      store_out<1>(p, y, row * 128 + rit0, q);
+    } else if (re > u1) {
+      publish_flagged<1>(p, cta, y, rit0, q);
+    } else {
+      keep = true;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) kept[0][e] = y[0][e];
+    }
+#pragma unroll
+    for (int e = 0; e < 4; ++e) y[0][e] = 0.0f;
+    --row;
+    left = C;
+  };
+
+  // Steady state: groups of R tiles k0..k0+R-1 whose refills k0+R..k0+2R-1 are interior
+  // tiles (before the CTA's last), so no tile of the group ends the CTA's range.  A group
+  // inside one tile row (the usual case) runs with no row-end test; a group that reaches
+  // a row end runs tile by tile with it, as a separate block, so the hot loop stays small.
+  uint32_t k0 = 0;
+  const uint8_t* cur[D];
+#pragma unroll
+  for (int s = 0; s < D; ++s) cur[s] = base[s] - static_cast<uint64_t>(R) * kRecordBytes;
+  auto main_loop = [&](auto wide_tag) {
+    for (; k0 + 2 * R < ntiles; k0 += R) {
+      if (left > static_cast<uint32_t>(R)) {
+#pragma unroll
+        for (int j = 0; j < R; ++j) {
+          tile_math(j, wide_tag);
+#pragma unroll
+          for (int s = 0; s < D; ++s) {
+            const uint8_t* a = cur[s] - j * kRecordBytes;
+            ld_plane(w[j][s], sc[j][s], a, a + scale_rel, l2_first);
+          }
+        }
+        left -= R;
+      } else {
+#pragma unroll
+        for (int j = 0; j < R; ++j) {
+          tile_math(j, wide_tag);
+#pragma unroll
+          for (int s = 0; s < D; ++s) {
+            const uint8_t* a = cur[s] - j * kRecordBytes;
+            ld_plane(w[j][s], sc[j][s], a, a + scale_rel, l2_first);
+          }
+          if (--left == 0) flush_row();
+        }
+      }
+#pragma unroll
+      for (int s = 0; s < D; ++s) cur[s] -= R * kRecordBytes;
+    }
+  };
+  if (any_wide) main_loop(std::true_type{});
+  else main_loop(std::false_type{});
+  // The rest (at most 2R tiles): refills with bounds and the edge mask, the CTA's end.
+#pragma unroll
+  for (int jj = 0; jj < 2 * R; ++jj) {
+    const uint32_t k = k0 + jj;
+    if (k >= ntiles) break;
+    tile_math(jj % R, std::true_type{});
+    if (k + R < ntiles) load_masked(jj % R, k + R, edge_mask(k + R));
+    if (--left == 0 || k + 1 == ntiles) flush_row();
+  }
+  if (keep) reduce_split_row<1, B1>(p, row_first, rb_first, total, ctas, cta, kept, rit0, q);
+  if (p.g_world > 1) gather_signal(p, ctas);
+}
+
+template <int NB, int XL, int D, bool B1 = false, bool I8 = false, bool MX = false>
+__global__ void __launch_bounds__(kStreamThreads, (NB == 1 && (XL == 1 || I8)) ? 2 : 1)
+    gemv_uniform_kernel(const __grid_constant__ GemvParams p) {
+  if constexpr (I8 && !MX && NB == 1) lean_body<XL, D, B1>(p, blockIdx.x, gridDim.x);
+  else uniform_body<NB, XL, D, B1, I8, MX>(p, blockIdx.x, gridDim.x);
+}
+
+// Independent GEMVs in one launch (hqb_gemv_grouped): CTAs [cta_base[k], cta_base[k+1]) run
+// problem k's stream-K share, so every problem streams at once and the launch's fixed costs
+// (start, activation limbs, tail) are paid once for the group.
+constexpr uint32_t kMaxGroup = 8;
+struct GroupParams {
+  GemvParams p[kMaxGroup];
+  uint32_t cta_base[kMaxGroup + 1];
+  uint32_t count;
+};
+static_assert(sizeof(GroupParams) <= 4096, "kernel parameter space");
+
+template <int XL, int D, bool B1>
+__global__ void __launch_bounds__(kStreamThreads, 2) gemv_grouped_kernel(const __grid_constant__ GroupParams g) {
+  uint32_t k = 0;
+  while (k + 1 < g.count && blockIdx.x >= g.cta_base[k + 1]) ++k;
+  lean_body<XL, D, B1>(g.p[k], blockIdx.x - g.cta_base[k], g.cta_base[k + 1] - g.cta_base[k]);
 }
 
 // --------------------------------------------------------------------------------------
@@ -2027,7 +2266,7 @@ uint32_t gemv_smem_cap() {
     m = std::max(m, ring_shape(xslot_bytes_for(HQB_MAX_BATCH, 2), cap, 0).smem);
   for (uint32_t cap = 1; cap <= HQB_MAX_STAGES; ++cap)
     m = std::max(m, ring_shape(0, cap, kXResidentMax).smem);
-  return std::max(std::max(std::max(m, kSmemBudget + 1024), kRowsSmemMax), kXResidentMaxI8 + 256);
+  return std::max(std::max(std::max(m, kSmemBudget + 1024), kRowsSmemMax), kXResidentMaxI8 + 4096 + 256);
 }
 
 // Resident CTAs per SM for a kernel variant at a given shared-memory size (cached).
@@ -2349,7 +2588,10 @@ int gemv_impl(const hqb_plane_matrix* m, uint32_t prefix, const uint8_t* depth, 
   const bool bulk_form = !simt && !x_prepared && batch <= 2 &&
                          !(flags & (HQB_FLAG_RING | HQB_FLAG_F16MMA | HQB_FLAG_STREAMK | HQB_FLAG_ROWBLOCK));
   const uint64_t sel_plane_bytes = static_cast<uint64_t>(m->grid_rows) * m->grid_cols * kRecordBytes * prefix;
-  const bool bulk_default = !mixed && prefix >= 2 && m->grid_cols >= 128 && sel_plane_bytes >= (96ull << 20);
+  // FP32 activations with a depth map take it too: its limbs keep activations of 2^100 and
+  // more exact (the register-ring depth-map kernel gives NaN rows for them).
+  const bool bulk_default = (mixed && x_dtype == HQB_F32) ||
+                            (!mixed && prefix >= 2 && m->grid_cols >= 128 && sel_plane_bytes >= (96ull << 20));
   if (bulk_form && ((flags & HQB_FLAG_BULK) || bulk_default)) {
     const uint32_t kd = mixed ? HQB_MAX_STAGES : prefix;
     // units: exact for a uniform prefix; a depth map's total lives on the device, so the
@@ -2432,7 +2674,11 @@ int gemv_impl(const hqb_plane_matrix* m, uint32_t prefix, const uint8_t* depth, 
   const uint64_t rows_items_cta = (static_cast<uint64_t>(m->grid_rows) * 8 + sms - 1) / sms;
   const bool rows_small = all_units <= static_cast<uint64_t>(kRowsUnitsMax) * 2 * sms &&
                           warp_units * 2 * sms <= all_units + 5ull * sms && (!i8_form || rows_items_cta <= 2);
+  // FP32 x at batch <= 2 (int8 limbs) keeps to the lean stream-K kernel unless the row-block
+  // kernel is asked for: only limb_item slots keep activations of 2^100 and more exact
   const bool rows_path = !mixed && !simt && batch <= 8 && !(flags & (HQB_FLAG_RING | HQB_FLAG_STREAMK)) &&
+                         (x_dtype != HQB_F32 || batch > 2 || x_prepared ||
+                          (flags & (HQB_FLAG_ROWBLOCK | HQB_FLAG_F16MMA))) &&
                          (rows_small || (flags & HQB_FLAG_ROWBLOCK)) &&
                          static_cast<uint64_t>(m->grid_rows) * m->grid_cols * kRecordBytes < (1ull << 32) &&
                          kRowsHeadBytes + static_cast<uint64_t>(kRowsWarps) * rows_xw <= kRowsSmemMax;
@@ -2466,8 +2712,11 @@ int gemv_impl(const hqb_plane_matrix* m, uint32_t prefix, const uint8_t* depth, 
   const uint64_t avg_tiles = static_cast<uint64_t>(m->grid_rows) * m->grid_cols / (static_cast<uint64_t>(sms) * 2);
   const bool fuse_prep = !x_prepared && (rows_path || (streaming && (!mixed || mx) && avg_tiles <= kFusedTilesMax));
   if (!x_prepared && !fuse_prep && info == nullptr) {
-    e = i8 ? launch_prep_i8(x, x_dtype, m->cols, batch, ws + L.xfrag, st)
-           : launch_prep(x, x_dtype, m->cols, batch, ws + L.xfrag, st);
+    // the int8 uniform stream-K kernel (lean form) reads limb_item slots; the depth-map form
+    // the register-ring builder's
+    e = (i8 && !mixed) ? launch_prep_limbs(x, x_dtype, m->cols, batch, ws + L.xfrag, (flags & HQB_FLAG_PDL) != 0, st)
+        : i8           ? launch_prep_i8(x, x_dtype, m->cols, batch, ws + L.xfrag, st)
+                       : launch_prep(x, x_dtype, m->cols, batch, ws + L.xfrag, st);
     if (e != cudaSuccess) {
       cudaGetLastError();
       return e;
@@ -2537,6 +2786,7 @@ int gemv_impl(const hqb_plane_matrix* m, uint32_t prefix, const uint8_t* depth, 
     p.x_res_slots = res_slots;
     smem = !streaming          ? rs.smem
            : (mixed && !mx)    ? static_cast<uint32_t>(x_all_bytes) + 256
+           : (i8 && !mixed)    ? res_slots * xslot + (kStreamThreads / 32) * 512 + 256  // + limb transpose areas
                                : res_slots * xslot + 256;
     threads = streaming ? kStreamThreads : kGemvThreads;
   }
@@ -2683,6 +2933,181 @@ HQB_API int hqb_gemv_batch(const hqb_gemv_call* calls, uint32_t count, void* wor
 
 }  // extern "C"
 
+namespace {
+
+using GroupKernel = void (*)(GroupParams);
+
+template <int XL, int D>
+GroupKernel pick_grouped_d(bool b1) {
+  return b1 ? gemv_grouped_kernel<XL, D, true> : gemv_grouped_kernel<XL, D, false>;
+}
+
+GroupKernel pick_grouped(uint32_t xl, uint32_t d, bool b1) {
+  if (xl == 1) {
+    switch (d) {
+      case 1: return pick_grouped_d<1, 1>(b1);
+      case 2: return pick_grouped_d<1, 2>(b1);
+      case 3: return pick_grouped_d<1, 3>(b1);
+      default: return pick_grouped_d<1, 4>(b1);
+    }
+  }
+  switch (d) {
+    case 1: return pick_grouped_d<2, 1>(b1);
+    case 2: return pick_grouped_d<2, 2>(b1);
+    case 3: return pick_grouped_d<2, 3>(b1);
+    default: return pick_grouped_d<2, 4>(b1);
+  }
+}
+
+// One grouped launch of independent calls, or HQB_ERR_UNSUPPORTED when they do not share
+// the form it needs (uniform prefix, batch <= 2, raw x of one dtype, int8 limbs).
+int grouped_launch(const hqb_gemv_call* calls, uint32_t count, void* workspace, uint64_t workspace_bytes,
+                   void* stream) {
+  if (count < 2 || count > kMaxGroup) return HQB_ERR_UNSUPPORTED;
+  const hqb_gemv_call& c0 = calls[0];
+  const uint32_t d = c0.prefix, batch = c0.batch;
+  const int xd = c0.x_dtype;
+  const uint32_t bad_flags = HQB_FLAG_SIMT | HQB_FLAG_RING | HQB_FLAG_TCGEN05 | HQB_FLAG_ROWBLOCK | HQB_FLAG_F16MMA |
+                             HQB_FLAG_BULK;
+  uint32_t maxR = 0, maxC = 0;
+  uint64_t units[kMaxGroup], total = 0;
+  for (uint32_t i = 0; i < count; ++i) {
+    const hqb_gemv_call& c = calls[i];
+    if (!plane_matrix_ok(c.m) || c.x == nullptr || c.y == nullptr) return HQB_ERR_INVALID;
+    if (c.depth != nullptr || c.depth_plan != nullptr || c.x_prepared || c.prefix != d || d == 0 ||
+        d > c.m->stage_count || c.batch != batch || batch == 0 || batch > 2 || c.x_dtype != xd ||
+        (c.flags & bad_flags))
+      return HQB_ERR_UNSUPPORTED;
+    if ((xd != HQB_F16 && xd != HQB_F32) || (c.y_dtype != HQB_F16 && c.y_dtype != HQB_F32)) return HQB_ERR_INVALID;
+    if (c.bias != nullptr && c.bias_dtype != HQB_F16 && c.bias_dtype != HQB_F32) return HQB_ERR_INVALID;
+    if (!stage_planes_ok(c.m, d)) return HQB_ERR_INVALID;
+    maxR = std::max(maxR, c.m->grid_rows);
+    maxC = std::max(maxC, c.m->grid_cols);
+    units[i] = static_cast<uint64_t>(c.m->grid_rows) * c.m->grid_cols * d;
+    total += units[i];
+  }
+  if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0) return HQB_ERR_INVALID;
+  int device = 0;
+  cudaError_t e = cudaGetDevice(&device);
+  if (e != cudaSuccess) return e;
+  const int sms = device_sm_count(device);
+  if (sms <= 0) return cudaErrorNoDevice;
+  const uint32_t xl = xd == HQB_F32 ? 2 : 1;
+  // the grouped launch uses the error word and the partials region (at its offset for the
+  // tallest call): the workspace of the call with the most tile rows is large enough
+  const WsLayout L = ws_layout(maxR, maxC, batch, xl, sms);
+  if (workspace_bytes < L.xfrag) return HQB_ERR_INVALID;
+  // CTAs dealt in proportion to each call's units (at least one each)
+  const GroupKernel k = pick_grouped(xl, d, batch == 1);
+  const uint32_t xslot = xslot_i8_bytes(batch);
+  GroupParams gp{};
+  gp.count = count;
+  uint32_t G = static_cast<uint32_t>(sms) * 2;
+  uint32_t res_max = 0;
+  for (int attempt = 0; attempt < 2; ++attempt) {
+    uint32_t acc = 0;
+    uint64_t seen = 0;
+    gp.cta_base[0] = 0;
+    for (uint32_t i = 0; i < count; ++i) {
+      seen += units[i];
+      uint32_t end = static_cast<uint32_t>((seen * G + total / 2) / total);
+      end = std::max(end, acc + 1);
+      if (i + 1 == count) end = std::max(G, acc + 1);
+      gp.cta_base[i + 1] = end;
+      acc = end;
+    }
+    res_max = 0;
+    for (uint32_t i = 0; i < count; ++i) {
+      const uint64_t g_i = gp.cta_base[i + 1] - gp.cta_base[i];
+      const uint64_t units_cta = (units[i] + g_i - 1) / g_i;
+      const uint32_t res = static_cast<uint32_t>(std::min<uint64_t>(calls[i].m->grid_cols, (units_cta + d - 1) / d + 1));
+      res_max = std::max(res_max, res);
+    }
+    if (static_cast<uint64_t>(res_max) * xslot <= kXResidentMaxI8) break;
+    if (attempt == 1) return HQB_ERR_UNSUPPORTED;
+  }
+  const uint32_t smem = res_max * xslot + (kStreamThreads / 32) * 512 + 256;  // + limb transpose areas
+  {
+    static std::mutex mu;
+    std::lock_guard<std::mutex> lock(mu);
+    e = cudaFuncSetAttribute(reinterpret_cast<const void*>(k), cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(kXResidentMaxI8 + 4096 + 256));
+    int per_sm = 0;
+    if (e == cudaSuccess)
+      e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, static_cast<int>(kStreamThreads), smem);
+    if (e != cudaSuccess) {
+      cudaGetLastError();
+      return e;
+    }
+    if (per_sm < 2) return HQB_ERR_UNSUPPORTED;
+  }
+  G = gp.cta_base[count];
+  if (G > static_cast<uint32_t>(sms) * kMaxCtasPerSm) return HQB_ERR_UNSUPPORTED;
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  for (uint32_t i = 0; i < count; ++i) {
+    const hqb_gemv_call& c = calls[i];
+    GemvParams& p = gp.p[i];
+    for (uint32_t s = 0; s < HQB_MAX_STAGES; ++s) p.planes[s] = static_cast<const uint8_t*>(c.m->planes[s]);
+    p.bias = c.bias;
+    p.y = c.y;
+    p.error = reinterpret_cast<int*>(ws);
+    // each call's CTAs publish split-row words in their own slots of the partials region
+    p.partials = reinterpret_cast<float*>(ws + L.partials + static_cast<uint64_t>(gp.cta_base[i]) * batch * 1024);
+    p.counters = reinterpret_cast<uint32_t*>(ws + L.counters);
+    p.rows = static_cast<uint32_t>(c.m->rows);
+    p.R = c.m->grid_rows;
+    p.C = c.m->grid_cols;
+    p.prefix = d;
+    p.stage_count = c.m->stage_count;
+    p.batch = batch;
+    p.xslot_bytes = xslot;
+    p.bias_dtype = c.bias_dtype;
+    p.y_dtype = c.y_dtype;
+    p.cols = static_cast<uint32_t>(c.m->cols);
+    p.shift_mul = 1u << 24;
+    p.pdl = (c.flags & HQB_FLAG_PDL) ? 1u : 0u;
+    p.x_raw = c.x;
+    p.x_vec = x_rows_vec(c.x, c.m->cols, xl) ? 1u : 0u;
+    p.total = units[i];
+    p.x_res_slots = res_max;
+  }
+  const cudaError_t prior = take_prior_error();
+  if (prior != cudaSuccess) return prior;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(G);
+  cfg.blockDim = dim3(kStreamThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = as_stream(stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  if (calls[0].flags & HQB_FLAG_PDL) {
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+  }
+  e = cudaLaunchKernelEx(&cfg, k, gp);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return e;
+  }
+  return HQB_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+HQB_API int hqb_gemv_grouped(const hqb_gemv_call* calls, uint32_t count, void* workspace, uint64_t workspace_bytes,
+                             void* stream) {
+  if (calls == nullptr || count == 0) return HQB_ERR_INVALID;
+  const int st = grouped_launch(calls, count, workspace, workspace_bytes, stream);
+  if (st != HQB_ERR_UNSUPPORTED) return st;
+  return hqb_gemv_batch(calls, count, workspace, workspace_bytes, stream);  // one by one
+}
+
+
+}  // extern "C"
+
 // A captured decode step: the CUDA graph of a batch of GEMV calls.
 struct hqb_step {
   cudaGraph_t graph = nullptr;
@@ -2691,8 +3116,26 @@ struct hqb_step {
 
 extern "C" {
 
+namespace {
+int step_create(const hqb_gemv_call* calls, uint32_t count, void* workspace, uint64_t workspace_bytes, hqb_step** step,
+                bool grouped);
+}
+
 HQB_API int hqb_step_create(const hqb_gemv_call* calls, uint32_t count, void* workspace, uint64_t workspace_bytes,
                             hqb_step** step) {
+  return step_create(calls, count, workspace, workspace_bytes, step, false);
+}
+
+HQB_API int hqb_step_create_grouped(const hqb_gemv_call* calls, uint32_t count, void* workspace,
+                                    uint64_t workspace_bytes, hqb_step** step) {
+  return step_create(calls, count, workspace, workspace_bytes, step, true);
+}
+
+}  // extern "C"
+
+namespace {
+int step_create(const hqb_gemv_call* calls, uint32_t count, void* workspace, uint64_t workspace_bytes, hqb_step** step,
+                bool grouped) {
   if (step == nullptr || calls == nullptr || count == 0) return HQB_ERR_INVALID;
   *step = nullptr;
   const cudaError_t prior = take_prior_error();
@@ -2707,7 +3150,8 @@ HQB_API int hqb_step_create(const hqb_gemv_call* calls, uint32_t count, void* wo
   }
   int status = cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal);
   if (status == cudaSuccess) {
-    status = hqb_gemv_batch(calls, count, workspace, workspace_bytes, s);
+    status = grouped ? hqb_gemv_grouped(calls, count, workspace, workspace_bytes, s)
+                     : hqb_gemv_batch(calls, count, workspace, workspace_bytes, s);
     cudaGraph_t g = nullptr;
     const cudaError_t end = cudaStreamEndCapture(s, &g);  // always end the capture
     if (status == HQB_OK) status = end;
@@ -2725,6 +3169,9 @@ HQB_API int hqb_step_create(const hqb_gemv_call* calls, uint32_t count, void* wo
   *step = st;
   return HQB_OK;
 }
+}  // namespace
+
+extern "C" {
 
 HQB_API int hqb_step_launch(hqb_step* step, void* stream) {
   if (step == nullptr || step->exec == nullptr) return HQB_ERR_INVALID;

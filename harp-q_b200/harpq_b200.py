@@ -94,6 +94,8 @@ EXPORTS = {
     "hqb_gemv_noalloc": (i32, [ctypes.POINTER(PlaneMatrixC), u32, vp, i32, u32, vp, i32, vp, i32, vp]),
     "hqb_gemv_batch": (i32, [ctypes.POINTER(GemvCallC), u32, vp, u64, vp]),
     "hqb_step_create": (i32, [ctypes.POINTER(GemvCallC), u32, vp, u64, ctypes.POINTER(vp)]),
+    "hqb_step_create_grouped": (i32, [ctypes.POINTER(GemvCallC), u32, vp, u64, ctypes.POINTER(vp)]),
+    "hqb_gemv_grouped": (i32, [ctypes.POINTER(GemvCallC), u32, vp, u64, vp]),
     "hqb_step_launch": (i32, [vp, vp]),
     "hqb_step_destroy": (i32, [vp]),
     "hqb_gemv_query": (i32, [ctypes.POINTER(PlaneMatrixC), u32, i32, i32, u32, i32, u32, ctypes.POINTER(LaunchInfo)]),
@@ -389,12 +391,14 @@ class Step:
     """A fixed list of GEMV calls (plane matrix, x, prefix, out, flags) on one stream with one
     workspace: the decode step's GEMVs for one host call.  graph=True (default) captures them
     once into a CUDA graph (hqb_step_create) and run() launches it; graph=False runs them
-    through hqb_gemv_batch.  Buffers are bound at construction; refill x and read out in
+    through hqb_gemv_batch.  independent=True (no call reads another's output) runs them as
+    one grouped kernel launch where they share its form (hqb_gemv_grouped).  Buffers are bound at construction; refill x and read out in
     place."""
 
-    def __init__(self, calls, workspace: Workspace, graph: bool = True):
+    def __init__(self, calls, workspace: Workspace, graph: bool = True, independent: bool = False):
         self.calls = list(calls)
         self.handle = None
+        self.independent = independent
         self.ws = workspace
         arr = (GemvCallC * len(self.calls))()
         self._keep = []
@@ -409,16 +413,16 @@ class Step:
         self.arr = arr
         if graph:
             h = vp()
-            check(lib().hqb_step_create(arr, len(self.calls), self.ws.ptr(), self.ws.nbytes, ctypes.byref(h)),
-                  "hqb_step_create")
+            create = lib().hqb_step_create_grouped if independent else lib().hqb_step_create
+            check(create(arr, len(self.calls), self.ws.ptr(), self.ws.nbytes, ctypes.byref(h)), "hqb_step_create")
             self.handle = h.value
 
     def run(self, stream=None) -> None:
         if self.handle is not None:
             check(lib().hqb_step_launch(self.handle, _stream(stream)), "hqb_step_launch")
         else:
-            check(lib().hqb_gemv_batch(self.arr, len(self.calls), self.ws.ptr(), self.ws.nbytes, _stream(stream)),
-                  "hqb_gemv_batch")
+            run = lib().hqb_gemv_grouped if self.independent else lib().hqb_gemv_batch
+            check(run(self.arr, len(self.calls), self.ws.ptr(), self.ws.nbytes, _stream(stream)), "hqb_gemv_batch")
 
     def close(self) -> None:
         if self.handle is not None:

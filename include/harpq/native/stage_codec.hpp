@@ -4,8 +4,8 @@
 //
 // DecodeStagePayload and Crc32c parse bytes on the host.  DequantizeStage,
 // DequantizePrefix and ProgressiveLinearReference keep their exact results
-// (bit-identical FP32) but run on the CUDA device; they throw std::runtime_error when
-// no device is usable.
+// (bit-identical FP32): they run on the CUDA device when one is usable and as host
+// loops of the same FP32 operations otherwise, so CPU-only callers keep them.
 #ifndef HARPQ_B200_NATIVE_STAGE_CODEC_HPP_
 #define HARPQ_B200_NATIVE_STAGE_CODEC_HPP_
 

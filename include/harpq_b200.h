@@ -257,6 +257,15 @@ typedef struct hqb_gemv_call {
 HQB_API int hqb_gemv_batch(const hqb_gemv_call* calls, uint32_t count, void* workspace, uint64_t workspace_bytes,
                            void* stream);
 
+/* Independent GEMVs (no call reads another's output) as ONE kernel launch: the calls'
+ * (tile, stage) units are dealt to the CTAs of one grid in proportion to their sizes, each
+ * CTA working on one call, so every call streams at once and the launch's fixed costs are
+ * paid once.  It applies to up to 8 calls that share a uniform prefix, batch (<= 2) and raw
+ * activation dtype; other call lists run one by one as in hqb_gemv_batch.  The workspace
+ * must be as large as the largest call's.  No reference counterpart. */
+HQB_API int hqb_gemv_grouped(const hqb_gemv_call* calls, uint32_t count, void* workspace, uint64_t workspace_bytes,
+                             void* stream);
+
 /* A decode step captured once: the calls of hqb_gemv_batch recorded into a CUDA graph
  * (their programmatic-dependent launches kept as graph edges) and instantiated.  Launching
  * it costs one graph launch on the host, whatever the number of GEMVs.  The buffers the
@@ -265,6 +274,9 @@ HQB_API int hqb_gemv_batch(const hqb_gemv_call* calls, uint32_t count, void* wor
 typedef struct hqb_step hqb_step;
 HQB_API int hqb_step_create(const hqb_gemv_call* calls, uint32_t count, void* workspace, uint64_t workspace_bytes,
                             hqb_step** step);
+/* The same for independent calls, captured as hqb_gemv_grouped (one kernel for the group). */
+HQB_API int hqb_step_create_grouped(const hqb_gemv_call* calls, uint32_t count, void* workspace,
+                                    uint64_t workspace_bytes, hqb_step** step);
 HQB_API int hqb_step_launch(hqb_step* step, void* stream);
 HQB_API int hqb_step_destroy(hqb_step* step);
 

@@ -31,7 +31,9 @@ from pathlib import Path
 ORACLE = Path(__file__).resolve().parent
 REPO = ORACLE.parent
 REF_OUT = ORACLE / "_ref"
-DEFAULT_REFERENCE = Path(os.environ.get("HQB_REFERENCE", "/root/reference"))
+# The reference checkout: $HQB_REFERENCE, else a directory named "reference" beside this
+# repository's directory.  Absent on machines that only run the prebuilt files.
+DEFAULT_REFERENCE = Path(os.environ.get("HQB_REFERENCE", str(REPO.parent / "reference")))
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 

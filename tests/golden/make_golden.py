@@ -24,6 +24,7 @@ from __future__ import annotations
 import argparse
 import hashlib
 import importlib.util
+import os
 import re
 import sys
 from pathlib import Path
@@ -122,7 +123,9 @@ def seeded_fixture(quantization, matrix_codec, integrity, name, rows, cols, std,
 
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser(description=__doc__)
-    ap.add_argument("--reference", type=Path, default=Path("/root/reference"))
+    default_ref = Path(os.environ.get("HQB_REFERENCE", str(Path(__file__).resolve().parents[3] / "reference")))
+    ap.add_argument("--reference", type=Path, default=default_ref,
+                    help="reference checkout ($HQB_REFERENCE, else 'reference' beside this repository)")
     ap.add_argument("--check", action="store_true", help="fail if committed fixtures differ")
     args = ap.parse_args(argv)
     quantization, matrix_codec, integrity, gen = _load_reference(args.reference)

@@ -561,3 +561,56 @@ def test_int8_limb_kernel_depth_map(rows, cols, batch):
         a = pm.gemv(xt, depth=u, y_dtype=torch.float32).cpu().numpy()
         b = pm.gemv(xt, prefix=p, y_dtype=torch.float32).cpu().numpy()
         assert rel_l2(a, b) <= 2e-5, f"depth map of {p} vs prefix {p}"
+
+
+@pytest.mark.parametrize("batch", [1, 2])
+def test_register_ring_int8_fp32_paths(batch):
+    """The register-ring int8 kernels with FP32 activations (forced with HQB_FLAG_STREAMK;
+    FP32 x takes the bulk kernel by default): the depth-map form, and a layer large enough
+    for the standalone limb preparation launch (prep_x_i8_kernel<float>, more than 24 tiles
+    per CTA on average).  Against the scalar-order oracle / FP64."""
+    import harpq_b200 as hqb
+
+    rng = np.random.default_rng(600 + batch)
+    m = random_matrix(rng, 520, 700)
+    pm = plane_matrix(m)
+    gr, gc = m.grid
+    depth = rng.integers(1, 5, size=(gr, gc)).astype(np.uint8)
+    plan = hqb.DepthPlan(torch.from_numpy(depth).cuda(), 4)
+    x = (rng.standard_normal((batch, m.cols)) * 3).astype(np.float32)
+    xt = torch.from_numpy(x).cuda()
+    fl = hqb.FLAG_STREAMK
+    assert pm.uses_int8_limbs(batch, hqb.F32, 0, mixed=True, flags=fl)
+    assert pm.gemv_kernel(batch, hqb.F32, 0, mixed=True, flags=fl) == "gemv_uniform_kernel"
+    y = pm.gemv(xt, depth=plan, y_dtype=torch.float32, flags=fl).cpu().numpy()
+    assert_close(y, orc.linear_mixed(m, x, depth), 2e-4, 2e-4, f"depth map FP32 b{batch}")
+    assert rel_l2(y, _fp64_reference(m, x, 4, depth=depth)) <= 2e-5
+    # standalone FP32 limb preparation: 16384x8192
+    rows, cols = 16384, 8192
+    big = random_matrix(rng, rows, cols, stages=2)
+    pb = plane_matrix(big)
+    assert pb.gemv_launches(batch, hqb.F32, 2, flags=fl) == 2  # limb preparation + GEMV
+    assert pb.uses_int8_limbs(batch, hqb.F32, 2, flags=fl)
+    xb = torch.from_numpy((rng.standard_normal((batch, cols)) * 2).astype(np.float32)).cuda()
+    yb = pb.gemv(xb, prefix=2, y_dtype=torch.float32, flags=fl)
+    e64 = (xb.double() @ pb.decode(2).double().T).cpu().numpy()
+    assert_close(yb.cpu().numpy(), e64, 2e-4, 2e-4, f"16384x8192 FP32 b{batch}")
+    assert rel_l2(yb.cpu().numpy(), e64) <= 2e-5
+
+
+@pytest.mark.parametrize("flags_name", ["STREAMK", "ROWBLOCK"])
+def test_register_ring_int8_nonfinite_activations(flags_name):
+    """FP16 activations holding Inf or NaN on the register-ring int8 kernels (the default for
+    FP16 x at batch <= 2): every output of that batch row is NaN, the other row is exact."""
+    import harpq_b200 as hqb
+
+    rng = np.random.default_rng(61)
+    m = random_matrix(rng, 512, 640)
+    pm = plane_matrix(m)
+    fl = getattr(hqb, "FLAG_" + flags_name)
+    for bad in (np.inf, -np.inf, np.nan):
+        x = rng.standard_normal((2, m.cols)).astype(np.float16)
+        x[0, 300] = bad
+        y = pm.gemv(torch.from_numpy(x).cuda(), prefix=3, y_dtype=torch.float32, flags=fl).cpu().numpy()
+        assert np.all(np.isnan(y[0])), bad
+        assert_close(y[1], orc.linear_reference(m, x[1:].astype(np.float32), 3)[0], 2e-4, 2e-4, "clean row")

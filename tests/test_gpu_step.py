@@ -59,3 +59,40 @@ def test_step_rejects_an_invalid_call_and_enqueues_nothing_after_it():
     assert e.value.status == hqb.HQB_ERR_INVALID
     with pytest.raises(hqb.HQBError):
         hqb.Step([(pm, x, 3, y, 0)], ws, graph=False).run()
+
+
+@pytest.mark.parametrize("batch,x_dtype", [(1, "f16"), (2, "f16"), (1, "f32")])
+def test_grouped_launch_matches_single_calls(batch, x_dtype):
+    """Independent GEMVs as one grouped launch (hqb_gemv_grouped, eager and captured): every
+    call's outputs against its own launch within the FP32 contract (the grouped grid splits
+    each call over fewer CTAs, so split-row sums may add in another order) and against FP64;
+    repeated grouped launches give identical bytes."""
+    import harpq_b200 as hqb
+    from conftest import assert_close
+
+    rng = np.random.default_rng(77 + batch)
+    shapes = [(12288, 4096), (4096, 4096), (22016, 4096), (4096, 11008), (300, 520)]
+    pms = [plane_matrix(random_matrix(rng, r, c, stages=2)) for r, c in shapes]
+    tdt = torch.float16 if x_dtype == "f16" else torch.float32
+    xs = [torch.from_numpy(rng.standard_normal((batch, c)).astype(np.float16)).cuda().to(tdt) for _, c in shapes]
+    ys = [torch.empty(batch, r, dtype=torch.float32, device="cuda") for r, _ in shapes]
+    xd = hqb.F16 if x_dtype == "f16" else hqb.F32
+    ws = hqb.Workspace(max(pm.workspace_bytes(batch, xd) for pm in pms))
+    calls = [(pm, x, 2, y, hqb.FLAG_PDL) for pm, x, y in zip(pms, xs, ys)]
+    outs = []
+    for graph in (False, True):
+        step = hqb.Step(calls, ws, graph=graph, independent=True)
+        for y in ys:
+            y.fill_(float("nan"))
+        step.run()
+        torch.cuda.synchronize()
+        outs.append([y.clone() for y in ys])
+        step.close()
+    for a, b in zip(*outs):
+        assert torch.equal(a, b)
+    for pm, x, y in zip(pms, xs, outs[0]):
+        alone = pm.gemv(x, prefix=2, y_dtype=torch.float32, workspace=ws)
+        assert_close(y.cpu().numpy(), alone.cpu().numpy(), 2e-4, 2e-4, "grouped vs alone")
+        e64 = (x.double() @ pm.decode(2).double().T).cpu().numpy()
+        assert_close(y.cpu().numpy(), e64, 2e-4, 2e-4, "grouped vs FP64")
+    assert ws.error_flags() == 0
