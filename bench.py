@@ -480,9 +480,9 @@ def run_ours(args, rank, world, device):
         gemv_us = float(t.item())
 
     # ---- e2e through the public API: pinned host x -> device, GEMVs, device -> host y.
-    # One host->device copy of the step's inputs and one device->host copy of its outputs;
-    # at N = 1 the step's GEMVs go to the library in one call (hqb.Step: hqb_gemv_batch), at
-    # N > 1 call by call with the all-gathers between them.
+    # One host->device copy of the step's inputs and one device->host copy of its outputs
+    # every step; at N = 1 copies and GEMVs are one library step (hqb.Step with inputs and
+    # outputs), at N > 1 call by call with the all-gathers between them.
     host_x_all = x_all.cpu().pin_memory()
 
     def gathered(g, copy):
@@ -491,20 +491,21 @@ def run_ours(args, rank, world, device):
         return y_full[g["name"]] if world > 1 else y_loc[g["name"]]
 
     if world == 1:
+        # each step is one hqb.Step whose graph holds the input copy, the GEMVs and the
+        # output copy (hqb_step_create_io); one host call per step
         host_y_all = torch.empty_like(y_all, device="cpu").pin_memory()
-        steps_api = gsteps if grouped else [
-            hqb.Step([(G["copies"][c], x_dev[G["src"]], prefix, y_loc[G["name"]], hqb.FLAG_PDL) for G in groups], ws)
-            for c in range(ncopies)]
+        steps_api = [hqb.Step([(G["copies"][c], x_dev[G["src"]], prefix, y_loc[G["name"]], hqb.FLAG_PDL)
+                               for G in groups], ws, independent=grouped, inputs=[(x_all, host_x_all)],
+                              outputs=[(host_y_all, y_all)]) for c in range(ncopies)]
         host_y = {"all": host_y_all}
     else:
         host_y = {g["name"]: torch.empty_like(gathered(g, 0), device="cpu").pin_memory() for g in groups}
 
     def e2e_step(copy):
-        x_all.copy_(host_x_all, non_blocking=True)
         if world == 1:
             steps_api[copy].run()
-            host_y_all.copy_(y_all, non_blocking=True)
         else:
+            x_all.copy_(host_x_all, non_blocking=True)
             step(copy)
             for g in groups:
                 host_y[g["name"]].copy_(gathered(g, copy), non_blocking=True)
@@ -740,7 +741,8 @@ def reference_gpu_kernel(device, gen):
     """The reference's own ProgressiveGemvKernel (native/src/progressive_gemv.cu:348-411),
     compiled for sm_100a from its sources into oracle/_ref/libharpq_ref_gpu.so and launched
     through its LaunchProgressiveGemv, timed on this GPU next to this library's drop-in
-    reference-layout kernel (hqb_raw_gemv) and its plane kernel, on the same codes and scales
+    reference-layout kernels (hqb_raw_gemv: raw_i8_kernel by default, the per-element
+    raw_gemv_kernel with HQB_RAW_GENERIC) and its plane kernel, on the same codes and scales
     (reference layout: row-major codes, FP16 scales), FP32 x/y as the reference takes them,
     weights rotating over > 3x L2."""
     import ctypes
@@ -784,13 +786,18 @@ def reference_gpu_kernel(device, gen):
         ws = hqb.Workspace(planes[0].workspace_bytes(1, hqb.F32), device)
         b = p * (rows * cols // 4 + rows * (cols // 128) * 2) + 4 * cols + 4 * rows  # FP32 x and y
         t_ref = _graph_us(ref, 16)
-        t_raw = _graph_us(lambda i: mats[i % n].gemv(x, p), 16)
+        t_raw = _graph_us(lambda i: mats[i % n].gemv(x, p, out=y, flags=hqb.RAW_REQUIRE_FAST), 16)
+        t_generic = _graph_us(lambda i: mats[i % n].gemv(x, p, out=y, flags=hqb.RAW_GENERIC), 16)
         xr = x.view(1, -1)
         t_plane = _graph_us(lambda i: planes[i % n].gemv(xr, prefix=p, out=y.view(1, -1), workspace=ws,
                                                           flags=hqb.FLAG_PDL), 16)
         res[f"{rows}x{cols}_p{p}"] = {
             "reference_kernel_us": round(t_ref, 3), "reference_kernel_gbs": round(b / (t_ref * 1e-6) / 1e9, 1),
             "hqb_raw_gemv_us": round(t_raw, 3), "hqb_raw_gemv_gbs": round(b / (t_raw * 1e-6) / 1e9, 1),
+            "hqb_raw_gemv_kernel": "raw_i8_kernel",
+            "hqb_raw_generic_us": round(t_generic, 3),
+            "hqb_raw_generic_gbs": round(b / (t_generic * 1e-6) / 1e9, 1),
+            "raw_speedup_vs_reference_kernel": round(t_ref / t_raw, 2),
             "plane_us": round(t_plane, 3), "plane_gbs": round(b / (t_plane * 1e-6) / 1e9, 1),
             "plane_speedup_vs_reference_kernel": round(t_ref / t_plane, 2)}
         del raw, mats, planes, ptrs

@@ -3118,7 +3118,8 @@ extern "C" {
 
 namespace {
 int step_create(const hqb_gemv_call* calls, uint32_t count, void* workspace, uint64_t workspace_bytes, hqb_step** step,
-                bool grouped);
+                bool grouped, const hqb_copy* h2d = nullptr, uint32_t n_h2d = 0, const hqb_copy* d2h = nullptr,
+                uint32_t n_d2h = 0);
 }
 
 HQB_API int hqb_step_create(const hqb_gemv_call* calls, uint32_t count, void* workspace, uint64_t workspace_bytes,
@@ -3131,11 +3132,22 @@ HQB_API int hqb_step_create_grouped(const hqb_gemv_call* calls, uint32_t count, 
   return step_create(calls, count, workspace, workspace_bytes, step, true);
 }
 
+HQB_API int hqb_step_create_io(const hqb_gemv_call* calls, uint32_t count, void* workspace, uint64_t workspace_bytes,
+                               const hqb_copy* h2d, uint32_t n_h2d, const hqb_copy* d2h, uint32_t n_d2h, int grouped,
+                               hqb_step** step) {
+  if ((n_h2d != 0 && h2d == nullptr) || (n_d2h != 0 && d2h == nullptr)) return HQB_ERR_INVALID;
+  for (uint32_t i = 0; i < n_h2d; ++i)
+    if (h2d[i].dst == nullptr || h2d[i].src == nullptr) return HQB_ERR_INVALID;
+  for (uint32_t i = 0; i < n_d2h; ++i)
+    if (d2h[i].dst == nullptr || d2h[i].src == nullptr) return HQB_ERR_INVALID;
+  return step_create(calls, count, workspace, workspace_bytes, step, grouped != 0, h2d, n_h2d, d2h, n_d2h);
+}
+
 }  // extern "C"
 
 namespace {
 int step_create(const hqb_gemv_call* calls, uint32_t count, void* workspace, uint64_t workspace_bytes, hqb_step** step,
-                bool grouped) {
+                bool grouped, const hqb_copy* h2d, uint32_t n_h2d, const hqb_copy* d2h, uint32_t n_d2h) {
   if (step == nullptr || calls == nullptr || count == 0) return HQB_ERR_INVALID;
   *step = nullptr;
   const cudaError_t prior = take_prior_error();
@@ -3150,8 +3162,14 @@ int step_create(const hqb_gemv_call* calls, uint32_t count, void* workspace, uin
   }
   int status = cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal);
   if (status == cudaSuccess) {
-    status = grouped ? hqb_gemv_grouped(calls, count, workspace, workspace_bytes, s)
-                     : hqb_gemv_batch(calls, count, workspace, workspace_bytes, s);
+    // the step's input copies, its GEMVs, its output copies: one cudaMemcpyAsync per copy
+    for (uint32_t i = 0; i < n_h2d && status == cudaSuccess; ++i)
+      status = cudaMemcpyAsync(h2d[i].dst, h2d[i].src, h2d[i].bytes, cudaMemcpyDefault, s);
+    if (status == cudaSuccess)
+      status = grouped ? hqb_gemv_grouped(calls, count, workspace, workspace_bytes, s)
+                       : hqb_gemv_batch(calls, count, workspace, workspace_bytes, s);
+    for (uint32_t i = 0; i < n_d2h && status == cudaSuccess; ++i)
+      status = cudaMemcpyAsync(d2h[i].dst, d2h[i].src, d2h[i].bytes, cudaMemcpyDefault, s);
     cudaGraph_t g = nullptr;
     const cudaError_t end = cudaStreamEndCapture(s, &g);  // always end the capture
     if (status == HQB_OK) status = end;

@@ -209,7 +209,16 @@ extern "C" {
 HQB_API int hqb_raw_gemv(const hqb_geometry* gm, const hqb_raw_stage* stages, uint32_t stage_count, uint32_t prefix,
                          const float* x, uint64_t x_count, const float* bias, uint64_t bias_count, float* y,
                          uint64_t y_count, void* stream) {
+  return hqb_raw_gemv_ex(gm, stages, stage_count, prefix, x, x_count, bias, bias_count, y, y_count, 0u, stream);
+}
+
+HQB_API int hqb_raw_gemv_ex(const hqb_geometry* gm, const hqb_raw_stage* stages, uint32_t stage_count,
+                            uint32_t prefix, const float* x, uint64_t x_count, const float* bias,
+                            uint64_t bias_count, float* y, uint64_t y_count, uint32_t flags, void* stream) {
   if (gm == nullptr || (stage_count > 0 && stages == nullptr)) return HQB_ERR_INVALID;
+  if ((flags & ~(HQB_RAW_GENERIC | HQB_RAW_REQUIRE_FAST)) != 0 ||
+      (flags & (HQB_RAW_GENERIC | HQB_RAW_REQUIRE_FAST)) == (HQB_RAW_GENERIC | HQB_RAW_REQUIRE_FAST))
+    return HQB_ERR_INVALID;
   uint64_t cb = 0, sc = 0;
   if (!geometry_ok(gm, &cb, &sc) || stage_count == 0 || stage_count > HQB_MAX_STAGES || prefix > stage_count ||
       x == nullptr || x_count != gm->original_columns || y == nullptr || y_count != gm->original_rows ||
@@ -227,6 +236,20 @@ HQB_API int hqb_raw_gemv(const hqb_geometry* gm, const hqb_raw_stage* stages, ui
   }
   const cudaError_t prior = take_prior_error();
   if (prior != cudaSuccess) return prior;
+  if (!(flags & HQB_RAW_GENERIC)) {
+    RawI8Launch a{};
+    a.geometry = gm;
+    for (uint32_t s = 0; s < prefix; ++s) {
+      a.codes[s] = stages[s].packed_codes;
+      a.scales[s] = stages[s].scale_fp16_bits;
+    }
+    a.prefix = prefix;
+    a.x = x;
+    a.bias = bias;
+    a.y = y;
+    const int r = launch_raw_i8(a, stream);
+    if (r != HQB_ERR_UNSUPPORTED || (flags & HQB_RAW_REQUIRE_FAST)) return r;
+  }
   const unsigned blocks = grid_for(g.rows, 8);
   const bool bytes = (g.group % 4 == 0) && (g.padded_cols % 4 == 0);
   if (bytes) raw_gemv_kernel<true><<<blocks, 256, 0, as_stream(stream)>>>(g, st, prefix, x, bias, y);

@@ -25,6 +25,7 @@ F32, F16 = 0, 1
 FLAG_PDL, FLAG_SIMT, FLAG_RING, FLAG_TCGEN05, FLAG_STREAMK, FLAG_ROWBLOCK = 1, 2, 4, 8, 16, 32
 FLAG_F16MMA = 64  # keep the GEMV kernels on FP16-fragment MMAs (no int8 activation limbs)
 FLAG_BULK = 128  # bulk-copy kernel (batch <= 2, raw x): default for large layers, forced by this flag
+RAW_GENERIC, RAW_REQUIRE_FAST = 1, 2  # hqb_raw_gemv_ex: per-element FMA kernel / int8 raw-layout kernel only
 I8_LIMBS = 4
 TILE = 128
 RECORD_BYTES = 4352
@@ -45,6 +46,10 @@ class Geometry(ctypes.Structure):
 
 class RawStage(ctypes.Structure):
     _fields_ = [("packed_codes", vp), ("packed_code_bytes", u64), ("scale_fp16_bits", vp), ("scale_count", u64)]
+
+
+class CopyC(ctypes.Structure):
+    _fields_ = [("dst", ctypes.c_void_p), ("src", ctypes.c_void_p), ("bytes", ctypes.c_uint64)]
 
 
 class RawStageF32(ctypes.Structure):
@@ -95,6 +100,8 @@ EXPORTS = {
     "hqb_gemv_batch": (i32, [ctypes.POINTER(GemvCallC), u32, vp, u64, vp]),
     "hqb_step_create": (i32, [ctypes.POINTER(GemvCallC), u32, vp, u64, ctypes.POINTER(vp)]),
     "hqb_step_create_grouped": (i32, [ctypes.POINTER(GemvCallC), u32, vp, u64, ctypes.POINTER(vp)]),
+    "hqb_step_create_io": (i32, [ctypes.POINTER(GemvCallC), u32, vp, u64, ctypes.POINTER(CopyC), u32,
+                                 ctypes.POINTER(CopyC), u32, i32, ctypes.POINTER(vp)]),
     "hqb_gemv_grouped": (i32, [ctypes.POINTER(GemvCallC), u32, vp, u64, vp]),
     "hqb_step_launch": (i32, [vp, vp]),
     "hqb_step_destroy": (i32, [vp]),
@@ -113,6 +120,8 @@ EXPORTS = {
     "hqb_decode_planes": (i32, [ctypes.POINTER(PlaneMatrixC), u32, vp, vp, u64, vp]),
     "hqb_raw_gemv": (i32, [ctypes.POINTER(Geometry), ctypes.POINTER(RawStage), u32, u32, vp, u64, vp, u64, vp, u64,
                            vp]),
+    "hqb_raw_gemv_ex": (i32, [ctypes.POINTER(Geometry), ctypes.POINTER(RawStage), u32, u32, vp, u64, vp, u64, vp,
+                              u64, u32, vp]),
     "hqb_raw_dequantize_stage": (i32, [ctypes.POINTER(Geometry), ctypes.POINTER(RawStageF32), u32, u32, vp, vp]),
     "hqb_raw_dequantize_prefix": (i32, [ctypes.POINTER(Geometry), ctypes.POINTER(RawStageF32), u32, u32, vp, vp]),
     "hqb_raw_linear_ordered": (i32, [ctypes.POINTER(Geometry), ctypes.POINTER(RawStageF32), u32, u32, vp, u64, vp,
@@ -395,7 +404,11 @@ class Step:
     one grouped kernel launch where they share its form (hqb_gemv_grouped).  Buffers are bound at construction; refill x and read out in
     place."""
 
-    def __init__(self, calls, workspace: Workspace, graph: bool = True, independent: bool = False):
+    def __init__(self, calls, workspace: Workspace, graph: bool = True, independent: bool = False,
+                 inputs=(), outputs=()):
+        """inputs: (device tensor, pinned host tensor) copied host -> device before the GEMVs;
+        outputs: (pinned host tensor, device tensor) copied device -> host after them; both
+        are captured into the step's graph (hqb_step_create_io)."""
         self.calls = list(calls)
         self.handle = None
         self.independent = independent
@@ -411,10 +424,30 @@ class Step:
             arr[i] = GemvCallC(ctypes.addressof(ms), prefix, _dtype_code(x), None, None, x.data_ptr(), x.shape[0], 0,
                                None, F32, _dtype_code(out), out.data_ptr(), flags, 0)
         self.arr = arr
+        if (inputs or outputs) and not graph:
+            raise ValueError("input/output copies need graph=True")
         if graph:
             h = vp()
-            create = lib().hqb_step_create_grouped if independent else lib().hqb_step_create
-            check(create(arr, len(self.calls), self.ws.ptr(), self.ws.nbytes, ctypes.byref(h)), "hqb_step_create")
+            if inputs or outputs:
+                for dst, src in [*inputs, *outputs]:
+                    if dst.numel() * dst.element_size() != src.numel() * src.element_size():
+                        raise ValueError("copy sizes differ")
+                    if not (dst.is_contiguous() and src.is_contiguous()):
+                        raise ValueError("copy buffers must be contiguous")
+                    host = src if src.device.type == "cpu" else dst
+                    if not host.is_pinned():
+                        raise ValueError("host buffers of a step must be pinned")
+                self._io = [*inputs, *outputs]
+                h2d = (CopyC * max(1, len(inputs)))(*[CopyC(d.data_ptr(), s_.data_ptr(), d.numel() * d.element_size())
+                                                      for d, s_ in inputs])
+                d2h = (CopyC * max(1, len(outputs)))(*[CopyC(d.data_ptr(), s_.data_ptr(), d.numel() * d.element_size())
+                                                       for d, s_ in outputs])
+                check(lib().hqb_step_create_io(arr, len(self.calls), self.ws.ptr(), self.ws.nbytes, h2d, len(inputs),
+                                               d2h, len(outputs), 1 if independent else 0, ctypes.byref(h)),
+                      "hqb_step_create_io")
+            else:
+                create = lib().hqb_step_create_grouped if independent else lib().hqb_step_create
+                check(create(arr, len(self.calls), self.ws.ptr(), self.ws.nbytes, ctypes.byref(h)), "hqb_step_create")
             self.handle = h.value
 
     def run(self, stream=None) -> None:
@@ -458,11 +491,13 @@ class RawMatrix:
             arr[i] = RawStageF32(c.data_ptr(), c.numel(), s.data_ptr(), s.numel())
         return arr
 
-    def gemv(self, x: torch.Tensor, prefix: int, bias: torch.Tensor | None = None, stream=None) -> torch.Tensor:
-        y = torch.empty(self.geom.original_rows, dtype=torch.float32, device=x.device)
-        check(lib().hqb_raw_gemv(ctypes.byref(self.geom), self._stages(), len(self.codes), prefix, _ptr(x), x.numel(),
-                                 _ptr(bias), 0 if bias is None else bias.numel(), _ptr(y), y.numel(), _stream(stream)),
-              "hqb_raw_gemv")
+    def gemv(self, x: torch.Tensor, prefix: int, bias: torch.Tensor | None = None, stream=None,
+             flags: int = 0, out: torch.Tensor | None = None) -> torch.Tensor:
+        """LaunchProgressiveGemv semantics (hqb_raw_gemv_ex); flags RAW_GENERIC / RAW_REQUIRE_FAST."""
+        y = out if out is not None else torch.empty(self.geom.original_rows, dtype=torch.float32, device=x.device)
+        check(lib().hqb_raw_gemv_ex(ctypes.byref(self.geom), self._stages(), len(self.codes), prefix, _ptr(x),
+                                    x.numel(), _ptr(bias), 0 if bias is None else bias.numel(), _ptr(y), y.numel(),
+                                    flags, _stream(stream)), "hqb_raw_gemv_ex")
         return y
 
     def dequantize_prefix(self, prefix: int, stream=None) -> torch.Tensor:

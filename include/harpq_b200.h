@@ -277,6 +277,22 @@ HQB_API int hqb_step_create(const hqb_gemv_call* calls, uint32_t count, void* wo
 /* The same for independent calls, captured as hqb_gemv_grouped (one kernel for the group). */
 HQB_API int hqb_step_create_grouped(const hqb_gemv_call* calls, uint32_t count, void* workspace,
                                     uint64_t workspace_bytes, hqb_step** step);
+
+/* One copy of a captured step: bytes from src to dst (cudaMemcpyDefault: host buffers must
+ * be page-locked, e.g. cudaHostAlloc, so that the copy can live in a CUDA graph). */
+typedef struct hqb_copy {
+  void* dst;
+  const void* src;
+  uint64_t bytes;
+} hqb_copy;
+
+/* A step that also moves its inputs and outputs: the n_h2d copies, then the GEMVs
+ * (grouped != 0: one grouped launch as hqb_step_create_grouped, else as hqb_step_create),
+ * then the n_d2h copies, all in the step's one CUDA graph.  A decode step that feeds
+ * host-resident activations and reads its results back is then one hqb_step_launch. */
+HQB_API int hqb_step_create_io(const hqb_gemv_call* calls, uint32_t count, void* workspace,
+                               uint64_t workspace_bytes, const hqb_copy* h2d, uint32_t n_h2d,
+                               const hqb_copy* d2h, uint32_t n_d2h, int grouped, hqb_step** step);
 HQB_API int hqb_step_launch(hqb_step* step, void* stream);
 HQB_API int hqb_step_destroy(hqb_step* step);
 
@@ -391,6 +407,19 @@ HQB_API int hqb_decode_planes(const hqb_plane_matrix* m, uint32_t prefix, const 
 HQB_API int hqb_raw_gemv(const hqb_geometry* g, const hqb_raw_stage* stages, uint32_t stage_count,
                          uint32_t prefix, const float* x, uint64_t x_count, const float* bias,
                          uint64_t bias_count, float* y, uint64_t y_count, void* stream);
+
+/* hqb_raw_gemv's kernel choice.  By default, 128x128 tiles with group 128 at prefix 1..4
+ * (8-byte aligned code arrays, at most 48K padded columns) run the int8-limb tensor-core
+ * kernel on the raw layout (raw_i8_kernel: no repack, no workspace, bits fixed by the
+ * shape); other geometries run the per-element FMA kernel (raw_gemv_kernel).
+ *   HQB_RAW_GENERIC       always the per-element FMA kernel.
+ *   HQB_RAW_REQUIRE_FAST  HQB_ERR_UNSUPPORTED (nothing enqueued) unless the int8 kernel
+ *                         applies. */
+#define HQB_RAW_GENERIC 1u
+#define HQB_RAW_REQUIRE_FAST 2u
+HQB_API int hqb_raw_gemv_ex(const hqb_geometry* g, const hqb_raw_stage* stages, uint32_t stage_count,
+                            uint32_t prefix, const float* x, uint64_t x_count, const float* bias,
+                            uint64_t bias_count, float* y, uint64_t y_count, uint32_t flags, void* stream);
 
 /* out[rows][cols] = code·scale of one stage, the exact FP32 product
  * (DequantizeStage, native/src/stage_codec.cpp:218-252).  Scales are FP32. */

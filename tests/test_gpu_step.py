@@ -96,3 +96,47 @@ def test_grouped_launch_matches_single_calls(batch, x_dtype):
         e64 = (x.double() @ pm.decode(2).double().T).cpu().numpy()
         assert_close(y.cpu().numpy(), e64, 2e-4, 2e-4, "grouped vs FP64")
     assert ws.error_flags() == 0
+
+
+@pytest.mark.parametrize("independent", [False, True])
+def test_step_with_captured_host_copies(independent):
+    """hqb_step_create_io: the step's graph copies pinned host x in, runs the GEMVs and
+    copies y out; each launch moves the host buffers' current contents."""
+    import harpq_b200 as hqb
+
+    rng = np.random.default_rng(77)
+    shapes = [(768, 512), (1024, 1000), (300, 512)]
+    pms = [plane_matrix(random_matrix(rng, r, c, stages=2)) for r, c in shapes]
+    cols = [c for _, c in shapes]
+    rows = [r for r, _ in shapes]
+    x_all = torch.empty(sum(cols), dtype=torch.float16, device="cuda")
+    y_all = torch.empty(sum(rows), dtype=torch.float16, device="cuda")
+    xs, ys, o = [], [], 0
+    for c in cols:
+        xs.append(x_all[o:o + c].view(1, c))
+        o += c
+    o = 0
+    for r in rows:
+        ys.append(y_all[o:o + r].view(1, r))
+        o += r
+    hx = torch.empty(sum(cols), dtype=torch.float16).pin_memory()
+    hy = torch.empty(sum(rows), dtype=torch.float16).pin_memory()
+    ws = hqb.Workspace(max(pm.workspace_bytes(1, hqb.F16) for pm in pms))
+    step = hqb.Step([(pm, x, 2, y, hqb.FLAG_PDL) for pm, x, y in zip(pms, xs, ys)], ws, independent=independent,
+                    inputs=[(x_all, hx)], outputs=[(hy, y_all)])
+    for trial in range(3):
+        hx.copy_(torch.from_numpy(rng.standard_normal(sum(cols)).astype(np.float16)))
+        hy.fill_(float("nan"))
+        step.run()
+        torch.cuda.synchronize()
+        xd = hx.cuda()
+        want, o = [], 0
+        for pm, c in zip(pms, cols):
+            want.append(pm.gemv(xd[o:o + c].view(1, c), prefix=2, y_dtype=torch.float16, workspace=ws))
+            o += c
+        assert torch.equal(hy, torch.cat(want, dim=1).view(-1).cpu()), f"trial {trial}"
+    step.close()
+    assert ws.error_flags() == 0
+    # pageable host memory cannot sit in the graph
+    with pytest.raises(ValueError):
+        hqb.Step([(pms[0], xs[0], 2, ys[0], 0)], ws, inputs=[(x_all, torch.empty(sum(cols), dtype=torch.float16))])
