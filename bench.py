@@ -910,6 +910,27 @@ def run_reference_arm(args, device):
 
 # ---------------------------------------------------------------------------------------
 
+def profile_steps(args, device) -> int:
+    """The workload's grouped step run eagerly args.ncu_steps times (hqb_gemv_grouped, one
+    launch per step, rotating weight copies): a short, plain command for a profiler to
+    capture (`ncu -k regex:gemv_grouped -s <warm-up> -c 1 python bench.py --ncu-steps 6`)."""
+    import harpq_b200 as hqb
+
+    prefix, groups, _, ncopies, _ = build_workload(args.workload, 0, 1, device, 3 * L2_BYTES)
+    gen = torch.Generator(device=device)
+    gen.manual_seed(7)
+    xs = {g["src"]: torch.randn(1, g["cols"], generator=gen, device=device).half() for g in groups}
+    ys = {g["name"]: torch.empty(1, g["nrows"], dtype=torch.float16, device=device) for g in groups}
+    ws = hqb.Workspace(max(g["copies"][0].workspace_bytes(1, hqb.F16) for g in groups), device)
+    steps = [hqb.Step([(G["copies"][c], xs[G["src"]], prefix, ys[G["name"]], hqb.FLAG_PDL) for G in groups], ws,
+                      graph=False, independent=True) for c in range(ncopies)]
+    for i in range(args.ncu_steps):
+        steps[i % ncopies].run()
+    torch.cuda.synchronize()
+    print(f"{args.ncu_steps} grouped steps of {args.workload}; device error flags {ws.error_flags()}")
+    return 0
+
+
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser(description=__doc__)
     ap.add_argument("--gpus", type=int, default=1)
@@ -925,6 +946,9 @@ def main(argv=None) -> int:
                     help="N = 1: the step's independent GEMVs as one grouped launch, or one launch per group")
     ap.add_argument("--fused-gather", action="store_true",
                     help="N > 1: gather outputs with the fused P2P gather instead of NCCL all_gather_into_tensor")
+    ap.add_argument("--ncu-steps", type=int, default=0,
+                    help="N = 1, for profiler captures: build the workload, run this many grouped steps "
+                         "eagerly (no graph, no timing, no JSON line) and exit")
     args = ap.parse_args(argv)
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -951,6 +975,8 @@ def main(argv=None) -> int:
                                              device_id=device)
     import harpq_b200  # noqa: F401  (fails loudly when the library is missing)
 
+    if args.ncu_steps > 0:
+        return profile_steps(args, device)
     result = run_ours(args, rank, world, device)
     if rank == 0 and world == 1 and not args.no_extras:
         result["supplementary"] = supplementary(device)

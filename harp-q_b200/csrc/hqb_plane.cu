@@ -2,9 +2,11 @@
 //
 //   repack_kernel        reference row-major stage -> plane records (one per tile)
 //   prep_x_kernel        activations -> per-tile FP16 tensor-core B fragments + correction sums
-//   prep_x_i8_kernel     FP16/FP32 activations -> per-tile int8 limbs + {L, K} epilogue constants
-//   gemv_uniform_kernel  stream-K GEMV with a per-warp register ring (uniform prefix, or a
-//                        depth map on the int8 form); split tile rows finished in-kernel
+//   gemv_uniform_kernel  stream-K GEMV with a per-warp register ring (uniform prefix; the
+//                        int8 form runs lean_body); split tile rows finished in-kernel
+//   gemv_unit_kernel     stream-K GEMV for a depth map on the int8 form, one (tile, stage)
+//                        unit per ring slot
+//   gemv_grouped_kernel  independent GEMVs in one launch (lean_body per problem)
 //   gemv_rows_kernel     row-block GEMV for small layers (no tile row split between CTAs)
 //   gemv_stream_kernel   depth maps where the int8 form does not apply
 //   gemv_kernel          warp-specialised, bulk-copy pipelined GEMV (tensor-core or CUDA-core
@@ -97,23 +99,6 @@ __global__ void __launch_bounds__(256) repack_kernel(const uint8_t* __restrict__
   }
 }
 
-
-// x [batch][cols] (FP16 or FP32) -> one limb slot per 128-column tile; one warp per
-// (tile column, batch row) item, four items per block.
-template <typename XT>
-__global__ void __launch_bounds__(128) prep_x_i8_kernel(const XT* __restrict__ x, uint32_t cols, uint32_t batch,
-                                                        uint32_t C, uint8_t* __restrict__ xfrag, uint32_t xslot,
-                                                        uint32_t vec) {
-  const uint32_t item = blockIdx.x * 4 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
-  if (item >= C * batch) return;  // the whole warp leaves together
-  const uint32_t c = item / batch;
-  float v[1][4];
-  const bool ok[1] = {true};
-  uint8_t* const slot[1] = {xfrag + static_cast<uint64_t>(c) * xslot};
-  const uint32_t b[1] = {item - c * batch};
-  load_x4<XT>(x + static_cast<uint64_t>(b[0]) * cols, c * 128 + 4 * lane, cols, vec != 0, v[0]);
-  prep_i8_items<1>(v, ok, slot, b, batch, lane);
-}
 
 // x [batch][cols] -> one fragment slot per 128-column tile; one warp per (tile column,
 // batch row) item, four items per block.
@@ -1372,6 +1357,183 @@ __device__ __forceinline__ void lean_body(const GemvParams& p, const uint32_t ct
   if (p.g_world > 1) gather_signal(p, ctas);
 }
 
+// Per-tile depth maps at batch <= 2 with raw x (or prepared limb slots): the lean body's
+// register ring with one (tile, stage) unit per slot, so a warp keeps 8 row-block records
+// in flight whatever the depths.  The CTA's units [u0, u1) come from the depth plan
+// (mixed_range); the walk goes down the tiles, t_end first, and up the stages inside a
+// tile (the uniform kernels' order of stage sums).  The loader runs 8 units ahead of the
+// math: it finds each unit's stage plane and tile from the depths (a 32-tile window per
+// warp in registers, the next window loaded 32 tiles early) and leaves the math, per slot,
+// the unit's limb slot and whether a tile row ends after it.
+template <int XL, bool B1>
+__device__ __forceinline__ void unit_body(const GemvParams& p, const uint32_t cta) {
+  constexpr int R = 8;
+  constexpr uint32_t XS = kLimbs * (B1 ? 1u : 2u) * 128u + 80u;  // xslot_i8_bytes(batch)
+  constexpr uint32_t kWideOff = kLimbs * (B1 ? 1u : 2u) * 128u + 64u;
+  constexpr uint32_t kRowEnd = 0x80000000u;
+  extern __shared__ __align__(16) uint8_t xres[];
+  const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, q = lane & 3;
+  const MixedRange rg = mixed_range(p, cta, lane);
+  griddep_launch_dependents();  // a following PDL kernel may be scheduled; it waits for this grid
+  if (cta >= rg.ctas) return;
+  const uint64_t total = rg.total, u0 = rg.u0, u1 = rg.u1;
+  const uint32_t ctas = rg.ctas, C = p.C;
+  const uint32_t t0 = rg.t0, s0 = rg.s0, t_end = rg.t_end, s_end = rg.s_end;
+  const uint32_t ntiles = t_end - t0 + 1;
+  const uint32_t n = static_cast<uint32_t>(u1 - u0);  // this CTA's units
+  const uint32_t row_first = t0 / C, row_last = t_end / C;
+  const uint64_t rb_first = rg.rb_first, re_last = rg.re_last;
+  const uint32_t rit0 = warp * 16 + g;
+  const uint32_t c_first = t0 % C;
+  const uint32_t lane_off = warp * kRowBlockBytes + lane * 16;
+  const uint32_t scale_rel = 512 + g * 4 - lane * 16;
+  const uint64_t l2_first = policy_evict_first();
+  const uint8_t* pb0 = p.planes[0] + lane_off;
+  const uint8_t* pb1 = p.planes[1] + lane_off;
+  const uint8_t* pb2 = p.planes[2] + lane_off;
+  const uint8_t* pb3 = p.planes[3] + lane_off;
+
+  // Depth window: lane i holds the depth of tile wtop - i (0 below t0).
+  auto load_win = [&](uint32_t top) -> uint32_t {
+    return (top >= lane && top - lane >= t0) ? clamp_depth(__ldg(p.depth + (top - lane)), p.stage_count) : 0u;
+  };
+  uint32_t wtop = t_end;
+  uint32_t dwin = load_win(wtop);
+  uint32_t dnext = wtop >= t0 + 32 ? load_win(wtop - 32) : 0u;
+  auto depth_of = [&](uint32_t t) -> uint32_t {  // t = the previous tile asked for, minus one
+    if (wtop - t >= 32) {
+      wtop -= 32;
+      dwin = dnext;
+      dnext = wtop >= t0 + 32 ? load_win(wtop - 32) : 0u;
+    }
+    return __shfl_sync(0xffffffffu, dwin, wtop - t);
+  };
+
+  // Loader: the unit the next refill loads (tile lt, stage ls of [.., lend)), its tile
+  // column and limb slot offset.
+  const uint32_t x_top = (C - 1) * XS;
+  uint32_t lt = t_end, ls = t_end == t0 ? s0 : 0u, lend = s_end;
+  uint32_t lcol = t_end % C;
+  uint32_t lxoff = resident_slot(lcol, c_first, C) * XS;
+  uint4 w[R];
+  uint32_t sc[R], meta[R];
+  auto refill = [&](int j) {
+    const uint8_t* b = ls == 0 ? pb0 : (ls == 1 ? pb1 : (ls == 2 ? pb2 : pb3));
+    const uint8_t* a = b + static_cast<uint64_t>(lt) * kRecordBytes;
+    ld_plane(w[j], sc[j], a, a + scale_rel, l2_first);
+    const bool last = ls + 1 == lend;
+    meta[j] = lxoff | (last && lcol == 0 ? kRowEnd : 0u);
+    if (!last) {
+      ++ls;
+    } else if (lt > t0) {
+      --lt;
+      ls = lt == t0 ? s0 : 0u;
+      lend = depth_of(lt);
+      lxoff = lxoff == 0 ? x_top : lxoff - XS;
+      lcol = lcol == 0 ? C - 1 : lcol - 1;
+    }
+  };
+#pragma unroll
+  for (int j = 0; j < R; ++j)
+    if (static_cast<uint32_t>(j) < n) refill(j);
+  griddep_wait();
+  if (min(C, ntiles) > p.x_res_slots) {  // the launch sized shared memory for fewer slots
+    if (threadIdx.x == 0) atomicOr(p.error, HQB_DEVERR_LAUNCH);
+    return;
+  }
+  const ColRanges cr = needed_columns(t0, t_end, C);
+  if (p.x_raw != nullptr) {
+    build_limb_slots<XL, kStreamThreads / 32>(p, xres, reinterpret_cast<float*>(xres + p.x_res_slots * XS) + warp * 128,
+                                              cr, c_first, warp, lane);
+  } else {  // slots prepared by one launch for all CTAs (prep_limbs_kernel)
+    constexpr uint32_t per_slot = XS / 16;
+    const uint32_t chunks = cr.count() * per_slot;
+    for (uint32_t t = threadIdx.x; t < chunks; t += kStreamThreads) {
+      const uint32_t ci = t / per_slot, k = t - ci * per_slot, c = cr.col(ci);
+      const uint4* src = reinterpret_cast<const uint4*>(p.xfrag + static_cast<uint64_t>(c) * XS) + k;
+      reinterpret_cast<uint4*>(xres + resident_slot(c, c_first, C) * XS)[k] = __ldcg(src);
+    }
+  }
+  __syncthreads();
+
+  const XLaneI8 xl8(B1 ? 1u : 2u, lane);
+  const uint32_t xres_a = smem_u32(xres);
+  bool any_wide = false;
+  for (uint32_t i = lane; i < cr.count() * (B1 ? 1u : 2u); i += 32) {
+    const uint32_t c = cr.col(B1 ? i : i >> 1), b = B1 ? 0u : (i & 1u);
+    const float k = __uint_as_float(
+        lds32a(xres_a + resident_slot(c, c_first, C) * XS + kLimbs * (B1 ? 1u : 2u) * 128u + (2u * b + 1u) * 4u));
+    any_wide = any_wide || !(k < 0.0f);
+  }
+  any_wide = __any_sync(0xffffffffu, any_wide);
+
+  uint32_t row = t_end / C;
+  float y[1][4] = {{0.0f, 0.0f, 0.0f, 0.0f}};
+  float kept[1][4];
+  bool keep = false;
+  // limbs of the current tile: consecutive units of one tile (its stages) share them
+  XFragI8 xf;
+  uint32_t xf_off = 0xffffffffu;
+  auto unit_math = [&](int j, uint32_t xo, auto wide_tag) {
+    constexpr bool WIDE = decltype(wide_tag)::value;
+    if (xo != xf_off) {
+      load_limbs<B1>(xf, xres_a + xo + xl8.frag, xres_a + xo + xl8.cst);
+      xf_off = xo;
+    }
+    uint32_t acc[2][4];
+    const uint4(&wj)[1] = *reinterpret_cast<const uint4(*)[1]>(&w[j]);
+    const uint32_t(&sj)[1] = *reinterpret_cast<const uint32_t(*)[1]>(&sc[j]);
+    bulk_tile_mma<1, false>(wj, xf, acc, 1u);
+    if (!WIDE || (xf.K[0] < 0.0f && (B1 || xf.K[1] < 0.0f))) {
+      bulk_tile_epilogue<1, B1, false>(sj, xf, acc, y, 1u);
+    } else {
+      const float f0 = __uint_as_float(lds32a(xres_a + xo + kWideOff));
+      const float f1 = B1 ? 1.0f : __uint_as_float(lds32a(xres_a + xo + kWideOff + 4));
+      bulk_tile_epilogue_wide<1, B1, false>(sj, xf, acc, y, 1u, f0, f1);
+    }
+  };
+  auto flush_row = [&]() {
+    quad_sum<B1>(y);
+    const uint64_t rb = row == row_first ? rb_first : u0, re = row == row_last ? re_last : u1;
+    if (rb >= u0 && re <= u1) {
+      store_out<1>(p, y, row * 128 + rit0, q);
+    } else if (re > u1) {
+      publish_flagged<1>(p, cta, y, rit0, q);
+    } else {
+      keep = true;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) kept[0][e] = y[0][e];
+    }
+#pragma unroll
+    for (int e = 0; e < 4; ++e) y[0][e] = 0.0f;
+    --row;
+  };
+
+  // One loop for all units: a refill only where a unit remains R ahead (no unit needs a mask).
+  auto main_loop = [&](auto wide_tag) {
+    for (uint32_t k0 = 0; k0 < n; k0 += R) {
+#pragma unroll
+      for (int j = 0; j < R; ++j) {
+        const uint32_t k = k0 + j;
+        if (k >= n) break;
+        const uint32_t m = meta[j];
+        unit_math(j, m & ~kRowEnd, wide_tag);
+        if (k + R < n) refill(j);
+        if ((m & kRowEnd) || k + 1 == n) flush_row();
+      }
+    }
+  };
+  if (any_wide) main_loop(std::true_type{});
+  else main_loop(std::false_type{});
+  if (keep) reduce_split_row<1, B1>(p, row_first, rb_first, total, ctas, cta, kept, rit0, q);
+  if (p.g_world > 1) gather_signal(p, ctas);
+}
+
+template <int XL, bool B1>
+__global__ void __launch_bounds__(kStreamThreads, 2) gemv_unit_kernel(const __grid_constant__ GemvParams p) {
+  unit_body<XL, B1>(p, blockIdx.x);
+}
+
 template <int NB, int XL, int D, bool B1 = false, bool I8 = false, bool MX = false>
 __global__ void __launch_bounds__(kStreamThreads, (NB == 1 && (XL == 1 || I8)) ? 2 : 1)
     gemv_uniform_kernel(const __grid_constant__ GemvParams p) {
@@ -2183,11 +2345,8 @@ GemvKernel pick_uniform_i8(uint32_t d) {
 }
 
 GemvKernel pick_mixed_i8(uint32_t batch, uint32_t xl) {
-  if (xl == 1)
-    return batch == 1 ? gemv_uniform_kernel<1, 1, HQB_MAX_STAGES, true, true, true>
-                      : gemv_uniform_kernel<1, 1, HQB_MAX_STAGES, false, true, true>;
-  return batch == 1 ? gemv_uniform_kernel<1, 2, HQB_MAX_STAGES, true, true, true>
-                    : gemv_uniform_kernel<1, 2, HQB_MAX_STAGES, false, true, true>;
+  if (xl == 1) return batch == 1 ? gemv_unit_kernel<1, true> : gemv_unit_kernel<1, false>;
+  return batch == 1 ? gemv_unit_kernel<2, true> : gemv_unit_kernel<2, false>;
 }
 
 GemvKernel pick_uniform_kernel(uint32_t nb, uint32_t xl, uint32_t d, uint32_t batch, bool i8) {
@@ -2328,21 +2487,6 @@ cudaError_t launch_tc(const GemvParams& p, uint32_t grid, uint32_t smem, bool pd
 // a multiple of 16 bytes.
 bool x_rows_vec(const void* x, uint64_t cols, uint32_t xl) {
   return (reinterpret_cast<uintptr_t>(x) & 15u) == 0 && (cols * (xl == 1 ? 2 : 4)) % 16 == 0;
-}
-
-cudaError_t launch_prep_i8(const void* x, int x_dtype, uint64_t cols, uint32_t batch, void* xfrag, cudaStream_t st) {
-  const uint32_t C = static_cast<uint32_t>((cols + 127) / 128);
-  const uint32_t blocks = (C * batch + 3) / 4;  // one warp per (tile column, batch row)
-  const uint32_t xl = x_dtype == HQB_F32 ? 2 : 1;
-  const uint32_t vec = x_rows_vec(x, cols, xl) ? 1u : 0u;
-  if (x_dtype == HQB_F32)
-    prep_x_i8_kernel<float><<<blocks, 128, 0, st>>>(static_cast<const float*>(x), static_cast<uint32_t>(cols), batch,
-                                                    C, static_cast<uint8_t*>(xfrag), xslot_i8_bytes(batch), vec);
-  else
-    prep_x_i8_kernel<__half><<<blocks, 128, 0, st>>>(static_cast<const __half*>(x), static_cast<uint32_t>(cols),
-                                                     batch, C, static_cast<uint8_t*>(xfrag), xslot_i8_bytes(batch),
-                                                     vec);
-  return cudaGetLastError();
 }
 
 cudaError_t launch_prep(const void* x, int x_dtype, uint64_t cols, uint32_t batch, void* xfrag, cudaStream_t st) {
@@ -2712,11 +2856,9 @@ int gemv_impl(const hqb_plane_matrix* m, uint32_t prefix, const uint8_t* depth, 
   const uint64_t avg_tiles = static_cast<uint64_t>(m->grid_rows) * m->grid_cols / (static_cast<uint64_t>(sms) * 2);
   const bool fuse_prep = !x_prepared && (rows_path || (streaming && (!mixed || mx) && avg_tiles <= kFusedTilesMax));
   if (!x_prepared && !fuse_prep && info == nullptr) {
-    // the int8 uniform stream-K kernel (lean form) reads limb_item slots; the depth-map form
-    // the register-ring builder's
-    e = (i8 && !mixed) ? launch_prep_limbs(x, x_dtype, m->cols, batch, ws + L.xfrag, (flags & HQB_FLAG_PDL) != 0, st)
-        : i8           ? launch_prep_i8(x, x_dtype, m->cols, batch, ws + L.xfrag, st)
-                       : launch_prep(x, x_dtype, m->cols, batch, ws + L.xfrag, st);
+    // the int8 stream-K kernels (lean uniform and unit depth-map bodies) read limb_item slots
+    e = i8 ? launch_prep_limbs(x, x_dtype, m->cols, batch, ws + L.xfrag, (flags & HQB_FLAG_PDL) != 0, st)
+           : launch_prep(x, x_dtype, m->cols, batch, ws + L.xfrag, st);
     if (e != cudaSuccess) {
       cudaGetLastError();
       return e;
@@ -2786,7 +2928,7 @@ int gemv_impl(const hqb_plane_matrix* m, uint32_t prefix, const uint8_t* depth, 
     p.x_res_slots = res_slots;
     smem = !streaming          ? rs.smem
            : (mixed && !mx)    ? static_cast<uint32_t>(x_all_bytes) + 256
-           : (i8 && !mixed)    ? res_slots * xslot + (kStreamThreads / 32) * 512 + 256  // + limb transpose areas
+           : i8                ? res_slots * xslot + (kStreamThreads / 32) * 512 + 256  // + limb transpose areas
                                : res_slots * xslot + 256;
     threads = streaming ? kStreamThreads : kGemvThreads;
   }
@@ -2800,6 +2942,7 @@ int gemv_impl(const hqb_plane_matrix* m, uint32_t prefix, const uint8_t* depth, 
     const char* name = rows_path ? "gemv_rows_kernel"
                        : !streaming ? "gemv_kernel"
                        : (mixed && !mx) ? "gemv_stream_kernel"
+                       : mx             ? "gemv_unit_kernel"
                                         : "gemv_uniform_kernel";
     return describe(name, (!x_prepared && !fuse_prep ? 1u : 0u) + 1u + (fix ? 1u : 0u), i8, grid, threads, smem);
   }
@@ -3103,107 +3246,6 @@ HQB_API int hqb_gemv_grouped(const hqb_gemv_call* calls, uint32_t count, void* w
   const int st = grouped_launch(calls, count, workspace, workspace_bytes, stream);
   if (st != HQB_ERR_UNSUPPORTED) return st;
   return hqb_gemv_batch(calls, count, workspace, workspace_bytes, stream);  // one by one
-}
-
-
-}  // extern "C"
-
-// A captured decode step: the CUDA graph of a batch of GEMV calls.
-struct hqb_step {
-  cudaGraph_t graph = nullptr;
-  cudaGraphExec_t exec = nullptr;
-};
-
-extern "C" {
-
-namespace {
-int step_create(const hqb_gemv_call* calls, uint32_t count, void* workspace, uint64_t workspace_bytes, hqb_step** step,
-                bool grouped, const hqb_copy* h2d = nullptr, uint32_t n_h2d = 0, const hqb_copy* d2h = nullptr,
-                uint32_t n_d2h = 0);
-}
-
-HQB_API int hqb_step_create(const hqb_gemv_call* calls, uint32_t count, void* workspace, uint64_t workspace_bytes,
-                            hqb_step** step) {
-  return step_create(calls, count, workspace, workspace_bytes, step, false);
-}
-
-HQB_API int hqb_step_create_grouped(const hqb_gemv_call* calls, uint32_t count, void* workspace,
-                                    uint64_t workspace_bytes, hqb_step** step) {
-  return step_create(calls, count, workspace, workspace_bytes, step, true);
-}
-
-HQB_API int hqb_step_create_io(const hqb_gemv_call* calls, uint32_t count, void* workspace, uint64_t workspace_bytes,
-                               const hqb_copy* h2d, uint32_t n_h2d, const hqb_copy* d2h, uint32_t n_d2h, int grouped,
-                               hqb_step** step) {
-  if ((n_h2d != 0 && h2d == nullptr) || (n_d2h != 0 && d2h == nullptr)) return HQB_ERR_INVALID;
-  for (uint32_t i = 0; i < n_h2d; ++i)
-    if (h2d[i].dst == nullptr || h2d[i].src == nullptr) return HQB_ERR_INVALID;
-  for (uint32_t i = 0; i < n_d2h; ++i)
-    if (d2h[i].dst == nullptr || d2h[i].src == nullptr) return HQB_ERR_INVALID;
-  return step_create(calls, count, workspace, workspace_bytes, step, grouped != 0, h2d, n_h2d, d2h, n_d2h);
-}
-
-}  // extern "C"
-
-namespace {
-int step_create(const hqb_gemv_call* calls, uint32_t count, void* workspace, uint64_t workspace_bytes, hqb_step** step,
-                bool grouped, const hqb_copy* h2d, uint32_t n_h2d, const hqb_copy* d2h, uint32_t n_d2h) {
-  if (step == nullptr || calls == nullptr || count == 0) return HQB_ERR_INVALID;
-  *step = nullptr;
-  const cudaError_t prior = take_prior_error();
-  if (prior != cudaSuccess) return prior;
-  cudaStream_t s = nullptr;
-  cudaError_t e = cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking);
-  if (e != cudaSuccess) return e;
-  hqb_step* st = new (std::nothrow) hqb_step();
-  if (st == nullptr) {
-    cudaStreamDestroy(s);
-    return cudaErrorMemoryAllocation;
-  }
-  int status = cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal);
-  if (status == cudaSuccess) {
-    // the step's input copies, its GEMVs, its output copies: one cudaMemcpyAsync per copy
-    for (uint32_t i = 0; i < n_h2d && status == cudaSuccess; ++i)
-      status = cudaMemcpyAsync(h2d[i].dst, h2d[i].src, h2d[i].bytes, cudaMemcpyDefault, s);
-    if (status == cudaSuccess)
-      status = grouped ? hqb_gemv_grouped(calls, count, workspace, workspace_bytes, s)
-                       : hqb_gemv_batch(calls, count, workspace, workspace_bytes, s);
-    for (uint32_t i = 0; i < n_d2h && status == cudaSuccess; ++i)
-      status = cudaMemcpyAsync(d2h[i].dst, d2h[i].src, d2h[i].bytes, cudaMemcpyDefault, s);
-    cudaGraph_t g = nullptr;
-    const cudaError_t end = cudaStreamEndCapture(s, &g);  // always end the capture
-    if (status == HQB_OK) status = end;
-    st->graph = g;
-    if (status == HQB_OK) status = cudaGraphInstantiate(&st->exec, g, 0);
-  }
-  cudaStreamDestroy(s);
-  if (status != HQB_OK) {
-    if (st->exec != nullptr) cudaGraphExecDestroy(st->exec);
-    if (st->graph != nullptr) cudaGraphDestroy(st->graph);
-    delete st;
-    cudaGetLastError();
-    return status;
-  }
-  *step = st;
-  return HQB_OK;
-}
-}  // namespace
-
-extern "C" {
-
-HQB_API int hqb_step_launch(hqb_step* step, void* stream) {
-  if (step == nullptr || step->exec == nullptr) return HQB_ERR_INVALID;
-  const cudaError_t prior = take_prior_error();
-  if (prior != cudaSuccess) return prior;
-  return cudaGraphLaunch(step->exec, as_stream(stream));
-}
-
-HQB_API int hqb_step_destroy(hqb_step* step) {
-  if (step == nullptr) return HQB_ERR_INVALID;
-  if (step->exec != nullptr) cudaGraphExecDestroy(step->exec);
-  if (step->graph != nullptr) cudaGraphDestroy(step->graph);
-  delete step;
-  return HQB_OK;
 }
 
 HQB_API int hqb_gemv(const hqb_plane_matrix* m, uint32_t prefix, const void* x, int x_dtype, uint32_t batch,

@@ -567,7 +567,7 @@ def test_int8_limb_kernel_depth_map(rows, cols, batch):
 def test_register_ring_int8_fp32_paths(batch):
     """The register-ring int8 kernels with FP32 activations (forced with HQB_FLAG_STREAMK;
     FP32 x takes the bulk kernel by default): the depth-map form, and a layer large enough
-    for the standalone limb preparation launch (prep_x_i8_kernel<float>, more than 24 tiles
+    for the standalone limb preparation launch (prep_limbs_kernel<float>, more than 24 tiles
     per CTA on average).  Against the scalar-order oracle / FP64."""
     import harpq_b200 as hqb
 
@@ -581,7 +581,7 @@ def test_register_ring_int8_fp32_paths(batch):
     xt = torch.from_numpy(x).cuda()
     fl = hqb.FLAG_STREAMK
     assert pm.uses_int8_limbs(batch, hqb.F32, 0, mixed=True, flags=fl)
-    assert pm.gemv_kernel(batch, hqb.F32, 0, mixed=True, flags=fl) == "gemv_uniform_kernel"
+    assert pm.gemv_kernel(batch, hqb.F32, 0, mixed=True, flags=fl) == "gemv_unit_kernel"
     y = pm.gemv(xt, depth=plan, y_dtype=torch.float32, flags=fl).cpu().numpy()
     assert_close(y, orc.linear_mixed(m, x, depth), 2e-4, 2e-4, f"depth map FP32 b{batch}")
     assert rel_l2(y, _fp64_reference(m, x, 4, depth=depth)) <= 2e-5

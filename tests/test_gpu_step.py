@@ -136,6 +136,17 @@ def test_step_with_captured_host_copies(independent):
             o += c
         assert torch.equal(hy, torch.cat(want, dim=1).view(-1).cpu()), f"trial {trial}"
     step.close()
+    # host buffers 2 bytes past a 16-byte boundary: the copies fall back to cudaMemcpyAsync
+    hx2 = torch.empty(sum(cols) + 8, dtype=torch.float16).pin_memory()[1:1 + sum(cols)]
+    hy2 = torch.empty(sum(rows) + 8, dtype=torch.float16).pin_memory()[1:1 + sum(rows)]
+    step = hqb.Step([(pm, x, 2, y, hqb.FLAG_PDL) for pm, x, y in zip(pms, xs, ys)], ws, independent=independent,
+                    inputs=[(x_all, hx2)], outputs=[(hy2, y_all)])
+    hx2.copy_(hx)
+    hy2.fill_(float("nan"))
+    step.run()
+    torch.cuda.synchronize()
+    assert torch.equal(hy2, hy)
+    step.close()
     assert ws.error_flags() == 0
     # pageable host memory cannot sit in the graph
     with pytest.raises(ValueError):
