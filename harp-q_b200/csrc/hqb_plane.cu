@@ -1471,15 +1471,10 @@ __device__ __forceinline__ void unit_body(const GemvParams& p, const uint32_t ct
   float y[1][4] = {{0.0f, 0.0f, 0.0f, 0.0f}};
   float kept[1][4];
   bool keep = false;
-  // limbs of the current tile: consecutive units of one tile (its stages) share them
-  XFragI8 xf;
-  uint32_t xf_off = 0xffffffffu;
   auto unit_math = [&](int j, uint32_t xo, auto wide_tag) {
     constexpr bool WIDE = decltype(wide_tag)::value;
-    if (xo != xf_off) {
-      load_limbs<B1>(xf, xres_a + xo + xl8.frag, xres_a + xo + xl8.cst);
-      xf_off = xo;
-    }
+    XFragI8 xf;
+    load_limbs<B1>(xf, xres_a + xo + xl8.frag, xres_a + xo + xl8.cst);
     uint32_t acc[2][4];
     const uint4(&wj)[1] = *reinterpret_cast<const uint4(*)[1]>(&w[j]);
     const uint32_t(&sj)[1] = *reinterpret_cast<const uint32_t(*)[1]>(&sc[j]);
@@ -1509,9 +1504,21 @@ __device__ __forceinline__ void unit_body(const GemvParams& p, const uint32_t ct
     --row;
   };
 
-  // One loop for all units: a refill only where a unit remains R ahead (no unit needs a mask).
+  // Steady state: groups of R units whose refills are all units of this CTA (no tests but
+  // the row end); then the rest, refilled only where a unit remains R ahead (no unit needs a
+  // mask, so the rest is the same loop with those tests).
   auto main_loop = [&](auto wide_tag) {
-    for (uint32_t k0 = 0; k0 < n; k0 += R) {
+    uint32_t k0 = 0;
+    for (; k0 + 2 * R <= n; k0 += R) {
+#pragma unroll
+      for (int j = 0; j < R; ++j) {
+        const uint32_t m = meta[j];
+        unit_math(j, m & ~kRowEnd, wide_tag);
+        refill(j);
+        if (m & kRowEnd) flush_row();
+      }
+    }
+    for (; k0 < n; k0 += R) {
 #pragma unroll
       for (int j = 0; j < R; ++j) {
         const uint32_t k = k0 + j;
