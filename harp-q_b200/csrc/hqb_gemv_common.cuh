@@ -926,11 +926,12 @@ __device__ __forceinline__ void bulk_tile_epilogue(const uint32_t (&sc)[D], cons
   }
 }
 
-// Limb slots of the tile columns a CTA touches, built from raw x by WARPS warps.  Every
-// CTA reads the same few KB of x at once, so the reads are L2-slice bound: each lane loads
-// four consecutive activations (one 8- or 16-byte load, no sector read twice), a per-warp
-// 512-byte shared-memory area turns them into limb_item's column order, and up to four
-// items per warp are loaded before any is transformed.
+// Limb slots of the tile columns a CTA touches, built from raw x by WARPS warps.  Each
+// lane loads four consecutive activations (one 8- or 16-byte load, no sector read twice),
+// a per-warp 512-byte shared-memory area turns them into limb_item's column order, and the
+// next item's load is in flight while the current one is transformed.  The loop is kept
+// rolled: it runs once per launch from a cold instruction cache, where a compact body
+// (one limb_item) costs less than unrolled ones.
 template <int XL, uint32_t WARPS>
 __device__ __forceinline__ void build_limb_slots(const GemvParams& p, uint8_t* xres, float* scratch,
                                                  const ColRanges& cr, uint32_t c_first, uint32_t warp, uint32_t lane) {
@@ -939,30 +940,33 @@ __device__ __forceinline__ void build_limb_slots(const GemvParams& p, uint8_t* x
   const uint32_t items = cr.count() * p.batch;
   const uint32_t q = lane >> 3, m = (lane >> 1) & 3u, h = lane & 1u;
   const uint32_t col_lane = 32u * q + 16u * h + m;  // limb_item's columns: col_lane + 4j
-  constexpr uint32_t W = 4;
-  for (uint32_t base = warp; base < items; base += W * WARPS) {
-    float v4[W][4];
-    uint32_t c[W], b[W];
+  auto fetch = [&](uint32_t it, float (&v)[4], uint32_t& c, uint32_t& b) {
+    const uint32_t ci = p.batch == 1 ? it : it >> 1;  // batch <= 2
+    b = it - ci * p.batch;
+    c = cr.col(ci);
+    load_x4<XT>(x + static_cast<uint64_t>(b) * p.cols, c * 128 + 4 * lane, p.cols, p.x_vec != 0, v);
+  };
+  uint32_t it = warp;
+  if (it >= items) return;
+  float v[4];
+  uint32_t c, b;
+  fetch(it, v, c, b);
+#pragma unroll 1
+  for (; it < items; it += WARPS) {
+    float vn[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    uint32_t cn = 0, bn = 0;
+    if (it + WARPS < items) fetch(it + WARPS, vn, cn, bn);
+    *reinterpret_cast<float4*>(scratch + 4 * lane) = make_float4(v[0], v[1], v[2], v[3]);
+    __syncwarp();
+    float u[4];
 #pragma unroll
-    for (uint32_t w = 0; w < W; ++w) {
-      const uint32_t it = base + w * WARPS;
-      const uint32_t ci = it < items ? it / p.batch : 0u;
-      b[w] = it < items ? it - ci * p.batch : 0u;
-      c[w] = cr.col(ci);
-      if (it < items)
-        load_x4<XT>(x + static_cast<uint64_t>(b[w]) * p.cols, c[w] * 128 + 4 * lane, p.cols, p.x_vec != 0, v4[w]);
-    }
+    for (int jj = 0; jj < 4; ++jj) u[jj] = scratch[col_lane + 4 * jj];
+    __syncwarp();
+    limb_item(u, xres + resident_slot(c, c_first, p.C) * p.xslot_bytes, b, p.batch, lane);
 #pragma unroll
-    for (uint32_t w = 0; w < W; ++w) {
-      if (base + w * WARPS >= items) break;
-      *reinterpret_cast<float4*>(scratch + 4 * lane) = make_float4(v4[w][0], v4[w][1], v4[w][2], v4[w][3]);
-      __syncwarp();
-      float v[4];
-#pragma unroll
-      for (int jj = 0; jj < 4; ++jj) v[jj] = scratch[col_lane + 4 * jj];
-      __syncwarp();
-      limb_item(v, xres + resident_slot(c[w], c_first, p.C) * p.xslot_bytes, b[w], p.batch, lane);
-    }
+    for (int jj = 0; jj < 4; ++jj) v[jj] = vn[jj];
+    c = cn;
+    b = bn;
   }
 }
 

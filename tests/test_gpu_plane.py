@@ -89,12 +89,26 @@ def test_fp32_activations_wide_dynamic_range():
     24 bits relative to its tile's largest |x|)."""
     rng = np.random.default_rng(7)
     m = random_matrix(rng, 256, 384)
-    pm = plane_matrix(m)
     mag = 10.0 ** rng.uniform(-6, 6, size=(2, m.cols))
     x = (np.sign(rng.standard_normal((2, m.cols))) * mag).astype(np.float32)
+    # rows whose codes are zero at the tile's largest columns depend on the small activations
+    for r in range(0, m.rows, 7):
+        for s in range(4):
+            c0 = int(np.argmax(np.abs(x[0, :128])))
+            byte, sh = divmod(r * m.geometry[3] + c0, 4)
+            m.codes[s][byte] &= np.uint8(~(3 << (2 * sh)) & 0xFF)
+    pm = plane_matrix(m)
     y = pm.gemv(torch.from_numpy(x).cuda(), prefix=4, y_dtype=torch.float32).cpu().numpy()
     e64 = _fp64_reference(m, x, 4)
     assert rel_l2(y, e64) <= 1e-5
+    # element by element: every x keeps >= 24 bits of its 128-column tile's largest |x|
+    # (2^-24 of it), and the FP32 sums of 3 tiles x 4 stages add at most 12 roundings of
+    # 2^-24 of the same magnitude: sum_c |w_rc| * tile max * 2^-20 bounds a row
+    w = np.abs(orc.dequantize_prefix_np(m, 4).astype(np.float64))
+    xa = np.abs(x.astype(np.float64))
+    tmax = np.repeat(np.pad(xa, ((0, 0), (0, -m.cols % 128))).reshape(2, -1, 128).max(axis=2), 128, axis=1)[:, :m.cols]
+    bound = tmax @ w.T * 2.0 ** -20
+    assert np.all(np.abs(y - e64) <= bound)
 
 
 def test_prefix_zero_writes_bias_or_zeros():
