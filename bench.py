@@ -300,6 +300,28 @@ def run_ours(args, rank, world, device):
     launches_per_step = sum(g["copies"][0].gemv_launches(1, hqb.F16, prefix) + (1 if fused else 0) for g in groups)
     if world == 1 and args.step_mode == "grouped":
         launches_per_step = 1
+    # N > 1, grouped: each group's shard output at a fixed offset of one padded buffer
+    # (slot_rows per group), the step's GEMVs as one grouped launch per rank, then ONE NCCL
+    # all-gather of the whole buffer
+    mg_grouped = world > 1 and not fused and args.step_mode == "grouped"
+    if mg_grouped:
+        launches_per_step = 1
+        slot_tot = sum(g["slot_rows"] for g in groups)
+        y_pad_all = torch.zeros(slot_tot, dtype=torch.float16, device=device)
+        y_pad, off = {}, 0
+        for g in groups:
+            y_pad[g["name"]] = y_pad_all[off:off + g["nrows"]].view(1, g["nrows"])
+            off += g["slot_rows"]
+        y_full_all = torch.empty(world, slot_tot, dtype=torch.float16, device=device)
+        mg_steps = [hqb.Step([(G["copies"][c], x_dev[G["src"]], prefix, y_pad[G["name"]], hqb.FLAG_PDL)
+                              for G in groups], ws, graph=False, independent=True) for c in range(ncopies)]
+
+        def gather_all():
+            torch.distributed.all_gather_into_tensor(y_full_all.view(-1), y_pad_all)
+
+        def gstep(copy):
+            mg_steps[copy].run()
+            gather_all()
 
     def gather(g):
         if world == 1:
@@ -347,6 +369,20 @@ def run_ours(args, rank, world, device):
             graphs[i % ncopies].replay()
         torch.cuda.synchronize()
 
+    ggraphs = []
+    if mg_grouped:
+        for i in range(max(3, args.warmup)):
+            gstep(i % ncopies)
+        torch.cuda.synchronize()
+        for c in range(ncopies):
+            g_ = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g_):
+                gstep(c)
+            ggraphs.append(g_)
+        for i in range(3):
+            ggraphs[i % ncopies].replay()
+        torch.cuda.synchronize()
+
     def barrier():
         if world > 1:
             torch.distributed.barrier()
@@ -376,8 +412,7 @@ def run_ours(args, rank, world, device):
         return out
 
     # the step's GEMVs as one grouped launch (hqb_gemv_grouped: the workload's layers take
-    # inputs of their own, so they are independent) -- N = 1 only, the all-gathers of N > 1
-    # sit between the launches
+    # inputs of their own, so they are independent); N > 1: mg_grouped above
     grouped = world == 1 and args.step_mode == "grouped"
     gsteps = []
     if grouped:
@@ -389,8 +424,10 @@ def run_ours(args, rank, world, device):
     t_timed0 = time.monotonic()
     chained_ms = time_steps(lambda i: graphs[i % ncopies].replay() if use_graph else step(i % ncopies))
     grouped_ms = time_steps(lambda i: gsteps[i % ncopies].run()) if grouped else None
+    if mg_grouped:
+        grouped_ms = time_steps(lambda i: ggraphs[i % ncopies].replay())
     t_timed1 = time.monotonic()
-    rep_ms = grouped_ms if grouped else chained_ms
+    rep_ms = grouped_ms if (grouped or mg_grouped) else chained_ms
     ms_per_step = statistics.median(rep_ms)
     # whole-job bytes: the full (unsharded) layers, each input once per group
     total_bytes = sum(group_bytes([{"nrows": m["rows"]} for m in g["members"]], g["cols"], prefix) for g in groups)
@@ -440,6 +477,32 @@ def run_ours(args, rank, world, device):
         # one kernel per step: its launches back to back (the grouped step graph) are the step
         by_kernel = {"gemv_grouped_kernel": [sum(G["bytes"] for G in groups), ms_per_step]}
         tot_ms = ms_per_step
+    mg_gemv_ms = None
+    if mg_grouped:
+        # this rank's grouped launch alone (graph of back-to-back launches, no gather)
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            for i in range(2):
+                mg_steps[i % ncopies].run()
+        torch.cuda.current_stream().wait_stream(side)
+        gq = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gq):
+            for i in range(per_graph):
+                mg_steps[i % ncopies].run()
+        for _ in range(3):
+            gq.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(5):
+            gq.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        mg_gemv_ms = e0.elapsed_time(e1) / (5 * per_graph)
+        del gq
+        by_kernel = {"gemv_grouped_kernel": [sum(G["bytes"] for G in groups), mg_gemv_ms]}
+        tot_ms = mg_gemv_ms
     # the roofline line is the kernel with the most device time; every kernel's share is listed
     dominant = max(by_kernel, key=lambda k: by_kernel[k][1])
     dom_b, dom_ms = by_kernel[dominant]
@@ -453,13 +516,19 @@ def run_ours(args, rank, world, device):
         side = torch.cuda.Stream()
         side.wait_stream(torch.cuda.current_stream())
         with torch.cuda.stream(side):
-            for G in groups:
-                gather(G)
+            if mg_grouped:
+                gather_all()
+            else:
+                for G in groups:
+                    gather(G)
         torch.cuda.current_stream().wait_stream(side)
         with torch.cuda.graph(gg):
             for _ in range(8):
-                for G in groups:
-                    gather(G)
+                if mg_grouped:
+                    gather_all()
+                else:
+                    for G in groups:
+                        gather(G)
         for _ in range(2):
             gg.replay()
         barrier()
@@ -473,7 +542,7 @@ def run_ours(args, rank, world, device):
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
         gather_us = round(float(t.item()) * 1e3, 3)
         del gg
-    gemv_us = sum(v["us"] for v in kern.values())
+    gemv_us = sum(v["us"] for v in kern.values()) if mg_gemv_ms is None else mg_gemv_ms * 1e3
     if world > 1:
         t = torch.tensor([gemv_us], device=device)
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
@@ -490,7 +559,9 @@ def run_ours(args, rank, world, device):
             return gathers[g["name"]][copy % 2].out
         return y_full[g["name"]] if world > 1 else y_loc[g["name"]]
 
-    if world == 1:
+    if mg_grouped:
+        host_y = {"all": torch.empty_like(y_full_all, device="cpu").pin_memory()}
+    elif world == 1:
         # each step is one hqb.Step whose graph holds the input copy, the GEMVs and the
         # output copy (hqb_step_create_io); one host call per step
         host_y_all = torch.empty_like(y_all, device="cpu").pin_memory()
@@ -502,7 +573,11 @@ def run_ours(args, rank, world, device):
         host_y = {g["name"]: torch.empty_like(gathered(g, 0), device="cpu").pin_memory() for g in groups}
 
     def e2e_step(copy):
-        if world == 1:
+        if mg_grouped:
+            x_all.copy_(host_x_all, non_blocking=True)
+            ggraphs[copy].replay()
+            host_y["all"].copy_(y_full_all, non_blocking=True)
+        elif world == 1:
             steps_api[copy].run()
         else:
             x_all.copy_(host_x_all, non_blocking=True)
@@ -529,7 +604,7 @@ def run_ours(args, rank, world, device):
     d2h = sum(y.numel() * 2 for y in host_y.values())
 
     clk.__exit__(None, None, None)
-    del graphs  # graphs holding NCCL work are released before the process group is destroyed
+    del graphs, ggraphs  # graphs holding NCCL work are released before the process group is destroyed
     torch.cuda.synchronize()
     gather_flags = 0
     for pair in gathers.values():
@@ -560,8 +635,11 @@ def run_ours(args, rank, world, device):
                    "layers": [[m["name"], m["rows"], g["cols"]] for g in groups for m in g["members"]],
                    "launches": [[g["name"], g["nrows"], g["cols"]] for g in groups],
                    "grouping": "layers sharing an input run as one row-stacked launch; step_mode grouped: "
-                               "the launch groups (independent inputs) run as one grouped kernel launch",
-                   "parallelism": (f"row-shard{world}+" + ("fused-p2p-allgather" if fused else "nccl-allgather"))
+                               "the launch groups (independent inputs) run as one grouped kernel launch, "
+                               "at N > 1 followed by one all-gather of every group's output",
+                   "parallelism": (f"row-shard{world}+" + ("fused-p2p-allgather" if fused else
+                                                            "one-nccl-allgather-per-step" if mg_grouped else
+                                                            "nccl-allgather-per-group"))
                                   if world > 1 else "single",
                    "l2": f"{ncopies} rotating weight copies, {ncopies * step_bytes / 2**20:.0f} MiB > 3x L2",
                    "graph": use_graph},
@@ -573,7 +651,7 @@ def run_ours(args, rank, world, device):
         "timing": {"repeats": repeats, "steps_per_repeat": args.steps,
                    "ms_per_step": [round(v, 5) for v in rep_ms], "median_ms": round(ms_per_step, 5),
                    "min_ms": round(min(rep_ms), 5), "max_ms": round(max(rep_ms), 5)},
-        "step_mode": "grouped" if grouped else "chained",
+        "step_mode": "grouped" if (grouped or mg_grouped) else "chained",
         # the same step as dependent launches (one launch per layer group, PDL between them,
         # as a decoder block whose layers wait for each other runs)
         "chained": {"value": round(total_bytes / (statistics.median(chained_ms) * 1e-3) / 1e9, 1),
@@ -587,7 +665,9 @@ def run_ours(args, rank, world, device):
         # gather alone (NCCL; the fused gather stores inside the GEMV), and the whole step
         result["per_rank"] = {"gemv_us": round(gemv_us, 3), "gather_us": gather_us,
                               "step_us": round(ms_per_step * 1e3, 3),
-                              "gather": "fused-p2p" if fused else "nccl-all_gather_into_tensor"}
+                              "gather": "fused-p2p" if fused else
+                                        ("one nccl all_gather_into_tensor of every group's output" if mg_grouped
+                                         else "nccl all_gather_into_tensor per group")}
     peaks = {}
     try:
         peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
