@@ -2819,12 +2819,15 @@ int gemv_impl(const hqb_plane_matrix* m, uint32_t prefix, const uint8_t* depth, 
                               ((static_cast<uint64_t>(m->grid_cols) * prefix + kRowsWarps - 1) / kRowsWarps);
   // With the int8 forms (raw x, batch <= 2) the stream-K kernel also wins once a
   // row-block CTA would take more than two row-block items (B200 timings at 2048..12288
-  // rows, prefix 1..4).
+  // rows, prefix 1..4), and at two items once the layer is wider than 32 tile columns
+  // (4096x8192: 7.1 / 8.5 against 8.2 / 10.6 us at prefix 1 / 2; 4096x4096 stays with the
+  // row-block kernel, 5.9 against 6.1 us at prefix 2).
   const bool i8_form = !mixed && !simt && !x_prepared && batch <= 2 &&
                        !(flags & (HQB_FLAG_RING | HQB_FLAG_F16MMA));
   const uint64_t rows_items_cta = (static_cast<uint64_t>(m->grid_rows) * 8 + sms - 1) / sms;
   const bool rows_small = all_units <= static_cast<uint64_t>(kRowsUnitsMax) * 2 * sms &&
-                          warp_units * 2 * sms <= all_units + 5ull * sms && (!i8_form || rows_items_cta <= 2);
+                          warp_units * 2 * sms <= all_units + 5ull * sms &&
+                          (!i8_form || rows_items_cta == 1 || (rows_items_cta == 2 && m->grid_cols <= 32));
   // FP32 x at batch <= 2 (int8 limbs) keeps to the lean stream-K kernel unless the row-block
   // kernel is asked for: only limb_item slots keep activations of 2^100 and more exact
   const bool rows_path = !mixed && !simt && batch <= 8 && !(flags & (HQB_FLAG_RING | HQB_FLAG_STREAMK)) &&
