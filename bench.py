@@ -786,7 +786,21 @@ def supplementary(device):
             sb[f"{rows}x4096_b{batch}"] = e
         del mats
     out["small_batch_p4"] = sb
-    del copies
+    # prefill (hqb_prefill_gemm): FP16 decode of the selected stages + cuBLAS FP16 GEMM,
+    # 11008x4096 at prefix 2, weights rotating; the GEMV at batch 16 beside it
+    pw = torch.empty(copies[0].prefill_workspace_bytes(), dtype=torch.uint8, device=device)
+    pf = {}
+    for batch in (16, 64, 256, 1024):
+        xb = torch.randn(batch, 4096, device=device, generator=gen).half()
+        yb = torch.empty(batch, 11008, device=device, dtype=torch.float16)
+        t = _graph_us(lambda i: copies[i % 4].prefill(xb, 2, out=yb, workspace=pw), 8)
+        e = {"us": round(t, 3), "tflops": round(2.0 * batch * 11008 * 4096 / (t * 1e-6) / 1e12, 1)}
+        if batch == 16:
+            tg = _graph_us(lambda i: copies[i % 4].gemv(xb, prefix=2, out=yb, workspace=ws, flags=hqb.FLAG_PDL), 32)
+            e["gemv_us"] = round(tg, 3)
+        pf[f"11008x4096_p2_b{batch}"] = e
+    out["prefill"] = pf
+    del pw, copies
     torch.cuda.empty_cache()
     out["prefix_sweep"] = prefix_sweep(device, gen)
     out["reference_gpu_kernel"] = reference_gpu_kernel(device, gen)

@@ -25,7 +25,7 @@ LIB = LIB_DIR / "libharpq_b200.so"
 API_TEST = LIB_DIR / "hqb_api_test"
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
-SOURCES = ["hqb_plane.cu", "hqb_bulk.cu", "hqb_raw.cu", "hqb_raw_i8.cu", "hqb_step.cu", "harpq_native.cu", "hqb_static_scratch.cu"]
+SOURCES = ["hqb_plane.cu", "hqb_bulk.cu", "hqb_raw.cu", "hqb_raw_i8.cu", "hqb_step.cu", "hqb_prefill.cu", "harpq_native.cu", "hqb_static_scratch.cu"]
 CFLAGS = [*ARCH, "-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-Xcompiler", "-Wall",
           "-Xcompiler", "-ffp-contract=off",
           "-I", str(REPO / "include"), "-I", str(CSRC)]

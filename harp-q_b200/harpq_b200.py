@@ -118,6 +118,8 @@ EXPORTS = {
     "hqb_gemv_noalloc_reset": (i32, [vp]),
     "hqb_gemv_noalloc_scratch": (i32, [ctypes.POINTER(vp)]),
     "hqb_decode_planes": (i32, [ctypes.POINTER(PlaneMatrixC), u32, vp, vp, u64, vp]),
+    "hqb_prefill_workspace_bytes": (u64, [ctypes.POINTER(PlaneMatrixC)]),
+    "hqb_prefill_gemm": (i32, [ctypes.POINTER(PlaneMatrixC), u32, vp, i32, u32, vp, i32, vp, i32, vp, u64, vp]),
     "hqb_raw_gemv": (i32, [ctypes.POINTER(Geometry), ctypes.POINTER(RawStage), u32, u32, vp, u64, vp, u64, vp, u64,
                            vp]),
     "hqb_raw_gemv_ex": (i32, [ctypes.POINTER(Geometry), ctypes.POINTER(RawStage), u32, u32, vp, u64, vp, u64, vp,
@@ -387,6 +389,26 @@ class PlaneMatrix:
                                     F32 if bias is None else _dtype_code(bias),
                                     F16 if gather.y_dtype == torch.float16 else F32, ctypes.byref(gather.c),
                                     ws.ptr(), ws.nbytes, flags, _stream(stream)), "hqb_gemv_gather")
+
+    def prefill(self, x: torch.Tensor, prefix: int, bias: torch.Tensor | None = None,
+                y_dtype: torch.dtype = torch.float16, workspace: torch.Tensor | None = None,
+                out: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+        """Large-batch product (hqb_prefill_gemm): FP16 x [batch][cols] -> y [batch][rows];
+        the selected stages decoded into FP16 weights in `workspace` (a uint8 device tensor of
+        prefill_workspace_bytes(), allocated here when not given), then a cuBLAS GEMM."""
+        x = x if x.dim() == 2 else x.unsqueeze(0)
+        if not x.is_contiguous():
+            raise ValueError("x must be contiguous")
+        y = out if out is not None else torch.empty(x.shape[0], self.rows, dtype=y_dtype, device=x.device)
+        if workspace is None:
+            workspace = torch.empty(self.prefill_workspace_bytes(), dtype=torch.uint8, device=x.device)
+        check(lib().hqb_prefill_gemm(ctypes.byref(self.c_struct()), prefix, _ptr(x), _dtype_code(x), x.shape[0],
+                                     _ptr(bias), F32 if bias is None else _dtype_code(bias), _ptr(y), _dtype_code(y),
+                                     _ptr(workspace), workspace.numel(), _stream(stream)), "hqb_prefill_gemm")
+        return y
+
+    def prefill_workspace_bytes(self) -> int:
+        return int(lib().hqb_prefill_workspace_bytes(ctypes.byref(self.c_struct())))
 
     def decode(self, prefix: int | None = None, depth: torch.Tensor | None = None, stream=None) -> torch.Tensor:
         out = torch.empty(self.rows, self.cols, dtype=torch.float32, device=self.device)

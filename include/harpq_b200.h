@@ -392,6 +392,22 @@ HQB_API int hqb_gather_wait(const uint32_t* flags, uint32_t world, uint32_t* epo
 HQB_API int hqb_gather_wait_ex(const uint32_t* flags, uint32_t world, uint32_t* epoch, int* device_flags,
                                uint64_t limit_ns, void* stream);
 
+/* ---- prefill (batch >> 16) ------------------------------------------------------------ */
+
+/* y[batch][rows] = x[batch][cols] · W_prefix^T (+ bias) for a large batch, the product the
+ * reference lists as future work (docs/RESEARCH_PLAN.md:104).  The selected stages are
+ * decoded once per call into FP16 weights in the workspace (each element the FP32 stage sum of
+ * DequantizePrefix, native/src/stage_codec.cpp:254-272, rounded once to FP16) and multiplied
+ * by cuBLAS with FP16 inputs and FP32 accumulation.  x: FP16 only (HQB_ERR_UNSUPPORTED
+ * otherwise); y, bias: FP16 or FP32.  Prefix 0 writes bias or zeros.  The workspace holds
+ * hqb_prefill_workspace_bytes(m) bytes, 256-byte aligned.  The first call on a host thread and
+ * device creates that thread's cuBLAS handle (kept until exit); a cuBLAS failure returns
+ * cudaErrorUnknown. */
+HQB_API uint64_t hqb_prefill_workspace_bytes(const hqb_plane_matrix* m);
+HQB_API int hqb_prefill_gemm(const hqb_plane_matrix* m, uint32_t prefix, const void* x, int x_dtype,
+                             uint32_t batch, const void* bias, int bias_dtype, void* y, int y_dtype,
+                             void* workspace, uint64_t workspace_bytes, void* stream);
+
 /* Dense FP32 weights [rows][cols] decoded from planes, Σ_{s<d} code·scale summed in
  * stage order from 0.0f — bit-identical to DequantizePrefix
  * (native/src/stage_codec.cpp:254-272).  depth NULL: uniform prefix. */
