@@ -57,8 +57,10 @@ __global__ void __launch_bounds__(256) decode_f16_kernel(hqb_plane_matrix m, uin
 #pragma unroll
       for (uint32_t s = 0; s < HQB_MAX_STAGES; ++s) {
         if (s >= prefix) break;
+        // code * scale is exact in FP32 (an FP16 scale times an integer in [-2, 1]), so one
+        // fused multiply-add rounds exactly as the separate product and sum do
         const float code = static_cast<float>(static_cast<int>((words[s][i] >> (2 * k)) & 3u) - 2);
-        wsum = __fadd_rn(wsum, __fmul_rn(code, sc[s][i & 1]));
+        wsum = __fmaf_rn(code, sc[s][i & 1], wsum);
       }
       h[k] = __float2half_rn(wsum);
     }
