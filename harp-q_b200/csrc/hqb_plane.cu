@@ -1552,6 +1552,9 @@ __global__ void __launch_bounds__(kStreamThreads, (NB == 1 && (XL == 1 || I8)) ?
 // problem k's stream-K share, so every problem streams at once and the launch's fixed costs
 // (start, activation limbs, tail) are paid once for the group.
 constexpr uint32_t kMaxGroup = 8;
+// Streaming time of building one limb column in a CTA, in (tile, stage) units: ~0.2 us
+// against ~0.156 us per unit at two CTAs per SM (per-CTA timelines of the 7B block step).
+constexpr double kLimbColUnits = 1.3;
 struct GroupParams {
   GemvParams p[kMaxGroup];
   uint32_t cta_base[kMaxGroup + 1];
@@ -3158,17 +3161,36 @@ int grouped_launch(const hqb_gemv_call* calls, uint32_t count, void* workspace, 
   uint32_t G = static_cast<uint32_t>(sms) * 2;
   uint32_t res_max = 0;
   for (int attempt = 0; attempt < 2; ++attempt) {
-    uint32_t acc = 0;
-    uint64_t seen = 0;
-    gp.cta_base[0] = 0;
-    for (uint32_t i = 0; i < count; ++i) {
-      seen += units[i];
-      uint32_t end = static_cast<uint32_t>((seen * G + total / 2) / total);
-      end = std::max(end, acc + 1);
-      if (i + 1 == count) end = std::max(G, acc + 1);
-      gp.cta_base[i + 1] = end;
-      acc = end;
+    // CTAs dealt so that every call's CTAs cost about the same: a CTA's time is its units
+    // plus the limb columns it builds (each about kLimbColUnits units of streaming time,
+    // B200 timelines); bisection on that cost, then the CTAs left over by rounding go to
+    // the calls in turn.
+    uint32_t gcount[kMaxGroup];
+    auto ctas_for = [&](uint32_t i, double cost) -> uint32_t {
+      const uint32_t C = calls[i].m->grid_cols;
+      uint32_t lo = 1, hi = G;  // smallest g with cost_i(g) <= cost
+      while (lo < hi) {
+        const uint32_t mid = (lo + hi) / 2;
+        const double u = static_cast<double>(units[i]) / mid;
+        const double cols = std::min<double>(C, u / d + 1.0);
+        if (u + kLimbColUnits * cols <= cost) hi = mid;
+        else lo = mid + 1;
+      }
+      return lo;
+    };
+    double clo = 0.0, chi = static_cast<double>(total) + kLimbColUnits * maxC + 1.0;
+    for (int it = 0; it < 48; ++it) {
+      const double mid = 0.5 * (clo + chi);
+      uint64_t need = 0;
+      for (uint32_t i = 0; i < count; ++i) need += ctas_for(i, mid);
+      if (need <= G) chi = mid;
+      else clo = mid;
     }
+    uint32_t used = 0;
+    for (uint32_t i = 0; i < count; ++i) used += (gcount[i] = ctas_for(i, chi));
+    for (uint32_t i = 0; used < G; i = (i + 1) % count, ++used) ++gcount[i];
+    gp.cta_base[0] = 0;
+    for (uint32_t i = 0; i < count; ++i) gp.cta_base[i + 1] = gp.cta_base[i] + gcount[i];
     res_max = 0;
     for (uint32_t i = 0; i < count; ++i) {
       const uint64_t g_i = gp.cta_base[i + 1] - gp.cta_base[i];
