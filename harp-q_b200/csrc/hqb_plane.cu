@@ -1552,9 +1552,11 @@ __global__ void __launch_bounds__(kStreamThreads, (NB == 1 && (XL == 1 || I8)) ?
 // problem k's stream-K share, so every problem streams at once and the launch's fixed costs
 // (start, activation limbs, tail) are paid once for the group.
 constexpr uint32_t kMaxGroup = 8;
-// Streaming time of building one limb column in a CTA, in (tile, stage) units: ~0.2 us
-// against ~0.156 us per unit at two CTAs per SM (per-CTA timelines of the 7B block step).
-constexpr double kLimbColUnits = 1.3;
+// Streaming time of building one limb column in a CTA, in (tile, stage) units.  Per-CTA
+// timelines of the 7B block step suggest ~1.3 (~0.2 us per column against ~0.156 us per
+// unit at two CTAs per SM); timed on B200, 0.8 gives the fastest 7B block step (27.8 against
+// 28.6 us at 1.3 and 2.0) and the 70B MLP step of the unweighted dealing (1.3: 2 % faster).
+constexpr double kLimbColUnits = 0.8;
 struct GroupParams {
   GemvParams p[kMaxGroup];
   uint32_t cta_base[kMaxGroup + 1];
