@@ -909,43 +909,10 @@ __device__ __forceinline__ void build_xfrag_tiles(const GemvParams& p, uint8_t* 
   }
 }
 
-// The same for the int8 limb slots (XL 1: FP16 x, 2: FP32 x), through prep_i8_items.
-template <int XL>
-__device__ __forceinline__ void build_xfrag_tiles_i8(const GemvParams& p, uint8_t* xres, const ColRanges& cr,
-                                                     uint32_t c_first) {
-  using XT = typename std::conditional<XL == 1, __half, float>::type;
-  const XT* x = static_cast<const XT*>(p.x_raw);
-  const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  constexpr int W = 2;
-  constexpr uint32_t kWarps = kStreamThreads / 32;
-  const uint32_t items = cr.count() * p.batch;
-  for (uint32_t base = warp; base < items; base += W * kWarps) {
-    float v[W][4];
-    bool ok[W];
-    uint8_t* slot[W];
-    uint32_t b[W];
-#pragma unroll
-    for (int w = 0; w < W; ++w) {
-      const uint32_t item = base + w * kWarps;
-      ok[w] = item < items;
-      const uint32_t it = ok[w] ? item : base;
-      const uint32_t ci = it / p.batch;
-      b[w] = it - ci * p.batch;
-      const uint32_t c = cr.col(ci);
-      slot[w] = xres + resident_slot(c, c_first, p.C) * p.xslot_bytes;
-      load_x4<XT>(x + static_cast<uint64_t>(b[w]) * p.cols, c * 128 + 4 * lane, p.cols, p.x_vec != 0, v[w]);
-    }
-    prep_i8_items<W>(v, ok, slot, b, p.batch, lane);
-  }
-}
-
-
-// The stream-K kernel's work as CTA `cta` of a grid of `grid` CTAs on problem p (the kernel
-// below, and one problem of a grouped launch).
-template <int NB, int XL, int D, bool B1 = false, bool I8 = false, bool MX = false>
+// The stream-K kernel's work on FP16 fragments as CTA `cta` of a grid of `grid` CTAs on
+// problem p (int8 limb launches run lean_body or unit_body instead).
+template <int NB, int XL, int D, bool B1 = false>
 __device__ __forceinline__ void uniform_body(const GemvParams& p, const uint32_t cta, const uint32_t grid) {
-  static_assert(!I8 || NB == 1, "the int8 limb path takes batch <= 2");
-  static_assert(!MX || (I8 && D == HQB_MAX_STAGES), "depth maps run on the int8 path at depth 4");
   constexpr int R = TilesAhead<D>::value;
   constexpr uint32_t kFull = (1u << D) - 1u;
   extern __shared__ __align__(16) uint8_t xres[];  // [resident activation slots]
@@ -953,21 +920,17 @@ __device__ __forceinline__ void uniform_body(const GemvParams& p, const uint32_t
   // The CTA's units [u0, u1): tiles t0..t_end, the first from stage s0, the last up to
   // stage s_end; rb_first / re_last: first unit of t0's tile row, end of t_end's.
   MixedRange rg{};
-  if constexpr (MX) {
-    rg = mixed_range(p, cta, lane);
-  } else {
-    rg.total = p.total;
-    rg.ctas = static_cast<uint32_t>(rg.total < grid ? rg.total : grid);
-    if (cta < rg.ctas) {
-      rg.u0 = unit_start(cta, rg.total, rg.ctas);
-      rg.u1 = unit_start(cta + 1, rg.total, rg.ctas);
-      rg.t0 = static_cast<uint32_t>(rg.u0 / D);
-      rg.s0 = static_cast<uint32_t>(rg.u0 % D);
-      rg.t_end = static_cast<uint32_t>((rg.u1 - 1) / D);
-      rg.s_end = static_cast<uint32_t>((rg.u1 - 1) % D) + 1;
-      rg.rb_first = static_cast<uint64_t>(rg.t0 / p.C) * p.C * D;
-      rg.re_last = static_cast<uint64_t>(rg.t_end / p.C + 1) * p.C * D;
-    }
+  rg.total = p.total;
+  rg.ctas = static_cast<uint32_t>(rg.total < grid ? rg.total : grid);
+  if (cta < rg.ctas) {
+    rg.u0 = unit_start(cta, rg.total, rg.ctas);
+    rg.u1 = unit_start(cta + 1, rg.total, rg.ctas);
+    rg.t0 = static_cast<uint32_t>(rg.u0 / D);
+    rg.s0 = static_cast<uint32_t>(rg.u0 % D);
+    rg.t_end = static_cast<uint32_t>((rg.u1 - 1) / D);
+    rg.s_end = static_cast<uint32_t>((rg.u1 - 1) % D) + 1;
+    rg.rb_first = static_cast<uint64_t>(rg.t0 / p.C) * p.C * D;
+    rg.re_last = static_cast<uint64_t>(rg.t_end / p.C + 1) * p.C * D;
   }
   const uint64_t total = rg.total, u0 = rg.u0, u1 = rg.u1;
   const uint32_t ctas = rg.ctas;
@@ -977,11 +940,10 @@ __device__ __forceinline__ void uniform_body(const GemvParams& p, const uint32_t
   const uint32_t t0 = rg.t0, s0 = rg.s0, t_end = rg.t_end, s_end = rg.s_end;
   const uint32_t ntiles = t_end - t0 + 1;
   const uint32_t mask_first = kFull & ~((1u << s0) - 1u), mask_last = (1u << s_end) - 1u;
-  // Stages of walk tile k (tile t_end - k) this CTA computes: all D (a depth map: the
-  // tile's depth), cut to the range at its two ends.
+  // Stages of walk tile k (tile t_end - k) this CTA computes: all D, cut to the range at
+  // its two ends.
   auto tile_mask = [&](uint32_t k) -> uint32_t {
     uint32_t m = kFull;
-    if constexpr (MX) m = (1u << clamp_depth(__ldg(p.depth + (t_end - k)), p.stage_count)) - 1u;
     if (k == 0) m &= mask_last;
     if (k == ntiles - 1) m &= mask_first;
     return m;
@@ -1005,14 +967,11 @@ __device__ __forceinline__ void uniform_body(const GemvParams& p, const uint32_t
   }
 
   // Register ring of R tiles x D stages.  A stage outside the CTA's units gets scale 0
-  // (codes 0): its products are finite and its contribution is exactly zero.  With a
-  // depth map such stages are not computed at all (live: the slot's stage mask).
+  // (codes 0): its products are finite and its contribution is exactly zero.
   uint4 w[R][D];
   uint32_t sc[R][D];
-  uint32_t live[R];
   const uint64_t l2_first = policy_evict_first();
   auto load_tile = [&](int slot, uint32_t mask) {
-    live[slot] = mask;
 #pragma unroll
     for (int s = 0; s < D; ++s) {
       if (D == 1 || (mask & (1u << s))) {
@@ -1046,8 +1005,7 @@ __device__ __forceinline__ void uniform_body(const GemvParams& p, const uint32_t
   {  // activation fragments of the tile columns this CTA touches, at their resident slots
     const ColRanges cr = needed_columns(t0, t_end, p.C);
     if (p.x_raw != nullptr) {
-      if constexpr (I8) build_xfrag_tiles_i8<XL>(p, xres, cr, c_first);
-      else build_xfrag_tiles<XL>(p, xres, cr, c_first);
+      build_xfrag_tiles<XL>(p, xres, cr, c_first);
     } else {
       const uint32_t per_slot = p.xslot_bytes / 16;
       const uint32_t chunks = cr.count() * per_slot;
@@ -1060,7 +1018,6 @@ __device__ __forceinline__ void uniform_body(const GemvParams& p, const uint32_t
   }
   __syncthreads();
   const XLane<NB, XL> xlane(p.batch, lane);
-  const XLaneI8 xlane8(p.batch, lane);
   uint32_t row = t_end / p.C;
   // activation slot of the current tile; the next tile's is the previous slot (mod C)
   const uint8_t* xs = xres + resident_slot(t_end % p.C, c_first, p.C) * p.xslot_bytes;
@@ -1082,7 +1039,6 @@ __device__ __forceinline__ void uniform_body(const GemvParams& p, const uint32_t
   const uint32_t row_first = t0 / p.C, row_last = t_end / p.C;
   auto advance = [&](uint32_t k) {
     if (--left == 0 || k + 1 == ntiles) {
-      if constexpr (I8) quad_sum<B1>(y);
       // the row's unit range, as far as it matters: inside [u0, u1) unless an end row
       const uint64_t rb = row == row_first ? rg.rb_first : u0, re = row == row_last ? rg.re_last : u1;
       if (rb >= u0 && re <= u1) {
@@ -1106,19 +1062,11 @@ __device__ __forceinline__ void uniform_body(const GemvParams& p, const uint32_t
     xs = xs == xres ? xs_top : xs - p.xslot_bytes;
   };
   auto one_tile = [&](int j) {
-    if constexpr (I8) {
-      XFragI8 xf;
-      load_xfrag_i8<B1>(xf, xlane8, xs);
-      uint32_t acc[CH][4];
-      tile_mma_i8<D, MX>(w[j], xf, acc, live[j]);
-      tile_epilogue_i8<D, B1, MX>(sc[j], xf, acc, y, live[j]);
-    } else {
-      XFrag<NB, XL> xf;
-      load_xfrag<NB, XL>(xf, xlane, xs);
-      float acc[CH][NB][4];
-      tile_mma<NB, XL, D>(w[j], xf, p.shift_mul, acc);
-      tile_epilogue<NB, XL, D, B1>(sc[j], xf, acc, y);
-    }
+    XFrag<NB, XL> xf;
+    load_xfrag<NB, XL>(xf, xlane, xs);
+    float acc[CH][NB][4];
+    tile_mma<NB, XL, D>(w[j], xf, p.shift_mul, acc);
+    tile_epilogue<NB, XL, D, B1>(sc[j], xf, acc, y);
   };
 
   uint32_t k0 = 0;
@@ -1541,11 +1489,12 @@ __global__ void __launch_bounds__(kStreamThreads, 2) gemv_unit_kernel(const __gr
   unit_body<XL, B1>(p, blockIdx.x);
 }
 
-template <int NB, int XL, int D, bool B1 = false, bool I8 = false, bool MX = false>
+template <int NB, int XL, int D, bool B1 = false, bool I8 = false>
 __global__ void __launch_bounds__(kStreamThreads, (NB == 1 && (XL == 1 || I8)) ? 2 : 1)
     gemv_uniform_kernel(const __grid_constant__ GemvParams p) {
-  if constexpr (I8 && !MX && NB == 1) lean_body<XL, D, B1>(p, blockIdx.x, gridDim.x);
-  else uniform_body<NB, XL, D, B1, I8, MX>(p, blockIdx.x, gridDim.x);
+  static_assert(!I8 || NB == 1, "the int8 limb path takes batch <= 2");
+  if constexpr (I8) lean_body<XL, D, B1>(p, blockIdx.x, gridDim.x);
+  else uniform_body<NB, XL, D, B1>(p, blockIdx.x, gridDim.x);
 }
 
 // Independent GEMVs in one launch (hqb_gemv_grouped): CTAs [cta_base[k], cta_base[k+1]) run
