@@ -202,9 +202,10 @@ __host__ __device__ inline uint32_t xslot_i8_bytes(uint32_t batch) { return kLim
 constexpr uint32_t kLimbMaxE = 100;  // tiles with max|x| >= 2^100 carry a wide factor
 
 // Limb preparation of W (tile column, batch row) items, one warp per item; lane L holds
-// columns 4L..4L+3 of the item's tile (v, zero past the last column).  Every path that
-// prepares limbs (prep_x_i8_kernel and the in-kernel builder) goes through this
-// function, so their slots are bit-identical.
+// columns 4L..4L+3 of the item's tile (v, zero past the last column).  The row-block
+// kernel (gemv_rows_kernel) builds its slots here; limb_item, with another lane layout,
+// builds the same bytes (for every finite tile below 2^kLimbMaxE) for the stream-K,
+// grouped, bulk and raw kernels.
 template <int W>
 __device__ __forceinline__ void prep_i8_items(const float (&v)[W][4], const bool (&ok)[W], uint8_t* const (&slot)[W],
                                               const uint32_t (&b)[W], uint32_t batch, uint32_t lane) {

@@ -2800,8 +2800,8 @@ int gemv_impl(const hqb_plane_matrix* m, uint32_t prefix, const uint8_t* depth, 
   const bool i8_raw = !simt && !x_prepared && batch <= 2 &&
                       !(flags & (HQB_FLAG_RING | HQB_FLAG_F16MMA));
   const bool i8_ok = !mixed && i8_raw;
-  // A depth map on the int8 stream-K kernel (depth-4 form, per-tile stage masks): its
-  // CTAs hold at most ceil(R·C·stage_count / SMs) units, so as many tiles plus one.
+  // A depth map on the int8 unit kernel (gemv_unit_kernel): its CTAs hold at most
+  // ceil(R·C·stage_count / SMs) units, so as many tiles plus one.
   const uint32_t mixed_res_slots = static_cast<uint32_t>(std::min<uint64_t>(
       m->grid_cols, (static_cast<uint64_t>(m->grid_rows) * m->grid_cols * m->stage_count + sms - 1) / sms + 1));
   const bool mx = mixed && i8_raw && static_cast<uint64_t>(mixed_res_slots) * xslot_i8_bytes(batch) <= kXResidentMaxI8;
