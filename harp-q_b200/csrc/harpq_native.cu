@@ -34,7 +34,7 @@ static_assert(sizeof(ProgressiveGemvStageDeviceView) == sizeof(hqb_raw_stage), "
 
 template <typename Error>
 std::size_t Mul(std::size_t a, std::size_t b, const char* what) {
-  if (a != 0 && b > std::numeric_limits<std::size_t>::max() / a) throw Error(std::string(what) + " overflows size_t");
+  if (a != 0 && b > std::numeric_limits<std::size_t>::max() / a) throw Error(std::string(what) + " does not fit in size_t");
   return a * b;
 }
 
@@ -152,7 +152,7 @@ float HalfBitsToFloat(std::uint16_t h) {
 std::size_t ScaleCountOf(const ScaleShape& shape) {
   std::size_t n = 1;
   for (std::size_t d : shape) {
-    if (d == 0) throw StageCodecError("scale_shape dimensions must be positive");
+    if (d == 0) throw StageCodecError("scale shape has a zero dimension");
     n = Mul<StageCodecError>(n, d, "scale count");
   }
   return n;
@@ -161,15 +161,15 @@ std::size_t ScaleCountOf(const ScaleShape& shape) {
 // ValidateMatrix of the stage codec (reference stage_codec.cpp:80-137).
 void ValidateCodecMatrix(const ProgressiveMatrix& m) {
   const MatrixGeometry& g = m.geometry;
-  if (g.original_rows == 0 || g.original_columns == 0) throw StageCodecError("original matrix dimensions must be positive");
+  if (g.original_rows == 0 || g.original_columns == 0) throw StageCodecError("matrix has zero rows or columns");
   if (g.tile_rows == 0 || g.tile_columns == 0 || g.group_size == 0)
-    throw StageCodecError("tile dimensions and group_size must be positive");
-  if (g.tile_columns % g.group_size != 0) throw StageCodecError("tile width must be divisible by group_size");
+    throw StageCodecError("tile shape or group size is zero");
+  if (g.tile_columns % g.group_size != 0) throw StageCodecError("group size does not divide the tile width");
   const std::size_t pr = Mul<StageCodecError>(CeilDiv(g.original_rows, g.tile_rows), g.tile_rows, "padded rows");
   const std::size_t pc = Mul<StageCodecError>(CeilDiv(g.original_columns, g.tile_columns), g.tile_columns, "padded columns");
-  if (g.padded_rows != pr || g.padded_columns != pc) throw StageCodecError("padded matrix dimensions do not match tile geometry");
+  if (g.padded_rows != pr || g.padded_columns != pc) throw StageCodecError("padded shape is not the shape rounded up to whole tiles");
   if (m.stages.empty() || m.stages.size() > kMaximumStageCount)
-    throw StageCodecError("a progressive matrix must contain between one and four stages");
+    throw StageCodecError("stage count is not in 1..4");
   const ScaleShape shape{g.padded_rows / g.tile_rows, g.padded_columns / g.tile_columns, g.tile_rows,
                          g.tile_columns / g.group_size};
   const std::size_t elements = Mul<StageCodecError>(g.padded_rows, g.padded_columns, "padded element count");
@@ -177,12 +177,12 @@ void ValidateCodecMatrix(const ProgressiveMatrix& m) {
   const std::size_t scale_count = ScaleCountOf(shape);
   for (std::size_t i = 0; i < m.stages.size(); ++i) {
     const DecodedStage& st = m.stages[i];
-    if (st.stage_index != i) throw StageCodecError("stages must form a zero-based contiguous prefix");
+    if (st.stage_index != i) throw StageCodecError("stage indices are not 0, 1, 2, ... in order");
     if (st.scale_shape != shape || st.scales.size() != scale_count)
-      throw StageCodecError("stage scale geometry does not match the matrix");
-    if (st.packed_codes.size() != code_bytes) throw StageCodecError("stage code payload length does not match the matrix");
+      throw StageCodecError("a stage's scale shape differs from the matrix's");
+    if (st.packed_codes.size() != code_bytes) throw StageCodecError("a stage's code bytes differ from the matrix's");
     for (float s : st.scales)
-      if (!std::isfinite(s) || s < 0.0F) throw StageCodecError("stage scales must be finite and non-negative");
+      if (!std::isfinite(s) || s < 0.0F) throw StageCodecError("a stage scale is negative, infinite or NaN");
   }
 }
 
@@ -278,37 +278,37 @@ HostGeometry ValidateGemvMatrix(const ProgressiveMatrix& m, std::size_t prefix, 
   const MatrixGeometry& g = m.geometry;
   if (g.original_rows == 0 || g.original_columns == 0 || g.padded_rows == 0 || g.padded_columns == 0 ||
       g.tile_rows == 0 || g.tile_columns == 0 || g.group_size == 0)
-    throw std::invalid_argument("matrix geometry dimensions must be positive");
-  if (g.tile_columns % g.group_size != 0) throw std::invalid_argument("tile width must be divisible by group size");
+    throw std::invalid_argument("geometry has a zero dimension");
+  if (g.tile_columns % g.group_size != 0) throw std::invalid_argument("group size does not divide the tile width");
   const std::size_t pr = Mul<std::overflow_error>(CeilDiv(g.original_rows, g.tile_rows), g.tile_rows, "padded rows");
   const std::size_t pc = Mul<std::overflow_error>(CeilDiv(g.original_columns, g.tile_columns), g.tile_columns, "padded columns");
-  if (g.padded_rows != pr || g.padded_columns != pc) throw std::invalid_argument("padded matrix shape disagrees with tile geometry");
+  if (g.padded_rows != pr || g.padded_columns != pc) throw std::invalid_argument("padded shape is not the shape rounded up to whole tiles");
   if (m.stages.empty() || m.stages.size() > kMaximumStageCount)
-    throw std::invalid_argument("a progressive matrix must contain between one and four stages");
-  if (prefix > m.stages.size()) throw std::invalid_argument("prefix exceeds the available stage count");
+    throw std::invalid_argument("stage count is not in 1..4");
+  if (prefix > m.stages.size()) throw std::invalid_argument("prefix is deeper than the matrix's stages");
   HostGeometry h{};
   h.rows = g.original_rows;
   h.cols = g.original_columns;
-  const std::size_t elements = Mul<std::overflow_error>(g.padded_rows, g.padded_columns, "padded matrix");
-  Mul<std::overflow_error>(g.original_rows, g.original_columns, "original matrix");
+  const std::size_t elements = Mul<std::overflow_error>(g.padded_rows, g.padded_columns, "padded element count");
+  Mul<std::overflow_error>(g.original_rows, g.original_columns, "element count");
   h.code_bytes = elements / 4 + (elements % 4 != 0 ? 1U : 0U);
   h.shape = ScaleShape{g.padded_rows / g.tile_rows, g.padded_columns / g.tile_columns, g.tile_rows,
                        g.tile_columns / g.group_size};
-  h.scale_count = Mul<std::overflow_error>(h.shape[0], h.shape[1], "scale grid");
-  h.scale_count = Mul<std::overflow_error>(h.scale_count, h.shape[2], "scale rows");
-  h.scale_count = Mul<std::overflow_error>(h.scale_count, h.shape[3], "scale groups");
+  h.scale_count = Mul<std::overflow_error>(h.shape[0], h.shape[1], "scale count over tiles");
+  h.scale_count = Mul<std::overflow_error>(h.scale_count, h.shape[2], "scale count over tile rows");
+  h.scale_count = Mul<std::overflow_error>(h.scale_count, h.shape[3], "scale count over groups");
   for (std::size_t i = 0; i < m.stages.size(); ++i) {
     const DecodedStage& st = m.stages[i];
-    if (st.stage_index != i) throw std::invalid_argument("stages must form a zero-based contiguous prefix");
-    if (st.packed_codes.size() != h.code_bytes) throw std::invalid_argument("stage packed-code byte count disagrees with geometry");
+    if (st.stage_index != i) throw std::invalid_argument("stage indices are not 0, 1, 2, ... in order");
+    if (st.packed_codes.size() != h.code_bytes) throw std::invalid_argument("a stage's code bytes differ from the geometry's");
     if (st.scale_shape != h.shape || st.scales.size() != h.scale_count)
-      throw std::invalid_argument("stage scale shape disagrees with geometry");
+      throw std::invalid_argument("a stage's scale shape differs from the geometry's");
     for (float s : st.scales) {
-      if (!std::isfinite(s) || s < 0.0F) throw std::invalid_argument("stage scales must be finite and non-negative");
+      if (!std::isfinite(s) || s < 0.0F) throw std::invalid_argument("a stage scale is negative, infinite or NaN");
       if (require_fp16) {
         const float back = __half2float(__float2half_rn(s));
-        if (!std::isfinite(back)) throw std::invalid_argument("stage scale is outside the finite FP16 range");
-        if (back != s) throw std::invalid_argument("stage scale is not exactly representable as FP16");
+        if (!std::isfinite(back)) throw std::invalid_argument("a stage scale overflows FP16");
+        if (back != s) throw std::invalid_argument("a stage scale is not an FP16 value");
       }
     }
   }
@@ -317,7 +317,7 @@ HostGeometry ValidateGemvMatrix(const ProgressiveMatrix& m, std::size_t prefix, 
 
 void ValidateFinite(const std::vector<float>& v, const char* what) {
   for (float x : v)
-    if (!std::isfinite(x)) throw std::invalid_argument(std::string(what) + " must contain only finite values");
+    if (!std::isfinite(x)) throw std::invalid_argument(std::string(what) + " holds an infinite or NaN value");
 }
 
 // ---- oracle ------------------------------------------------------------------------------
@@ -372,7 +372,7 @@ __global__ void AddBias(float* y, const float* bias, std::uint64_t batch, std::u
 
 int CublasDim(std::size_t v, const char* what) {
   if (v > static_cast<std::size_t>(std::numeric_limits<int>::max()))
-    throw std::invalid_argument(std::string(what) + " exceeds the cuBLAS int range");
+    throw std::invalid_argument(std::string(what) + " is too large for cuBLAS int sizes");
   return static_cast<int>(v);
 }
 
@@ -383,21 +383,21 @@ int CublasDim(std::size_t v, const char* what) {
 DecodedStage DecodeStagePayload(const std::vector<std::uint8_t>& payload, std::uint16_t expected_stage,
                                 const ScaleShape& scale_shape) {
   static constexpr std::uint8_t kMagic[8] = {'H', 'Q', 'S', 'T', 'A', 'G', 'E', 0};
-  if (payload.size() < 20) throw StageCodecError("stage payload is truncated");
-  if (std::memcmp(payload.data(), kMagic, 8) != 0) throw StageCodecError("stage payload magic is invalid");
+  if (payload.size() < 20) throw StageCodecError("payload is shorter than its header");
+  if (std::memcmp(payload.data(), kMagic, 8) != 0) throw StageCodecError("payload does not begin with the stage magic");
   const std::uint16_t version = Le16(payload.data() + 8);
   const std::uint16_t stage = Le16(payload.data() + 10);
   const std::size_t code_bytes = Le32(payload.data() + 12);
   const std::size_t scale_count = Le32(payload.data() + 16);
-  if (version != kStageCodecVersion) throw StageCodecError("unsupported stage codec version " + std::to_string(version));
-  if (stage != expected_stage) throw StageCodecError("payload stage does not match expected stage");
+  if (version != kStageCodecVersion) throw StageCodecError("stage codec version not supported: " + std::to_string(version));
+  if (stage != expected_stage) throw StageCodecError("payload holds a different stage from the one asked for");
   const std::size_t expected_scales = ScaleCountOf(scale_shape);
-  if (scale_count != expected_scales) throw StageCodecError("scale count does not match metadata");
+  if (scale_count != expected_scales) throw StageCodecError("payload scale count differs from the geometry's");
   const std::size_t scale_bytes = Mul<StageCodecError>(expected_scales, 2, "scale bytes");
   if (code_bytes > std::numeric_limits<std::size_t>::max() - 20 ||
       scale_bytes > std::numeric_limits<std::size_t>::max() - 20 - code_bytes)
-    throw StageCodecError("payload length overflows size_t");
-  if (payload.size() != 20 + code_bytes + scale_bytes) throw StageCodecError("stage payload length does not match its header");
+    throw StageCodecError("payload size does not fit in size_t");
+  if (payload.size() != 20 + code_bytes + scale_bytes) throw StageCodecError("payload size differs from the size its header implies");
   DecodedStage d;
   d.stage_index = stage;
   d.scale_shape = scale_shape;
@@ -406,8 +406,8 @@ DecodedStage DecodeStagePayload(const std::vector<std::uint8_t>& payload, std::u
   const std::uint8_t* sp = payload.data() + 20 + code_bytes;
   for (std::size_t i = 0; i < expected_scales; ++i) {
     const float s = HalfBitsToFloat(Le16(sp + 2 * i));
-    if (!std::isfinite(s)) throw StageCodecError("stage scales must be finite");
-    if (s < 0.0F) throw StageCodecError("stage scales cannot be negative");
+    if (!std::isfinite(s)) throw StageCodecError("a payload scale is infinite or NaN");
+    if (s < 0.0F) throw StageCodecError("a payload scale is negative");
     d.scales.push_back(s);
   }
   return d;
@@ -415,7 +415,7 @@ DecodedStage DecodeStagePayload(const std::vector<std::uint8_t>& payload, std::u
 
 std::vector<float> DequantizeStage(const ProgressiveMatrix& matrix, std::size_t stage_index) {
   ValidateCodecMatrix(matrix);
-  if (stage_index >= matrix.stages.size()) throw StageCodecError("stage_index is outside the available prefix");
+  if (stage_index >= matrix.stages.size()) throw StageCodecError("stage index is past the matrix's stages");
   const std::size_t n = Mul<StageCodecError>(matrix.geometry.original_rows, matrix.geometry.original_columns, "output element count");
   if (!DeviceUsable()) return HostDequantize(matrix, stage_index, stage_index + 1, false);
   DeviceArray<float> out(n);
@@ -430,7 +430,7 @@ std::vector<float> DequantizeStage(const ProgressiveMatrix& matrix, std::size_t 
 
 std::vector<float> DequantizePrefix(const ProgressiveMatrix& matrix, std::size_t prefix) {
   ValidateCodecMatrix(matrix);
-  if (prefix > matrix.stages.size()) throw StageCodecError("prefix exceeds the available stage count");
+  if (prefix > matrix.stages.size()) throw StageCodecError("prefix is deeper than the matrix's stages");
   const std::size_t n = Mul<StageCodecError>(matrix.geometry.original_rows, matrix.geometry.original_columns, "output element count");
   if (!DeviceUsable()) return HostDequantize(matrix, 0, prefix, true);
   DeviceArray<float> out(n);
@@ -447,15 +447,15 @@ std::vector<float> ProgressiveLinearReference(const std::vector<float>& inputs, 
                                               const ProgressiveMatrix& matrix, std::size_t prefix,
                                               const std::vector<float>& bias) {
   ValidateCodecMatrix(matrix);
-  if (prefix > matrix.stages.size()) throw StageCodecError("prefix exceeds the available stage count");
+  if (prefix > matrix.stages.size()) throw StageCodecError("prefix is deeper than the matrix's stages");
   const MatrixGeometry& g = matrix.geometry;
   if (inputs.size() != Mul<StageCodecError>(batch_size, g.original_columns, "input element count"))
-    throw StageCodecError("input element count does not match batch geometry");
-  if (!bias.empty() && bias.size() != g.original_rows) throw StageCodecError("bias length must match output features");
+    throw StageCodecError("input size is not batch x columns");
+  if (!bias.empty() && bias.size() != g.original_rows) throw StageCodecError("bias size is not the row count");
   for (float v : inputs)
-    if (!std::isfinite(v)) throw StageCodecError("inputs and bias must be finite");
+    if (!std::isfinite(v)) throw StageCodecError("an input or bias value is infinite or NaN");
   for (float v : bias)
-    if (!std::isfinite(v)) throw StageCodecError("inputs and bias must be finite");
+    if (!std::isfinite(v)) throw StageCodecError("an input or bias value is infinite or NaN");
   const std::size_t n = Mul<StageCodecError>(batch_size, g.original_rows, "linear output element count");
   if (n == 0) return {};
   if (!DeviceUsable()) return HostLinearOrdered(matrix, prefix, inputs, batch_size, bias);
@@ -473,7 +473,7 @@ std::vector<float> ProgressiveLinearReference(const std::vector<float>& inputs, 
 }
 
 std::uint32_t Crc32c(const std::uint8_t* data, std::size_t size, std::uint32_t crc) {
-  if (data == nullptr && size != 0) throw std::invalid_argument("CRC32C data cannot be null when size is non-zero");
+  if (data == nullptr && size != 0) throw std::invalid_argument("CRC32C given a null pointer with a non-zero size");
   static const auto table = [] {
     std::array<std::uint32_t, 256> t{};
     for (std::uint32_t i = 0; i < 256; ++i) {
@@ -506,8 +506,8 @@ cudaError_t LaunchProgressiveGemv(const ProgressiveGemvIoDeviceView& io, const P
 std::vector<float> ProgressiveGemvCuda(const std::vector<float>& input, const ProgressiveMatrix& matrix,
                                        std::size_t prefix, const std::vector<float>& bias) {
   const HostGeometry h = ValidateGemvMatrix(matrix, prefix, true);
-  if (input.size() != h.cols) throw std::invalid_argument("batch-one input element count disagrees with matrix geometry");
-  if (!bias.empty() && bias.size() != h.rows) throw std::invalid_argument("bias element count disagrees with output features");
+  if (input.size() != h.cols) throw std::invalid_argument("input size is not the column count");
+  if (!bias.empty() && bias.size() != h.rows) throw std::invalid_argument("bias size is not the row count");
   ValidateFinite(input, "input");
   ValidateFinite(bias, "bias");
   DeviceArray<float> x(input.size()), y(h.rows), b(bias.size());
@@ -563,8 +563,8 @@ std::vector<float> ProgressiveLinearCudaOracle(const std::vector<float>& inputs,
                                                const std::vector<float>& bias) {
   const HostGeometry h = ValidateGemvMatrix(matrix, prefix, false);
   if (inputs.size() != Mul<std::overflow_error>(batch_size, h.cols, "input"))
-    throw std::invalid_argument("input element count disagrees with batch and matrix geometry");
-  if (!bias.empty() && bias.size() != h.rows) throw std::invalid_argument("bias element count disagrees with output features");
+    throw std::invalid_argument("input size is not batch x columns");
+  if (!bias.empty() && bias.size() != h.rows) throw std::invalid_argument("bias size is not the row count");
   ValidateFinite(inputs, "inputs");
   ValidateFinite(bias, "bias");
   if (batch_size == 0) return {};
